@@ -1,0 +1,569 @@
+// fxr_capi.cu — extern "C" entry points declared in include/fxr.h: argument validation, workspace
+// carve-up, TMA tensor-map encoding and kernel launches. All kernels of the library are compiled in
+// this one translation unit so they share one device error word.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "fxr.h"
+#include "fxr_attention.cuh"
+#include "fxr_device.cuh"
+#include "fxr_mem_kernels.cuh"
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int32_t fail(int32_t status, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return status;
+}
+
+int32_t cuda_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return FXR_OK;
+    return fail(FXR_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define FXR_CHECK_LAUNCH(what)                                                                     \
+    do {                                                                                           \
+        cudaError_t e_ = cudaGetLastError();                                                       \
+        if (e_ != cudaSuccess) return cuda_status(e_, what);                                       \
+    } while (0)
+
+constexpr int kMaxDevices = 64;
+
+int sm_count() {
+    static int counts[kMaxDevices] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+    if (counts[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            n = 148;
+        counts[dev] = n;
+    }
+    return counts[dev];
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+size_t dtype_bytes(int32_t dt) {
+    switch (dt) {
+        case FXR_F32: return 4;
+        case FXR_F16: return 2;
+        case FXR_BF16: return 2;
+        default: return 0;
+    }
+}
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// ---- tensor maps ----------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D map over a row-major [rows, cols] 16-bit matrix with row stride ld (elements); box 64 x 128
+// (one 128-byte swizzle span wide), 128-byte swizzle, zero fill out of bounds.
+int32_t make_tmap(CUtensorMap* map, const void* ptr, int32_t dtype, int64_t cols, int64_t rows,
+                  int64_t ld) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(FXR_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType t =
+        dtype == FXR_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUresult r = fn(map, t, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(FXR_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return FXR_OK;
+}
+
+// ---- descriptor checks ------------------------------------------------------------------------
+int32_t check_desc(const fxr_frame_desc* d, bool need_tc) {
+    if (!d) return fail(FXR_ERR_INVALID, "null descriptor");
+    if (d->n_tokens < 0 || d->n_heads <= 0 || d->head_dim <= 0)
+        return fail(FXR_ERR_INVALID, "bad geometry: n_tokens=%d n_heads=%d head_dim=%d",
+                    d->n_tokens, d->n_heads, d->head_dim);
+    if (d->head_dim != fxr::kHeadDim)
+        return fail(FXR_ERR_UNSUPPORTED, "head_dim %d unsupported (this path is built for 128)",
+                    d->head_dim);
+    if (d->dtype != FXR_BF16 && d->dtype != FXR_F16)
+        return fail(FXR_ERR_UNSUPPORTED, "dtype %d unsupported on the tensor-core path", d->dtype);
+    if (d->rope_n_axes < 0 || d->rope_n_axes > 4)
+        return fail(FXR_ERR_INVALID, "rope_n_axes %d outside [0,4]", d->rope_n_axes);
+    int sum = 0;
+    for (int a = 0; a < d->rope_n_axes; ++a) {
+        if (d->rope_axes_dim[a] <= 0 || (d->rope_axes_dim[a] & 1))
+            return fail(FXR_ERR_INVALID, "rope_axes_dim[%d]=%d must be positive and even", a,
+                        d->rope_axes_dim[a]);
+        sum += d->rope_axes_dim[a];
+    }
+    if (sum > d->head_dim) return fail(FXR_ERR_INVALID, "rope axes sum %d > head_dim", sum);
+    if (d->rope_n_axes > 0 && !(d->rope_theta > 0.f))
+        return fail(FXR_ERR_INVALID, "rope_theta must be > 0");
+    const int64_t C = (int64_t)d->n_heads * d->head_dim;
+    if (d->ld_qkv < C || d->ld_cache < C || d->ld_out < C)
+        return fail(FXR_ERR_INVALID, "row strides must be >= n_heads*head_dim (%lld)", (long long)C);
+    if ((d->ld_qkv % 8) || (d->ld_cache % 8) || (d->ld_out % 8))
+        return fail(FXR_ERR_INVALID, "row strides must be multiples of 8 elements (16 bytes)");
+    (void)need_tc;
+    return FXR_OK;
+}
+
+void fill_rope(const fxr_frame_desc* d, fxr::RopeTable* t) {
+    for (int j = 0; j < fxr::kPairs; ++j) {
+        t->omega[j] = 0.f;
+        t->axis[j] = -1;
+    }
+    int j = 0;
+    for (int a = 0; a < d->rope_n_axes; ++a) {
+        const int half = d->rope_axes_dim[a] / 2;
+        for (int jj = 0; jj < half && j < fxr::kPairs; ++jj, ++j) {
+            t->omega[j] = (float)std::pow((double)d->rope_theta,
+                                          -2.0 * (double)jj / (double)d->rope_axes_dim[a]);
+            t->axis[j] = (int8_t)a;
+        }
+    }
+}
+
+struct Views {
+    int32_t* count;
+    int32_t* idx;
+    void* qc;
+    int64_t ld_qc;
+    void* save;
+    size_t total;
+};
+
+Views carve(const fxr_frame_desc* d, void* ws) {
+    Views v{};
+    const size_t N = (size_t)(d->n_tokens > 0 ? d->n_tokens : 1);
+    const size_t C = (size_t)d->n_heads * d->head_dim;
+    const size_t eb = dtype_bytes(d->dtype);
+    size_t off = 0;
+    char* b = static_cast<char*>(ws);
+    v.count = reinterpret_cast<int32_t*>(b ? b + off : nullptr);
+    off = align_up(off + sizeof(int32_t), 256);
+    v.idx = reinterpret_cast<int32_t*>(b ? b + off : nullptr);
+    off = align_up(off + N * sizeof(int32_t), 256);
+    v.qc = b ? b + off : nullptr;
+    v.ld_qc = (int64_t)C;
+    off = align_up(off + N * C * eb, 256);
+    v.save = b ? b + off : nullptr;
+    off = align_up(off + N * 2 * C * eb, 256);
+    v.total = off;
+    return v;
+}
+
+int grid_rows(int64_t rows, int rows_per_cta) {
+    const int64_t need = (rows + rows_per_cta - 1) / rows_per_cta;
+    const int64_t cap = (int64_t)sm_count() * 8;
+    return (int)std::max<int64_t>(1, std::min(need, cap));
+}
+
+template <typename T>
+int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
+                         const int32_t* count, const void* ck, const void* cv, const int32_t* idx,
+                         void* out, cudaStream_t stream, float* dbg = nullptr) {
+    static bool configured[kMaxDevices] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < kMaxDevices && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(fxr::attn::attention_kernel<T>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)fxr::attn::kSmemBytes);
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
+        configured[dev] = true;
+    }
+    const int64_t C = (int64_t)d->n_heads * d->head_dim;
+    const int64_t N = d->n_tokens;
+    CUtensorMap tq, tk, tv;
+    int32_t st;
+    if ((st = make_tmap(&tq, qc, d->dtype, C, N, ld_qc)) != FXR_OK) return st;
+    if ((st = make_tmap(&tk, ck, d->dtype, C, N, d->ld_cache)) != FXR_OK) return st;
+    if ((st = make_tmap(&tv, cv, d->dtype, C, N, d->ld_cache)) != FXR_OK) return st;
+    fxr::attn::Params p{};
+    p.count = count;
+    p.idx = idx;
+    p.out = out;
+    p.ld_out = d->ld_out;
+    p.n_tokens = d->n_tokens;
+    p.n_heads = d->n_heads;
+    p.dbg = dbg;
+    const float scale = d->softmax_scale > 0.f ? d->softmax_scale : 1.0f / std::sqrt((float)d->head_dim);
+    p.scale_log2 = scale * 1.4426950408889634f;
+    const int64_t max_tiles = (N + fxr::attn::kBM - 1) / fxr::attn::kBM * d->n_heads;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_tiles, sm_count()));
+    fxr::attn::attention_kernel<T><<<grid, fxr::attn::kThreads, fxr::attn::kSmemBytes, stream>>>(
+        tq, tk, tv, p);
+    FXR_CHECK_LAUNCH("attention_kernel launch");
+    return FXR_OK;
+}
+
+template <typename T>
+int32_t launch_gather(const fxr_frame_desc* d, const void* q, const void* k, const void* v,
+                      const int32_t* mask, const int32_t* idx, const int32_t* count,
+                      const int32_t* pos, const float* nq, const float* nk, void* qc, int64_t ld_qc,
+                      void* ck, void* cv, void* save, cudaStream_t stream) {
+    fxr::GatherArgs a{};
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.mask = mask;
+    a.idx = idx;
+    a.count = count;
+    a.pos = pos;
+    a.norm_q = nq;
+    a.norm_k = nk;
+    a.qc = qc;
+    a.cache_k = ck;
+    a.cache_v = cv;
+    a.save = save;
+    a.ld_qkv = d->ld_qkv;
+    a.ld_qc = ld_qc;
+    a.ld_cache = d->ld_cache;
+    a.n_tokens = d->n_tokens;
+    a.n_heads = d->n_heads;
+    a.n_axes = d->rope_n_axes;
+    a.eps = d->eps;
+    fill_rope(d, &a.rope);
+    const int grid = grid_rows(d->n_tokens, fxr::kGatherThreads / 32);
+    fxr::gather_norm_rope_kernel<T><<<grid, fxr::kGatherThreads, 0, stream>>>(a);
+    FXR_CHECK_LAUNCH("gather_norm_rope_kernel launch");
+    return FXR_OK;
+}
+
+}  // namespace
+
+// =============================================================================================
+extern "C" {
+
+int32_t fxr_abi_version(void) { return FXR_ABI_VERSION; }
+
+const char* fxr_build_info(void) {
+    return "fxr sm_100a: tcgen05/TMEM flash attention + fused gather/RMSNorm/RoPE; nvcc "
+#ifdef __CUDACC_VER_MAJOR__
+           "12.x"
+#endif
+        ;
+}
+
+const char* fxr_last_error_string(void) { return t_last_error.c_str(); }
+
+int32_t fxr_check_device_error(void* stream, uint32_t* word_out) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_status(e, "cudaStreamSynchronize");
+    uint32_t w = 0;
+    e = cudaMemcpyFromSymbol(&w, fxr::g_error_word, sizeof(w));
+    if (e != cudaSuccess) return cuda_status(e, "read error word");
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(fxr::g_error_word, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_status(e, "clear error word");
+    if (word_out) *word_out = w;
+    if (w & fxr::kErrTimeout) return fail(FXR_ERR_TIMEOUT, "device wait timed out (word 0x%x)", w);
+    if (w) return fail(FXR_ERR_INVALID, "device bounds check failed (word 0x%x)", w);
+    return FXR_OK;
+}
+
+size_t fxr_workspace_size(const fxr_frame_desc* desc) {
+    if (!desc || dtype_bytes(desc->dtype) == 0 || desc->n_heads <= 0 || desc->head_dim <= 0) return 0;
+    return carve(desc, nullptr).total;
+}
+
+int32_t fxr_workspace_views(const fxr_frame_desc* desc, void* workspace, int32_t** idx,
+                            int32_t** count, void** qc, int64_t* ld_qc, void** save) {
+    if (!desc || !workspace) return fail(FXR_ERR_INVALID, "null descriptor or workspace");
+    Views v = carve(desc, workspace);
+    if (idx) *idx = v.idx;
+    if (count) *count = v.count;
+    if (qc) *qc = v.qc;
+    if (ld_qc) *ld_qc = v.ld_qc;
+    if (save) *save = v.save;
+    return FXR_OK;
+}
+
+int32_t fxr_mask_compact(int32_t* mask, const uint8_t* valid, int32_t n_tokens, int32_t* idx,
+                         int32_t* count, void* stream) {
+    if (n_tokens < 0) return fail(FXR_ERR_INVALID, "n_tokens < 0");
+    if (!count || (n_tokens > 0 && (!mask || !idx))) return fail(FXR_ERR_INVALID, "null pointer");
+    fxr::compact_kernel<<<1, fxr::kCompactThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        mask, valid, n_tokens, idx, count);
+    FXR_CHECK_LAUNCH("compact_kernel launch");
+    return FXR_OK;
+}
+
+int32_t fxr_preprocess_mask(int32_t* mask, const uint8_t* valid, int32_t n_tokens, void* stream) {
+    if (n_tokens < 0) return fail(FXR_ERR_INVALID, "n_tokens < 0");
+    if (n_tokens == 0) return FXR_OK;
+    if (!mask || !valid) return fail(FXR_ERR_INVALID, "null pointer");
+    fxr::preprocess_mask_kernel<<<(n_tokens + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        mask, valid, n_tokens);
+    FXR_CHECK_LAUNCH("preprocess_mask_kernel launch");
+    return FXR_OK;
+}
+
+int32_t fxr_gather_norm_rope(const fxr_frame_desc* desc, const void* q, const void* k,
+                             const void* v, const int32_t* mask, const int32_t* idx,
+                             const int32_t* count, const int32_t* pos, const float* norm_q,
+                             const float* norm_k, void* qc, int64_t ld_qc, void* cache_k,
+                             void* cache_v, void* save, void* stream) {
+    int32_t st = check_desc(desc, false);
+    if (st != FXR_OK) return st;
+    if (desc->n_tokens == 0) return FXR_OK;
+    if (!q || !k || !v || !mask || !idx || !count || !norm_q || !norm_k || !qc || !cache_k ||
+        !cache_v || (desc->rope_n_axes > 0 && !pos))
+        return fail(FXR_ERR_INVALID, "null pointer argument");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(qc) || !aligned16(cache_k) ||
+        !aligned16(cache_v) || (save && !aligned16(save)) || (ld_qc % 8))
+        return fail(FXR_ERR_INVALID, "Q/K/V/qc/cache/save must be 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (desc->dtype == FXR_BF16)
+        return launch_gather<__nv_bfloat16>(desc, q, k, v, mask, idx, count, pos, norm_q, norm_k, qc,
+                                            ld_qc, cache_k, cache_v, save, s);
+    return launch_gather<__half>(desc, q, k, v, mask, idx, count, pos, norm_q, norm_k, qc, ld_qc,
+                                 cache_k, cache_v, save, s);
+}
+
+int32_t fxr_attention_active(const fxr_frame_desc* desc, const void* qc, int64_t ld_qc,
+                             const int32_t* count, const void* cache_k, const void* cache_v,
+                             const int32_t* idx, void* out, void* stream) {
+    int32_t st = check_desc(desc, true);
+    if (st != FXR_OK) return st;
+    if (desc->n_tokens == 0) return FXR_OK;
+    if (!qc || !count || !cache_k || !cache_v || !idx || !out)
+        return fail(FXR_ERR_INVALID, "null pointer argument");
+    if (!aligned16(qc) || !aligned16(cache_k) || !aligned16(cache_v) || !aligned16(out) ||
+        (ld_qc % 8) || ld_qc < (int64_t)desc->n_heads * desc->head_dim)
+        return fail(FXR_ERR_INVALID, "qc/cache/out must be 16-byte aligned with ld_qc >= C, %% 8");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (desc->dtype == FXR_BF16)
+        return launch_attention<__nv_bfloat16>(desc, qc, ld_qc, count, cache_k, cache_v, idx, out, s);
+    return launch_attention<__half>(desc, qc, ld_qc, count, cache_k, cache_v, idx, out, s);
+}
+
+// Diagnostic variant of fxr_attention_active (not part of the public header): also writes CTA 0's
+// first tile internals into dbg (34816 floats): raw scores of key tile 0, unnormalised O, row sums,
+// row maxima.
+int32_t fxr_debug_attention(const fxr_frame_desc* desc, const void* qc, int64_t ld_qc,
+                            const int32_t* count, const void* cache_k, const void* cache_v,
+                            const int32_t* idx, void* out, float* dbg, void* stream) {
+    int32_t st = check_desc(desc, true);
+    if (st != FXR_OK) return st;
+    if (!qc || !count || !cache_k || !cache_v || !idx || !out || !dbg)
+        return fail(FXR_ERR_INVALID, "null pointer argument");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (desc->dtype == FXR_BF16)
+        return launch_attention<__nv_bfloat16>(desc, qc, ld_qc, count, cache_k, cache_v, idx, out, s, dbg);
+    return launch_attention<__half>(desc, qc, ld_qc, count, cache_k, cache_v, idx, out, s, dbg);
+}
+
+int32_t fxr_restore_rows(const fxr_frame_desc* desc, const int32_t* mask, const int32_t* idx,
+                         const int32_t* count, const void* save, void* cache_k, void* cache_v,
+                         void* stream) {
+    int32_t st = check_desc(desc, false);
+    if (st != FXR_OK) return st;
+    if (desc->n_tokens == 0) return FXR_OK;
+    if (!mask || !idx || !count || !save || !cache_k || !cache_v)
+        return fail(FXR_ERR_INVALID, "null pointer argument");
+    if (!aligned16(save) || !aligned16(cache_k) || !aligned16(cache_v))
+        return fail(FXR_ERR_INVALID, "save/cache must be 16-byte aligned");
+    const int64_t row_bytes = (int64_t)desc->n_heads * desc->head_dim * (int64_t)dtype_bytes(desc->dtype);
+    fxr::restore_rows_kernel<<<grid_rows(desc->n_tokens, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        mask, idx, count, static_cast<const uint4*>(save), static_cast<char*>(cache_k),
+        static_cast<char*>(cache_v), desc->ld_cache * (int64_t)dtype_bytes(desc->dtype),
+        (int32_t)(row_bytes / 16), desc->n_tokens);
+    FXR_CHECK_LAUNCH("restore_rows_kernel launch");
+    return FXR_OK;
+}
+
+static int32_t rows_copy(bool scatter, const void* src, int64_t ld_src, const int32_t* idx,
+                         const int32_t* count, int32_t host_count, void* dst, int64_t ld_dst,
+                         int64_t row_bytes, void* stream) {
+    if (!count && host_count < 0) return fail(FXR_ERR_INVALID, "need a device count or host_count >= 0");
+    if (!count && host_count == 0) return FXR_OK;
+    if (!src || !dst || !idx || row_bytes <= 0) return fail(FXR_ERR_INVALID, "null pointer or row_bytes <= 0");
+    const int64_t rows_hint = count ? (int64_t)1 << 16 : host_count;
+    const int grid = grid_rows(rows_hint, 8);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const char* sp = static_cast<const char*>(src);
+    char* dp = static_cast<char*>(dst);
+    const bool v16 = aligned16(src) && aligned16(dst) && row_bytes % 16 == 0 && ld_src % 16 == 0 &&
+                     ld_dst % 16 == 0;
+    const bool v4 = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 3) == 0 &&
+                    row_bytes % 4 == 0 && ld_src % 4 == 0 && ld_dst % 4 == 0;
+    if (v16) {
+        if (scatter)
+            fxr::rows_copy_kernel<uint4, true><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes / 16);
+        else
+            fxr::rows_copy_kernel<uint4, false><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes / 16);
+    } else if (v4) {
+        if (scatter)
+            fxr::rows_copy_kernel<uint32_t, true><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes / 4);
+        else
+            fxr::rows_copy_kernel<uint32_t, false><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes / 4);
+    } else {
+        if (scatter)
+            fxr::rows_copy_kernel<uint8_t, true><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes);
+        else
+            fxr::rows_copy_kernel<uint8_t, false><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes);
+    }
+    FXR_CHECK_LAUNCH("rows_copy_kernel launch");
+    return FXR_OK;
+}
+
+int32_t fxr_gather_rows(const void* src, int64_t ld_src_bytes, const int32_t* idx,
+                        const int32_t* count, int32_t host_count, void* dst, int64_t ld_dst_bytes,
+                        int64_t row_bytes, void* stream) {
+    return rows_copy(false, src, ld_src_bytes, idx, count, host_count, dst, ld_dst_bytes, row_bytes, stream);
+}
+
+int32_t fxr_scatter_rows(const void* src, int64_t ld_src_bytes, const int32_t* idx,
+                         const int32_t* count, int32_t host_count, void* dst, int64_t ld_dst_bytes,
+                         int64_t row_bytes, void* stream) {
+    return rows_copy(true, src, ld_src_bytes, idx, count, host_count, dst, ld_dst_bytes, row_bytes, stream);
+}
+
+int32_t fxr_kv_sync(void* keys, void* values, void* cached_keys, void* cached_values,
+                    const int32_t* mask, int32_t n_tokens, int64_t row_elems, int32_t dtype,
+                    void* stream) {
+    const size_t eb = dtype_bytes(dtype);
+    if (eb == 0) return fail(FXR_ERR_INVALID, "bad dtype %d", dtype);
+    if (n_tokens < 0 || row_elems < 0) return fail(FXR_ERR_INVALID, "negative size");
+    if (n_tokens == 0 || row_elems == 0) return FXR_OK;
+    if (!keys || !values || !cached_keys || !cached_values || !mask)
+        return fail(FXR_ERR_INVALID, "null pointer argument");
+    const int64_t row_bytes = row_elems * (int64_t)eb;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t cap = (int64_t)sm_count() * 16;
+    const bool v16 = aligned16(keys) && aligned16(values) && aligned16(cached_keys) &&
+                     aligned16(cached_values) && row_bytes % 16 == 0;
+    if (v16) {
+        const int64_t words = row_bytes / 16, total = words * n_tokens;
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, cap));
+        fxr::kv_sync_kernel<uint4><<<grid, 256, 0, s>>>(static_cast<uint4*>(keys), static_cast<uint4*>(values),
+                                                        static_cast<uint4*>(cached_keys), static_cast<uint4*>(cached_values),
+                                                        mask, n_tokens, words);
+    } else {
+        const int64_t words = row_bytes / (int64_t)eb, total = words * n_tokens;
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, cap));
+        if (eb == 4)
+            fxr::kv_sync_kernel<uint32_t><<<grid, 256, 0, s>>>(static_cast<uint32_t*>(keys), static_cast<uint32_t*>(values),
+                                                               static_cast<uint32_t*>(cached_keys), static_cast<uint32_t*>(cached_values),
+                                                               mask, n_tokens, words);
+        else
+            fxr::kv_sync_kernel<uint16_t><<<grid, 256, 0, s>>>(static_cast<uint16_t*>(keys), static_cast<uint16_t*>(values),
+                                                               static_cast<uint16_t*>(cached_keys), static_cast<uint16_t*>(cached_values),
+                                                               mask, n_tokens, words);
+    }
+    FXR_CHECK_LAUNCH("kv_sync_kernel launch");
+    return FXR_OK;
+}
+
+int32_t fxr_output_cache_sync(void* pred, void* cache, const int32_t* mask, uint8_t* valid,
+                              int32_t n_text, int32_t n_image, int32_t channels, int32_t dtype,
+                              void* stream) {
+    const size_t eb = dtype_bytes(dtype);
+    if (eb == 0) return fail(FXR_ERR_INVALID, "bad dtype %d", dtype);
+    if (n_text < 0 || n_image < 0 || channels < 0) return fail(FXR_ERR_INVALID, "negative size");
+    if (n_image == 0 || channels == 0) return FXR_OK;
+    if (!pred || !cache || !mask || !valid) return fail(FXR_ERR_INVALID, "null pointer argument");
+    const int64_t row_bytes = (int64_t)channels * (int64_t)eb;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t cap = (int64_t)sm_count() * 16;
+    if (aligned16(pred) && aligned16(cache) && row_bytes % 16 == 0) {
+        const int64_t words = row_bytes / 16, total = words * n_image;
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, cap));
+        fxr::out_cache_sync_kernel<uint4><<<grid, 256, 0, s>>>(static_cast<uint4*>(pred), static_cast<uint4*>(cache),
+                                                               mask, valid, n_text, n_image, words);
+    } else {
+        const int64_t words = channels, total = words * n_image;
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, cap));
+        if (eb == 4)
+            fxr::out_cache_sync_kernel<uint32_t><<<grid, 256, 0, s>>>(static_cast<uint32_t*>(pred), static_cast<uint32_t*>(cache),
+                                                                      mask, valid, n_text, n_image, words);
+        else
+            fxr::out_cache_sync_kernel<uint16_t><<<grid, 256, 0, s>>>(static_cast<uint16_t*>(pred), static_cast<uint16_t*>(cache),
+                                                                      mask, valid, n_text, n_image, words);
+    }
+    FXR_CHECK_LAUNCH("out_cache_sync_kernel launch");
+    return FXR_OK;
+}
+
+int32_t fxr_rms_norm(const void* x, void* y, const float* w, float eps, int64_t rows, int32_t dim,
+                     int32_t dtype, void* stream) {
+    if (rows < 0 || dim < 0) return fail(FXR_ERR_INVALID, "negative size");
+    if (rows == 0 || dim == 0) return FXR_OK;
+    if (!x || !y || !w) return fail(FXR_ERR_INVALID, "null pointer argument");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int grid = grid_rows(rows, 8);
+    switch (dtype) {
+        case FXR_F32:
+            fxr::rms_norm_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), static_cast<float*>(y), w, eps, rows, dim);
+            break;
+        case FXR_F16:
+            fxr::rms_norm_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y), w, eps, rows, dim);
+            break;
+        case FXR_BF16:
+            fxr::rms_norm_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), w, eps, rows, dim);
+            break;
+        default:
+            return fail(FXR_ERR_INVALID, "bad dtype %d", dtype);
+    }
+    FXR_CHECK_LAUNCH("rms_norm_kernel launch");
+    return FXR_OK;
+}
+
+int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void* k, const void* v,
+                          int32_t* mask, const uint8_t* valid, const int32_t* pos,
+                          const float* norm_q, const float* norm_k, void* cache_k, void* cache_v,
+                          void* out, void* workspace, size_t workspace_bytes, void* stream) {
+    int32_t st = check_desc(desc, true);
+    if (st != FXR_OK) return st;
+    if (desc->n_tokens == 0) return FXR_OK;
+    if (!workspace) return fail(FXR_ERR_INVALID, "null workspace");
+    const Views w = carve(desc, workspace);
+    if (workspace_bytes < w.total)
+        return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, w.total);
+    if (!aligned16(workspace)) return fail(FXR_ERR_INVALID, "workspace must be 16-byte aligned");
+    if ((st = fxr_mask_compact(mask, valid, desc->n_tokens, w.idx, w.count, stream)) != FXR_OK) return st;
+    if ((st = fxr_gather_norm_rope(desc, q, k, v, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc,
+                                   w.ld_qc, cache_k, cache_v, w.save, stream)) != FXR_OK)
+        return st;
+    if ((st = fxr_attention_active(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, out,
+                                   stream)) != FXR_OK)
+        return st;
+    return fxr_restore_rows(desc, mask, w.idx, w.count, w.save, cache_k, cache_v, stream);
+}
+
+}  // extern "C"

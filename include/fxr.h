@@ -1,0 +1,180 @@
+/*
+ * fxr.h — C ABI of the B200 (sm_100a) sparse stream-editing attention path.
+ *
+ * One frame of a FLUX.2 double-stream attention slice under a spatial KV cache:
+ *   change mask -> ascending index list of executed tokens -> gather of their Q/K/V rows with
+ *   per-head QK-RMSNorm and multi-axis RoPE in the gather's epilogue -> attention of the executed
+ *   queries against every key (fresh K/V for executed tokens, cached K/V for skipped ones) ->
+ *   scatter of the outputs into the full-frame buffer and update of the K/V cache rows.
+ *
+ * Conventions (all entry points):
+ *   - plain C: pointers, sizes, an opaque stream handle (a cudaStream_t passed as void*);
+ *   - every pointer argument except the descriptor is DEVICE memory owned by the caller;
+ *     nothing allocates device memory;
+ *   - asynchronous on `stream`; nothing synchronises the host, so a sequence of calls can be
+ *     captured into a CUDA graph;
+ *   - the number of executed tokens M is produced on the device by fxr_mask_compact and read on
+ *     the device by the later steps (`count` argument), so no device->host copy is needed;
+ *   - return FXR_OK (0) or an error status; fxr_last_error_string() describes the last error of
+ *     the calling thread; no C++ exception crosses this boundary.
+ *
+ * Layouts: token-major rows, text tokens first ([0, T)) then image tokens ([T, N)).
+ *   Q, K, V, out, cache_k, cache_v: [N rows, row stride ld (elements)], head h of a row at
+ *   columns [h*D, (h+1)*D). For head sharding, pass base pointers offset by head_begin*D.
+ *   mask: int32 [N], 0 = skip, 1 = execute, 2 = execute + update cache
+ *   (fluxrt-cpp tools/export_onnx.py:126-129, src/inference/kernels/spatial_kv_cache.cu:12-87).
+ *   valid: uint8 [N] cache-row validity (spatial_kv_cache.h:45), NULL = every row valid.
+ *   pos: int32 [N, rope_n_axes] position ids.
+ */
+#ifndef FXR_H
+#define FXR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FXR_ABI_VERSION 1
+
+/* Status codes. The reference's plugin enqueue returns 0 / -1
+ * (src/inference/plugins/flux2_double_block_plugin.cpp:208,230); these refine the -1. */
+typedef enum fxr_status {
+    FXR_OK = 0,
+    FXR_ERR_INVALID = 1,      /* bad argument: null pointer, unsupported size, misaligned buffer */
+    FXR_ERR_CUDA = 2,         /* a CUDA runtime call or kernel launch failed */
+    FXR_ERR_TIMEOUT = 3,      /* a bounded device-side wait gave up (device error word set) */
+    FXR_ERR_UNSUPPORTED = 4,  /* valid request this build does not implement (e.g. head_dim != 128 on the tensor-core path) */
+    FXR_ERR_WORKSPACE = 5,    /* workspace smaller than fxr_workspace_size() */
+    FXR_ERR_NCCL = 6          /* NCCL call failed */
+} fxr_status;
+
+/* Storage element types (compute is fp32 throughout). */
+typedef enum fxr_dtype { FXR_F32 = 0, FXR_F16 = 1, FXR_BF16 = 2 } fxr_dtype;
+
+/* Frame geometry and RoPE / norm parameters. Plain old data; zero-initialise, then fill. */
+typedef struct fxr_frame_desc {
+    int32_t n_tokens;        /* N = T + I */
+    int32_t n_text;          /* T (informational: text rows are [0, T)) */
+    int32_t n_heads;         /* heads processed by this call (24 for FLUX.2-Klein) */
+    int32_t head_dim;        /* D; the tensor-core attention supports 128 */
+    int32_t dtype;           /* fxr_dtype of Q/K/V/out/cache: FXR_BF16 or FXR_F16 */
+    int32_t rope_n_axes;     /* 1..4 */
+    int32_t rope_axes_dim[4];/* even, sum == head_dim (e.g. 16/56/56 or 32/32/32/32) */
+    float rope_theta;        /* 10000 (FLUX.1 layout) or 2000 (Klein config.json:22) */
+    float eps;               /* RMSNorm epsilon, 1e-6 (flux2_double_block_plugin.cpp:413) */
+    float softmax_scale;     /* <= 0 selects 1/sqrt(head_dim) (attention_kernels.cu:101) */
+    int32_t reserved0;
+    int64_t ld_qkv;          /* row stride (elements) of Q, K, V */
+    int64_t ld_cache;        /* row stride of cache_k, cache_v */
+    int64_t ld_out;          /* row stride of out */
+} fxr_frame_desc;
+
+/* Library ABI version (FXR_ABI_VERSION) and build information. */
+int32_t fxr_abi_version(void);
+const char* fxr_build_info(void);
+
+/* Last error message of the calling thread ("" if none). */
+const char* fxr_last_error_string(void);
+
+/* Reads and clears the device error word of the current device (set by bounded waits that gave
+ * up and by checked-build bounds checks). Synchronises `stream`. Returns FXR_OK or FXR_ERR_TIMEOUT. */
+int32_t fxr_check_device_error(void* stream, uint32_t* word_out);
+
+/* ---- workspace ------------------------------------------------------------------------------ */
+/* Bytes of caller-provided workspace fxr_frame_forward needs (idx, count, compact Q, saved rows
+ * of mask==1 tokens). Replaces the reference's workspace carve-up
+ * (flux2_double_block_plugin.cpp:167-185, 347-366). */
+size_t fxr_workspace_size(const fxr_frame_desc* desc);
+
+/* ---- individual steps ----------------------------------------------------------------------- */
+
+/* Mask preprocess + compaction. Replaces preprocess_mask_kernel (spatial_kv_cache.cu:12-19,
+ * SpatialCache::preprocess_mask spatial_kv_cache.cu:153-158) and the host-supplied index lists of
+ * the reference (test_gather_scatter.cpp:47,77). mask[i] = 2 where valid[i] == 0; idx[0..M) =
+ * ascending i with mask[i] != 0; *count = M (device int32). Warp-ballot + block scan. */
+int32_t fxr_mask_compact(int32_t* mask, const uint8_t* valid, int32_t n_tokens,
+                         int32_t* idx, int32_t* count, void* stream);
+
+/* Reference preprocess alone (spatial_kv_cache.cu:12-19): mask[i] = 2 where !valid[i]. */
+int32_t fxr_preprocess_mask(int32_t* mask, const uint8_t* valid, int32_t n_tokens, void* stream);
+
+/* Fused gather + per-head QK-RMSNorm + multi-axis RoPE + cache-row write.
+ * Replaces gather_tokens (gather_scatter_kernels.cu:15-41) + rms_norm (flux2_kernels.cu:58-90,
+ * per head) + the K/V merge/update of sync_kv_cache_kernel (spatial_kv_cache.cu:55-87) restricted
+ * to the executed rows. For m < *count, token i = idx[m], mode = mask[i]:
+ *   qc[m]      = rope(rmsnorm(Q[i], norm_q))          (compact, row stride ld_qc)
+ *   if mode == 1: save[m] = (cache_k[i], cache_v[i])  (restored by fxr_restore_rows)
+ *   cache_k[i] = rope(rmsnorm(K[i], norm_k)),  cache_v[i] = V[i]  (bit-exact copy)
+ * save: [N, 2*n_heads*head_dim] elements, may be NULL when no mask value is 1. */
+int32_t fxr_gather_norm_rope(const fxr_frame_desc* desc,
+                             const void* q, const void* k, const void* v,
+                             const int32_t* mask, const int32_t* idx, const int32_t* count,
+                             const int32_t* pos, const float* norm_q, const float* norm_k,
+                             void* qc, int64_t ld_qc, void* cache_k, void* cache_v, void* save,
+                             void* stream);
+
+/* Attention of the compact queries against all N cache rows, with the scatter fused into the
+ * epilogue: out[idx[m], h*D..] = softmax(qc[m,h] K_h^T * scale) V_h for m < *count.
+ * Replaces attention_fwd (attention_kernels.cu:85-173) + scatter_tokens
+ * (gather_scatter_kernels.cu:46-72). tcgen05/TMEM flash attention, TMA-staged K/V tiles.
+ * qc rows must be allocated for N rows (rows >= count are read but never stored). */
+int32_t fxr_attention_active(const fxr_frame_desc* desc,
+                             const void* qc, int64_t ld_qc, const int32_t* count,
+                             const void* cache_k, const void* cache_v,
+                             const int32_t* idx, void* out, void* stream);
+
+/* Restores the cache rows of mask==1 tokens from `save` (written by fxr_gather_norm_rope). */
+int32_t fxr_restore_rows(const fxr_frame_desc* desc, const int32_t* mask, const int32_t* idx,
+                         const int32_t* count, const void* save, void* cache_k, void* cache_v,
+                         void* stream);
+
+/* Byte-exact row gather / scatter over the first *count indices (count may be a device
+ * pointer, or NULL with host_count >= 0). 16-byte vectorised when row_bytes and strides allow.
+ * Replace gather_tokens / scatter_tokens (gather_scatter_kernels.cu:15-72). */
+int32_t fxr_gather_rows(const void* src, int64_t ld_src_bytes, const int32_t* idx,
+                        const int32_t* count, int32_t host_count,
+                        void* dst, int64_t ld_dst_bytes, int64_t row_bytes, void* stream);
+int32_t fxr_scatter_rows(const void* src, int64_t ld_src_bytes, const int32_t* idx,
+                         const int32_t* count, int32_t host_count,
+                         void* dst, int64_t ld_dst_bytes, int64_t row_bytes, void* stream);
+
+/* Full-frame K/V merge + update with the reference's exact semantics
+ * (sync_kv_cache_kernel, spatial_kv_cache.cu:55-87): keys[i] = execute ? keys[i] : cached[i];
+ * if update: cached[i] = fresh keys[i]; same for values. row_elems elements of `dtype` per row. */
+int32_t fxr_kv_sync(void* keys, void* values, void* cached_keys, void* cached_values,
+                    const int32_t* mask, int32_t n_tokens, int64_t row_elems, int32_t dtype,
+                    void* stream);
+
+/* Output-cache merge + valid-flag update (sync_output_cache_kernel, spatial_kv_cache.cu:21-53):
+ * image rows i in [0, n_image): pred = execute ? pred : cache; if update: cache = pred and
+ * valid[n_text + i] = 1. */
+int32_t fxr_output_cache_sync(void* pred, void* cache, const int32_t* mask, uint8_t* valid,
+                              int32_t n_text, int32_t n_image, int32_t channels, int32_t dtype,
+                              void* stream);
+
+/* Standalone row RMSNorm with the reference signature semantics (launch_rms_norm,
+ * flux2_kernels.h:22-24): y = x * rsqrt(mean(x^2) + eps) * w over rows of `dim` elements. */
+int32_t fxr_rms_norm(const void* x, void* y, const float* w, float eps, int64_t rows,
+                     int32_t dim, int32_t dtype, void* stream);
+
+/* ---- composite ------------------------------------------------------------------------------ */
+/* One frame: compact -> gather/norm/RoPE/cache write -> attention + scatter -> restore of
+ * mask==1 rows. The body of the sparse attention plugin's enqueue. Workspace: see
+ * fxr_workspace_size. Four kernel launches, no host synchronisation. */
+int32_t fxr_frame_forward(const fxr_frame_desc* desc,
+                          const void* q, const void* k, const void* v,
+                          int32_t* mask, const uint8_t* valid, const int32_t* pos,
+                          const float* norm_q, const float* norm_k,
+                          void* cache_k, void* cache_v, void* out,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* Device pointers into the workspace (for callers that want idx / count / compact Q). */
+int32_t fxr_workspace_views(const fxr_frame_desc* desc, void* workspace, int32_t** idx,
+                            int32_t** count, void** qc, int64_t* ld_qc, void** save);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FXR_H */

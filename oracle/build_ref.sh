@@ -1,0 +1,18 @@
+#!/usr/bin/env bash
+# Compiles fluxrt-cpp's own CUDA kernels for sm_100a from the reference sources, where they lie,
+# together with oracle/ref_shim.cu, into oracle/_ref/libfxr_refkernels.so (git-ignored; the .so
+# travels to the GPU box). No reference source is copied into this repository.
+# The reference's TensorRT plugin classes are not built: NvInferRuntime.h is absent here.
+set -euo pipefail
+here="$(cd "$(dirname "$0")" && pwd)"
+ref="${FXR_REFERENCE_ROOT:-/root/reference}"
+src="$ref/src/inference"
+out="$here/_ref"
+mkdir -p "$out"
+nvcc -gencode arch=compute_100a,code=sm_100a -O3 -std=c++17 -Xcompiler -fPIC -shared \
+  -I"$src/plugins" -I"$src/kernels" -I"$ref/src" \
+  "$src/plugins/gather_scatter_kernels.cu" "$src/plugins/flux2_kernels.cu" \
+  "$src/plugins/attention_kernels.cu" "$src/kernels/spatial_kv_cache.cu" \
+  "$here/ref_shim.cu" -o "$out/libfxr_refkernels.so.tmp"
+mv "$out/libfxr_refkernels.so.tmp" "$out/libfxr_refkernels.so"
+echo "$out/libfxr_refkernels.so"

@@ -1,0 +1,86 @@
+"""CPU tests of the C-ABI boundary: the library builds and loads, exports every symbol the public
+header declares, and rejects bad arguments before touching the GPU."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+import fxr
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "fxr.h")
+
+
+def _declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(fxr_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import build as B
+    B.build()
+    return fxr.load()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    declared = _declared_symbols()
+    assert len(declared) >= 15
+    out = subprocess.run(["nm", "-D", "--defined-only", fxr.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (fxr_[a-z0-9_]+)", out))
+    missing = [s for s in declared if s not in exported]
+    assert not missing, missing
+    assert sorted(fxr.EXPORTED) == sorted(s for s in declared if s in fxr.EXPORTED)
+    for s in declared:
+        assert hasattr(lib, s)
+
+
+def test_library_is_sm100a_only_and_self_contained(lib):
+    out = subprocess.run(["ldd", fxr.LIB_PATH], capture_output=True, text=True).stdout
+    assert "libcudart" not in out      # static runtime: nothing to resolve against torch's copy
+    assert "libtorch" not in out and "libpython" not in out
+    assert lib.fxr_abi_version() == 1
+
+
+def test_frame_desc_layout_matches_header():
+    # fxr_frame_desc: 10 int32 + 3 float + int32 reserved = 14*4 = 56 bytes, then 3 int64 -> 80
+    assert ctypes.sizeof(fxr.FrameDesc) == 80
+    assert fxr.FrameDesc.ld_qkv.offset == 56
+
+
+def test_workspace_size_and_views(lib):
+    cfg = fxr.FrameConfig(n_tokens=4608, n_text=512)
+    n = fxr.workspace_size(cfg)
+    C = 24 * 128
+    assert n >= 4608 * 4 + 4608 * C * 2 * 3
+    assert n % 256 == 0
+
+
+def test_invalid_arguments_rejected_without_gpu(lib):
+    d = fxr.FrameConfig(n_tokens=16, n_text=4, head_dim=64).desc()
+    st = lib.fxr_attention_active(ctypes.byref(d), None, 0, None, None, None, None, None, None)
+    assert st == fxr.FXR_ERR_UNSUPPORTED
+    assert b"head_dim" in lib.fxr_last_error_string()
+    d = fxr.FrameConfig(n_tokens=16, n_text=4).desc()
+    d.rope_axes_dim[0] = 15
+    st = lib.fxr_gather_norm_rope(ctypes.byref(d), *([None] * 10), 0, None, None, None, None)
+    assert st == fxr.FXR_ERR_INVALID
+    assert lib.fxr_mask_compact(None, None, -1, None, None, None) == fxr.FXR_ERR_INVALID
+    d = fxr.FrameConfig(n_tokens=16, n_text=4).desc()
+    st = lib.fxr_frame_forward(ctypes.byref(d), *([None] * 11), None, 0, None)
+    assert st == fxr.FXR_ERR_INVALID
+    assert lib.fxr_kv_sync(None, None, None, None, None, 4, 4, 7, None) == fxr.FXR_ERR_INVALID
+
+
+def test_product_path_has_no_cpu_fallback():
+    """The product package never imports or links the oracle."""
+    pkg = os.path.join(ROOT, "fluxrt-cpp_b200")
+    for dirpath, _, files in os.walk(pkg):
+        for f in files:
+            if f.endswith((".py", ".cu", ".cuh", ".cpp", ".h")):
+                text = open(os.path.join(dirpath, f)).read()
+                assert "oracle" not in text.lower(), f

@@ -1,0 +1,367 @@
+"""GPU parity tests: every step of the CUDA path, called through the C ABI, against the CPU oracle
+on the same seeded inputs.
+
+Bars (stated per test): compaction, gather/scatter/copies and cache bookkeeping bit-exact;
+normed+roped Q/K and attention outputs within max-abs 2e-3 and mean-abs 2e-4 of the fp32 oracle
+for fp16 storage. bf16 storage rounds every stored value (half-ulp 2^-9 relative, mean-abs ~1.1e-3
+for unit-RMS rows), so stored bf16 Q'/K' are checked against the oracle rounded to bf16: at most
+1 bf16 ulp apart element-wise and mean-abs <= 2e-4; bf16 attention outputs (|O| << 1) against the
+fp32 oracle at max-abs 4e-3 / mean-abs 2e-4.
+"""
+import numpy as np
+import pytest
+import torch
+
+import fxr
+import oracle as O
+import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+TDT = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}
+TOL_F16 = dict(max_abs=2e-3, mean_abs=2e-4)
+TOL_BF16_O = dict(max_abs=4e-3, mean_abs=2e-4)
+
+
+def dev(a, dtype="f32"):
+    return torch.from_numpy(np.ascontiguousarray(a)).to("cuda").to(TDT[dtype]) if dtype != "i32" else \
+        torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).to("cuda")
+
+
+def host(t):
+    return t.float().cpu().numpy() if t.is_floating_point() else t.cpu().numpy()
+
+
+def assert_close(got, ref, max_abs, mean_abs, what=""):
+    err = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+    assert np.isfinite(got).all(), f"{what}: non-finite values"
+    assert err.max() <= max_abs, f"{what}: max-abs {err.max():.3e} > {max_abs}"
+    assert err.mean() <= mean_abs, f"{what}: mean-abs {err.mean():.3e} > {mean_abs}"
+
+
+def assert_bf16_close(got, ref_fp32, what=""):
+    """|got - bf16(ref)| <= 1 bf16 ulp of bf16(ref) element-wise, mean-abs <= 2e-4."""
+    r = W.round_storage(ref_fp32, "bf16").astype(np.float64)
+    g = got.astype(np.float64)
+    assert np.isfinite(g).all(), f"{what}: non-finite values"
+    mag = np.maximum(np.abs(r), 2.0 ** -126)
+    ulp = 2.0 ** (np.floor(np.log2(mag)) - 7)
+    err = np.abs(g - r)
+    bad = err > ulp * (1 + 1e-6)
+    assert not bad.any(), f"{what}: {bad.sum()} elements > 1 bf16 ulp (worst {err[bad].max():.3e})"
+    assert err.mean() <= 2e-4, f"{what}: mean-abs vs bf16(oracle) {err.mean():.3e} > 2e-4"
+
+
+def check_qk(got, ref, dtype, what):
+    if dtype == "bf16":
+        assert_bf16_close(got, ref, what)
+    else:
+        assert_close(got, ref, what=what, **TOL_F16)
+
+
+def cfg_of(w: W.Workload, n_heads=None) -> fxr.FrameConfig:
+    return fxr.FrameConfig(n_tokens=w.n_tokens, n_text=w.n_text, n_heads=n_heads or w.n_heads,
+                           dtype=w.dtype, rope_axes=w.rope_axes, rope_theta=w.rope_theta)
+
+
+def small(w: W.Workload, n_heads: int) -> W.Workload:
+    return W.Workload(w.name + f"_h{n_heads}", w.grid_h, w.grid_w, w.n_text, n_heads, w.head_dim,
+                      w.dtype, w.active, w.pattern, w.rope_axes, w.rope_theta)
+
+
+def sync_ok():
+    torch.cuda.synchronize()
+    assert fxr.check_device_error() == 0
+
+
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("n", [0, 1, 31, 33, 1536, 4608, 16896, 40000])
+def test_mask_compact_bit_exact(cuda, n):
+    rng = np.random.default_rng(n + 11)
+    mask = rng.choice([0, 1, 2], size=n, p=[0.7, 0.1, 0.2]).astype(np.int32)
+    valid = (rng.random(n) < 0.9).astype(np.uint8)
+    m_ref, idx_ref = O.mask_compact(mask, valid)
+    dm = dev(mask, "i32")
+    dv = torch.from_numpy(valid).cuda()
+    idx = torch.full((max(n, 1),), -7, dtype=torch.int32, device="cuda")
+    cnt = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    fxr.mask_compact(dm, dv, idx, cnt)
+    sync_ok()
+    M = int(cnt.item())
+    assert M == idx_ref.size
+    assert np.array_equal(host(dm), m_ref)
+    assert np.array_equal(host(idx)[:M], idx_ref)
+    # without a validity array: pure compaction, mask untouched
+    dm2 = dev(mask, "i32")
+    fxr.mask_compact(dm2, None, idx, cnt)
+    sync_ok()
+    assert np.array_equal(host(dm2), mask)
+    assert np.array_equal(host(idx)[: int(cnt.item())], np.nonzero(mask)[0])
+
+
+def _frame_tensors(w: W.Workload, fr: dict):
+    t = {k: dev(fr[k], w.dtype) for k in ("q", "k", "v", "cache_k", "cache_v", "out")}
+    t["mask"] = dev(fr["mask"], "i32")
+    t["pos"] = dev(fr["pos"], "i32")
+    t["norm_q"] = dev(fr["norm_q"])
+    t["norm_k"] = dev(fr["norm_k"])
+    return t
+
+
+def _with_exec_only(fr: dict, seed: int, frac: float = 0.05) -> dict:
+    """Turns a fraction of the executed image rows into mask 1 (execute, keep cache)."""
+    rng = np.random.default_rng(seed)
+    m = fr["mask"].copy()
+    cand = np.nonzero(m == 2)[0]
+    pick = cand[rng.random(cand.size) < frac]
+    m[pick] = 1
+    fr = dict(fr)
+    fr["mask"] = m
+    return fr
+
+
+@pytest.mark.parametrize("wl,heads", [(W.C1, 24), (W.KLEIN, 6), (W.C2, 4)])
+def test_gather_norm_rope_parity(cuda, wl, heads):
+    w = small(wl, heads)
+    fr = _with_exec_only(W.make_frame(w, seed=5), seed=6)
+    cfg = cfg_of(w)
+    t = _frame_tensors(w, fr)
+    N, C = w.n_tokens, heads * 128
+    idx = torch.zeros(N, dtype=torch.int32, device="cuda")
+    cnt = torch.zeros(1, dtype=torch.int32, device="cuda")
+    qc = torch.zeros(N, C, dtype=TDT[w.dtype], device="cuda")
+    save = torch.zeros(N, 2 * C, dtype=TDT[w.dtype], device="cuda")
+    fxr.mask_compact(t["mask"], None, idx, cnt)
+    fxr.gather_norm_rope(cfg, t["q"], t["k"], t["v"], t["mask"], idx, cnt, t["pos"], t["norm_q"],
+                         t["norm_k"], qc, t["cache_k"], t["cache_v"], save)
+    sync_ok()
+    M = int(cnt.item())
+    idx_h = host(idx)[:M]
+    mask = fr["mask"]
+    assert np.array_equal(idx_h, np.nonzero(mask)[0])
+    # oracle per executed row and head
+    qn = O.rms_norm(fr["q"][idx_h].reshape(-1, 128), fr["norm_q"]).reshape(M, C)
+    kn = O.rms_norm(fr["k"][idx_h].reshape(-1, 128), fr["norm_k"]).reshape(M, C)
+    for r, i in enumerate(idx_h):
+        for h in range(heads):
+            sl = slice(h * 128, (h + 1) * 128)
+            qn[r, sl] = O.rope_row(qn[r, sl], fr["pos"][i], w.rope_axes, w.rope_theta)
+            kn[r, sl] = O.rope_row(kn[r, sl], fr["pos"][i], w.rope_axes, w.rope_theta)
+    check_qk(host(qc)[:M], qn, w.dtype, "Q'")
+    ck, cv = host(t["cache_k"]), host(t["cache_v"])
+    check_qk(ck[idx_h], kn, w.dtype, "K'")
+    assert np.array_equal(cv[idx_h], fr["v"][idx_h])                     # V copy: bit-exact
+    skipped = mask == 0
+    assert np.array_equal(ck[skipped], fr["cache_k"][skipped])
+    assert np.array_equal(cv[skipped], fr["cache_v"][skipped])
+    ones = np.nonzero(mask[idx_h] == 1)[0]
+    sv = host(save)
+    for r in ones:                                                         # saved old rows: bit-exact
+        assert np.array_equal(sv[r, :C], fr["cache_k"][idx_h[r]])
+        assert np.array_equal(sv[r, C:], fr["cache_v"][idx_h[r]])
+
+
+@pytest.mark.parametrize("M,N,H,dtype", [(1, 128, 1, "f16"), (77, 300, 2, "f16"), (256, 1536, 3, "bf16"),
+                                         (300, 1000, 2, "bf16"), (640, 4608, 2, "f16")])
+def test_attention_parity(cuda, M, N, H, dtype):
+    rng = np.random.default_rng(M * 7 + N)
+    C = H * 128
+    f = lambda *s: W.round_storage(rng.normal(size=s).astype(np.float32), dtype)
+    qc, k, v = f(N, C), f(N, C), f(N, C)
+    idx = np.sort(rng.choice(N, size=M, replace=False)).astype(np.int32)
+    out0 = f(N, C)
+    cfg = fxr.FrameConfig(n_tokens=N, n_text=0, n_heads=H, dtype=dtype)
+    d_out = dev(out0, dtype)
+    cnt = torch.tensor([M], dtype=torch.int32, device="cuda")
+    fxr.attention_active(cfg, dev(qc, dtype), cnt, dev(k, dtype), dev(v, dtype), dev(idx, "i32"), d_out)
+    sync_ok()
+    ref = O.attention(qc[:M], k, v, H, 128)
+    got = host(d_out)
+    tol = TOL_F16 if dtype == "f16" else TOL_BF16_O
+    assert_close(got[idx], ref, what="O", **tol)
+    untouched = np.ones(N, dtype=bool)
+    untouched[idx] = False
+    assert np.array_equal(got[untouched], out0[untouched])
+
+
+def _run_frame(w: W.Workload, fr: dict, valid=None, cfg=None):
+    cfg = cfg or cfg_of(w)
+    t = _frame_tensors(w, fr)
+    ws = torch.empty(fxr.workspace_size(cfg), dtype=torch.uint8, device="cuda")
+    dvalid = None if valid is None else torch.from_numpy(valid).cuda()
+    fxr.frame_forward(cfg, t["q"], t["k"], t["v"], t["mask"], dvalid, t["pos"], t["norm_q"],
+                      t["norm_k"], t["cache_k"], t["cache_v"], t["out"], ws)
+    sync_ok()
+    return {k: host(v) for k, v in t.items()}
+
+
+@pytest.mark.parametrize("wl,heads", [(W.C1, 24), (W.KLEIN, 24), (W.C3, 4), (W.C2, 6)])
+def test_frame_forward_parity(cuda, wl, heads):
+    w = small(wl, heads)
+    fr = _with_exec_only(W.make_frame(w, seed=21), seed=22)
+    rng = np.random.default_rng(23)
+    valid = (rng.random(w.n_tokens) < 0.97).astype(np.uint8)
+    g = _run_frame(w, fr, valid)
+    r = O.frame_forward(fr["q"], fr["k"], fr["v"], fr["mask"], valid, fr["pos"], fr["norm_q"],
+                        fr["norm_k"], fr["cache_k"], fr["cache_v"], fr["out"], heads, 128,
+                        w.rope_axes, w.rope_theta)
+    assert np.array_equal(g["mask"], r["mask"])                            # preprocess: bit-exact
+    ex = r["idx"]
+    skipped = r["mask"] == 0
+    assert np.array_equal(g["out"][skipped], fr["out"][skipped])           # untouched: bit-exact
+    assert np.array_equal(g["cache_k"][skipped], fr["cache_k"][skipped])
+    assert np.array_equal(g["cache_v"][skipped], fr["cache_v"][skipped])
+    ones = r["mask"] == 1
+    assert np.array_equal(g["cache_k"][ones], fr["cache_k"][ones])         # restored: bit-exact
+    assert np.array_equal(g["cache_v"][ones], fr["cache_v"][ones])
+    twos = r["mask"] == 2
+    assert np.array_equal(g["cache_v"][twos], fr["v"][twos])
+    tol_o = TOL_F16 if w.dtype == "f16" else TOL_BF16_O
+    check_qk(g["cache_k"][twos], r["cache_k"][twos], w.dtype, "K' cache")
+    assert_close(g["out"][ex], r["out"][ex], what="O", **tol_o)
+
+
+def test_frame_forward_deterministic_and_noop(cuda):
+    w = small(W.C2, 4)
+    fr = W.make_frame(w, seed=31)
+    a = _run_frame(w, fr)
+    b = _run_frame(w, fr)
+    for k in ("out", "cache_k", "cache_v", "mask"):
+        assert np.array_equal(a[k], b[k]), k
+    # nothing executed (all valid, mask 0): the frame is a no-op
+    fr0 = dict(fr)
+    fr0["mask"] = np.zeros(w.n_tokens, dtype=np.int32)
+    c = _run_frame(w, fr0, valid=np.ones(w.n_tokens, dtype=np.uint8))
+    assert np.array_equal(c["out"], fr["out"])
+    assert np.array_equal(c["cache_k"], fr["cache_k"])
+
+
+def test_full_size_c2_properties(cuda):
+    """BASELINE-size frame (1024^2, 25 %, 24 heads, bf16): checks that need no full oracle run:
+    untouched rows, cache bookkeeping, and a sampled subset of executed rows against the oracle."""
+    w = W.C2
+    fr = W.make_frame(w, seed=41)
+    g = _run_frame(w, fr)
+    mask = fr["mask"]
+    skipped = mask == 0
+    assert np.array_equal(g["out"][skipped], fr["out"][skipped])
+    assert np.array_equal(g["cache_v"][mask == 2], fr["v"][mask == 2])
+    ex = np.nonzero(mask)[0]
+    rng = np.random.default_rng(42)
+    rows = np.sort(rng.choice(ex.size, size=48, replace=False))
+    # oracle on the sampled rows: Q' from the oracle, all keys from the GPU cache after the frame
+    # (its K' rows are checked against the oracle in the smaller frame tests)
+    C = w.n_heads * 128
+    qn = O.rms_norm(fr["q"][ex[rows]].reshape(-1, 128), fr["norm_q"]).reshape(-1, C)
+    for r_, i in enumerate(ex[rows]):
+        for h in range(w.n_heads):
+            sl = slice(h * 128, (h + 1) * 128)
+            qn[r_, sl] = O.rope_row(qn[r_, sl], fr["pos"][i], w.rope_axes, w.rope_theta)
+    qn = W.round_storage(qn, "bf16")
+    ref = O.attention(qn, g["cache_k"], g["cache_v"], w.n_heads, 128)
+    assert_close(g["out"][ex[rows]], ref, what="O (sampled)", **TOL_BF16_O)
+
+
+# ---------------------------------------------------------------------------------------------
+# reference known-answer tests, run through the GPU path
+# ---------------------------------------------------------------------------------------------
+def test_reference_gather_scatter_known_answers(cuda):
+    import json, os
+    kat = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "reference_kat.json")))
+    g = kat["gather"]
+    src = dev(np.array(g["src"], dtype=np.float32).reshape(-1, g["dim"]))
+    dst = torch.zeros(len(g["indices"]), g["dim"], device="cuda")
+    fxr.gather_rows(src, dev(np.array(g["indices"]), "i32"), dst, host_count=len(g["indices"]))
+    sync_ok()
+    assert host(dst).reshape(-1).tolist() == g["expected"]
+    s = kat["scatter"]
+    dst = torch.full((s["seq_len"], s["dim"]), s["dst_init"], device="cuda")
+    src = dev(np.array(s["src"], dtype=np.float32).reshape(-1, s["dim"]))
+    fxr.scatter_rows(src, dev(np.array(s["indices"]), "i32"), dst, host_count=len(s["indices"]))
+    sync_ok()
+    assert host(dst).reshape(-1).tolist() == s["expected"]
+
+
+def test_reference_spatial_cache_known_answers(cuda):
+    import json, os
+    kat = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "reference_kat.json")))
+    c = kat["cache"]
+    n = c["img_len"] + c["txt_len"]
+    valid = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    mask = dev(np.array(c["mask0"]), "i32")
+    fxr.preprocess_mask(mask, valid)
+    sync_ok()
+    assert host(mask).tolist() == c["mask0_expected"]
+    pred = dev(np.array(c["pred1"], dtype=np.float32).reshape(c["img_len"], c["out_ch"]))
+    cache = torch.zeros_like(pred)
+    fxr.output_cache_sync(pred, cache, mask, valid, c["txt_len"])
+    sync_ok()
+    assert host(pred).reshape(-1).tolist() == c["pred1_expected"]
+    mask2 = dev(np.array(c["mask2"]), "i32")
+    pred2 = dev(np.array(c["pred2"], dtype=np.float32).reshape(c["img_len"], c["out_ch"]))
+    fxr.output_cache_sync(pred2, cache, mask2, valid, c["txt_len"])
+    sync_ok()
+    flat = host(pred2).reshape(-1)
+    for k, v in c["pred2_checks"].items():
+        assert flat[int(k)] == v
+    m = kat["cache_mixed"]
+    t_, i_ = m["txt_len"], m["img_len"]
+    valid = torch.zeros(t_ + i_, dtype=torch.uint8, device="cuda")
+    mk = torch.zeros(t_ + i_, dtype=torch.int32, device="cuda")
+    fxr.preprocess_mask(mk, valid)
+    sync_ok()
+    assert host(mk).tolist() == m["after_reset_expected"]
+    pred = torch.ones(i_, m["out_ch"], device="cuda")
+    fxr.output_cache_sync(pred, torch.zeros_like(pred), dev(np.array(m["populate_mask"]), "i32"), valid, t_)
+    mk = torch.zeros(t_ + i_, dtype=torch.int32, device="cuda")
+    idx = torch.zeros(t_ + i_, dtype=torch.int32, device="cuda")
+    cnt = torch.zeros(1, dtype=torch.int32, device="cuda")
+    fxr.mask_compact(mk, valid, idx, cnt)
+    sync_ok()
+    assert host(mk).tolist() == m["final_expected"]
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+def test_kv_sync_bit_exact(cuda, dtype):
+    rng = np.random.default_rng(9)
+    n, e = 257, 3 * 128 + (0 if dtype != "f32" else 1)
+    arrs = [W.round_storage(rng.normal(size=(n, e)).astype(np.float32), dtype) for _ in range(4)]
+    mask = rng.choice([0, 1, 2], size=n).astype(np.int32)
+    ref = O.kv_sync(*arrs, mask)
+    d = [dev(a, dtype) for a in arrs]
+    fxr.kv_sync(*d, dev(mask, "i32"))
+    sync_ok()
+    for got, exp in zip(d, ref):
+        assert np.array_equal(host(got), exp)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_output_cache_sync_bit_exact(cuda, dtype):
+    rng = np.random.default_rng(10)
+    T, I, ch = 5, 300, 3072
+    pred = W.round_storage(rng.normal(size=(I, ch)).astype(np.float32), dtype)
+    cache = W.round_storage(rng.normal(size=(I, ch)).astype(np.float32), dtype)
+    mask = rng.choice([0, 1, 2], size=T + I).astype(np.int32)
+    valid = (rng.random(T + I) < 0.5).astype(np.uint8)
+    rp, rc, rv = O.output_cache_sync(pred, cache, mask, valid, T)
+    dp, dc, dv = dev(pred, dtype), dev(cache, dtype), torch.from_numpy(valid).cuda()
+    fxr.output_cache_sync(dp, dc, dev(mask, "i32"), dv, T)
+    sync_ok()
+    assert np.array_equal(host(dp), rp) and np.array_equal(host(dc), rc)
+    assert np.array_equal(host(dv), rv)
+
+
+@pytest.mark.parametrize("dtype,dim", [("f32", 3072), ("f32", 100), ("f16", 128), ("bf16", 128)])
+def test_rms_norm_standalone(cuda, dtype, dim):
+    rng = np.random.default_rng(dim)
+    x = W.round_storage(rng.normal(size=(37, dim)).astype(np.float32), dtype)
+    w = rng.normal(1, 0.1, size=dim).astype(np.float32)
+    ref = O.rms_norm(x, w, 1e-6)
+    dx = dev(x, dtype)
+    dy = torch.empty_like(dx)
+    fxr.rms_norm(dx, dy, dev(w), 1e-6)
+    sync_ok()
+    if dtype == "f32":
+        assert_close(host(dy), ref, what="rmsnorm", max_abs=2e-5, mean_abs=2e-6)
+    else:
+        check_qk(host(dy), ref, dtype, "rmsnorm")
