@@ -341,29 +341,39 @@ def run_ours(args):
 
 
 def per_kernel_times(cfg, w, frames, wss, stream, reps: int):
+    """Per-kernel device time: the four launches of `reps` frames are captured in one CUDA graph
+    with event records between them (on the launching stream), so host launch overhead does not
+    leak into the intervals; median over frames."""
     import torch
-    import fxr
-    ev = lambda: torch.cuda.Event(enable_timing=True)
-    acc = {"compact_us": [], "gather_us": [], "attention_us": [], "restore_us": []}
-    for i in range(reps):
-        fr, ws = frames[i % len(frames)], wss[i % len(wss)]
-        idx, cnt, qc, ld_qc, save = fxr.workspace_views(cfg, ws)
-        e = [ev() for _ in range(5)]
-        e[0].record(stream)
-        _raw_compact(fr, idx, cnt)
-        e[1].record(stream)
-        _raw_gather(cfg, fr, idx, cnt, qc, ld_qc, save)
-        e[2].record(stream)
-        _raw_attention(cfg, fr, qc, ld_qc, cnt, idx)
-        e[3].record(stream)
-        _raw_restore(cfg, fr, idx, cnt, save)
-        e[4].record(stream)
-        torch.cuda.synchronize()
-        if i >= 2:
-            acc["compact_us"].append(e[0].elapsed_time(e[1]) * 1e3)
-            acc["gather_us"].append(e[1].elapsed_time(e[2]) * 1e3)
-            acc["attention_us"].append(e[2].elapsed_time(e[3]) * 1e3)
-            acc["restore_us"].append(e[3].elapsed_time(e[4]) * 1e3)
+    ev = lambda: torch.cuda.Event(enable_timing=True, external=True)
+    names = ["compact_us", "gather_us", "attention_us", "restore_us"]
+    events = [[ev() for _ in range(5)] for _ in range(reps)]
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        s = torch.cuda.current_stream()
+        for i in range(reps):
+            fr, ws = frames[i % len(frames)], wss[i % len(wss)]
+            idx, cnt, qc, ld_qc, save = __import__("fxr").workspace_views(cfg, ws)
+            e = events[i]
+            e[0].record(s)
+            _raw_compact(fr, idx, cnt)
+            e[1].record(s)
+            _raw_gather(cfg, fr, idx, cnt, qc, ld_qc, save)
+            e[2].record(s)
+            _raw_attention(cfg, fr, qc, ld_qc, cnt, idx)
+            e[3].record(s)
+            _raw_restore(cfg, fr, idx, cnt, save)
+            e[4].record(s)
+    g.replay()
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    acc = {k: [] for k in names}
+    for i in range(2, reps):
+        e = events[i]
+        for k, name in enumerate(names):
+            acc[name].append(e[k].elapsed_time(e[k + 1]) * 1e3)
+    del g
     return {k: statistics.median(v) for k, v in acc.items()}
 
 

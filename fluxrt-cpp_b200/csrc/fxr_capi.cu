@@ -13,6 +13,7 @@
 
 #include "fxr.h"
 #include "fxr_attention.cuh"
+#include "fxr_compat_kernels.cuh"
 #include "fxr_device.cuh"
 #include "fxr_mem_kernels.cuh"
 
@@ -194,7 +195,7 @@ int grid_rows(int64_t rows, int rows_per_cta) {
 template <typename T>
 int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
                          const int32_t* count, const void* ck, const void* cv, const int32_t* idx,
-                         void* out, cudaStream_t stream, float* dbg = nullptr) {
+                         void* out, cudaStream_t stream) {
     static bool configured[kMaxDevices] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -219,10 +220,9 @@ int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
     p.ld_out = d->ld_out;
     p.n_tokens = d->n_tokens;
     p.n_heads = d->n_heads;
-    p.dbg = dbg;
     const float scale = d->softmax_scale > 0.f ? d->softmax_scale : 1.0f / std::sqrt((float)d->head_dim);
     p.scale_log2 = scale * 1.4426950408889634f;
-    const int64_t max_tiles = (N + fxr::attn::kBM - 1) / fxr::attn::kBM * d->n_heads;
+    const int64_t max_tiles = (N + fxr::attn::kUnitRows - 1) / fxr::attn::kUnitRows * d->n_heads;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_tiles, sm_count()));
     fxr::attn::attention_kernel<T><<<grid, fxr::attn::kThreads, fxr::attn::kSmemBytes, stream>>>(
         tq, tk, tv, p);
@@ -257,7 +257,9 @@ int32_t launch_gather(const fxr_frame_desc* d, const void* q, const void* k, con
     a.n_axes = d->rope_n_axes;
     a.eps = d->eps;
     fill_rope(d, &a.rope);
-    const int grid = grid_rows(d->n_tokens, fxr::kGatherThreads / 32);
+    const int64_t groups = (d->n_heads + fxr::kGatherHeadsPerItem - 1) / fxr::kGatherHeadsPerItem;
+    const int64_t need = ((int64_t)d->n_tokens * groups + 7) / 8;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, (int64_t)sm_count() * fxr::kGatherMinBlocks));
     fxr::gather_norm_rope_kernel<T><<<grid, fxr::kGatherThreads, 0, stream>>>(a);
     FXR_CHECK_LAUNCH("gather_norm_rope_kernel launch");
     return FXR_OK;
@@ -370,22 +372,6 @@ int32_t fxr_attention_active(const fxr_frame_desc* desc, const void* qc, int64_t
     if (desc->dtype == FXR_BF16)
         return launch_attention<__nv_bfloat16>(desc, qc, ld_qc, count, cache_k, cache_v, idx, out, s);
     return launch_attention<__half>(desc, qc, ld_qc, count, cache_k, cache_v, idx, out, s);
-}
-
-// Diagnostic variant of fxr_attention_active (not part of the public header): also writes CTA 0's
-// first tile internals into dbg (34816 floats): raw scores of key tile 0, unnormalised O, row sums,
-// row maxima.
-int32_t fxr_debug_attention(const fxr_frame_desc* desc, const void* qc, int64_t ld_qc,
-                            const int32_t* count, const void* cache_k, const void* cache_v,
-                            const int32_t* idx, void* out, float* dbg, void* stream) {
-    int32_t st = check_desc(desc, true);
-    if (st != FXR_OK) return st;
-    if (!qc || !count || !cache_k || !cache_v || !idx || !out || !dbg)
-        return fail(FXR_ERR_INVALID, "null pointer argument");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (desc->dtype == FXR_BF16)
-        return launch_attention<__nv_bfloat16>(desc, qc, ld_qc, count, cache_k, cache_v, idx, out, s, dbg);
-    return launch_attention<__half>(desc, qc, ld_qc, count, cache_k, cache_v, idx, out, s, dbg);
 }
 
 int32_t fxr_restore_rows(const fxr_frame_desc* desc, const int32_t* mask, const int32_t* idx,
@@ -541,6 +527,29 @@ int32_t fxr_rms_norm(const void* x, void* y, const float* w, float eps, int64_t 
             return fail(FXR_ERR_INVALID, "bad dtype %d", dtype);
     }
     FXR_CHECK_LAUNCH("rms_norm_kernel launch");
+    return FXR_OK;
+}
+
+int32_t fxr_attention_f32_bhsd(const float* q, const float* k, const float* v, float* out,
+                               int32_t batch, int32_t num_heads, int32_t q_len, int32_t kv_len,
+                               int32_t head_dim, void* stream) {
+    if (batch < 0 || num_heads < 0 || q_len < 0 || kv_len < 0 || head_dim < 0)
+        return fail(FXR_ERR_INVALID, "negative size");
+    if (batch == 0 || num_heads == 0 || q_len == 0 || kv_len == 0 || head_dim == 0) return FXR_OK;
+    if (head_dim > fxr::kF32AttnMaxD)
+        return fail(FXR_ERR_UNSUPPORTED, "head_dim %d > %d", head_dim, fxr::kF32AttnMaxD);
+    if (!q || !k || !v || !out) return fail(FXR_ERR_INVALID, "null pointer argument");
+    const size_t smem = fxr::f32_attention_smem(head_dim);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(fxr::attention_f32_bhsd_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention_f32)");
+    }
+    const dim3 grid((q_len + fxr::kF32AttnWarps - 1) / fxr::kF32AttnWarps, batch * num_heads);
+    const float scale = 1.0f / std::sqrt((float)head_dim);
+    fxr::attention_f32_bhsd_kernel<<<grid, fxr::kF32AttnWarps * 32, smem, static_cast<cudaStream_t>(stream)>>>(
+        q, k, v, out, q_len, kv_len, head_dim, scale);
+    FXR_CHECK_LAUNCH("attention_f32_bhsd_kernel launch");
     return FXR_OK;
 }
 

@@ -123,6 +123,16 @@ struct GatherArgs {
 
 constexpr int kGatherThreads = 256;
 
+// sin/cos of a rotary angle (|angle| up to a few thousand radians): Cody-Waite reduction by 2*pi
+// with the constant split into an exactly representable head (6.28125) and a tail, then the
+// hardware sine/cosine on [-pi, pi] (absolute error ~4e-7 there).
+__device__ __forceinline__ void rope_sincos(float ang, float* s, float* c) {
+    const float k = rintf(ang * 0.15915494309189535f);
+    float r = fmaf(-k, 6.28125f, ang);
+    r = fmaf(-k, 1.9353071795864769e-3f, r);
+    __sincosf(r, s, c);
+}
+
 template <typename T>
 __device__ __forceinline__ void norm_rope_store(const uint4& x, const float* w, float eps,
                                                 const float* cs, const float* sn, T* dst,
@@ -151,20 +161,21 @@ __device__ __forceinline__ void norm_rope_store(const uint4& x, const float* w, 
     if (active) *reinterpret_cast<uint4*>(dst) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
 }
 
+// Work item = (executed row m, group of up to 8 heads); one warp per item. All 12 of a lane's
+// 16-byte loads (Q, K, V of 4 head pairs) are issued before any arithmetic so that every warp keeps
+// 6 KB in flight; 2 CTAs of 8 warps per SM keep ~96 KB in flight per SM.
+constexpr int kGatherHeadsPerItem = 8;
+constexpr int kGatherMinBlocks = 2;
+
 template <typename T>
-__global__ void __launch_bounds__(kGatherThreads)
+__global__ void __launch_bounds__(kGatherThreads, kGatherMinBlocks)
 gather_norm_rope_kernel(const __grid_constant__ GatherArgs a) {
     const int lane = threadIdx.x & 31, half = lane >> 4, sub = lane & 15;
     const int warps_per_cta = kGatherThreads / 32;
     const int32_t M = *a.count;
     const int64_t C = (int64_t)a.n_heads * kHeadDim;
-    float wq[8], wk[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        wq[e] = a.norm_q[8 * sub + e];
-        wk[e] = a.norm_k[8 * sub + e];
-    }
-    const int npairs = (a.n_heads + 1) >> 1;
+    const int groups = (a.n_heads + kGatherHeadsPerItem - 1) / kGatherHeadsPerItem;
+    const int64_t items = (int64_t)M * groups;
     const T* __restrict__ Q = static_cast<const T*>(a.q);
     const T* __restrict__ K = static_cast<const T*>(a.k);
     const T* __restrict__ V = static_cast<const T*>(a.v);
@@ -173,14 +184,33 @@ gather_norm_rope_kernel(const __grid_constant__ GatherArgs a) {
     T* __restrict__ CV = static_cast<T*>(a.cache_v);
     T* __restrict__ SV = static_cast<T*>(a.save);
 
-    for (int32_t m = blockIdx.x * warps_per_cta + (threadIdx.x >> 5); m < M;
-         m += gridDim.x * warps_per_cta) {
-        const int32_t i = a.idx[m];
+    for (int64_t it = (int64_t)blockIdx.x * warps_per_cta + (threadIdx.x >> 5); it < items;
+         it += (int64_t)gridDim.x * warps_per_cta) {
+        const int32_t m = (int32_t)(it / groups);
+        const int h0 = (int)(it - (int64_t)m * groups) * kGatherHeadsPerItem;
+        const int32_t i = __ldg(a.idx + m);
         if (i < 0 || i >= a.n_tokens) {
             if (lane == 0) atomicOr(&g_error_word, kErrBounds);
             continue;
         }
-        const int32_t mode = a.mask[i];
+        const T* qrow = Q + (int64_t)i * a.ld_qkv + 8 * sub;
+        const T* krow = K + (int64_t)i * a.ld_qkv + 8 * sub;
+        const T* vrow = V + (int64_t)i * a.ld_qkv + 8 * sub;
+        uint4 qv[4], kv[4], vv[4];
+        bool act[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int h = h0 + 2 * u + half;
+            act[u] = h < a.n_heads;
+            if (act[u]) {
+                qv[u] = __ldg(reinterpret_cast<const uint4*>(qrow + h * kHeadDim));
+                kv[u] = __ldg(reinterpret_cast<const uint4*>(krow + h * kHeadDim));
+                vv[u] = __ldg(reinterpret_cast<const uint4*>(vrow + h * kHeadDim));
+            } else {
+                qv[u] = kv[u] = vv[u] = make_uint4(0, 0, 0, 0);
+            }
+        }
+        const int32_t mode = __ldg(a.mask + i);
         float cs[4], sn[4];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
@@ -190,52 +220,42 @@ gather_norm_rope_kernel(const __grid_constant__ GatherArgs a) {
                 cs[t] = 1.f;
                 sn[t] = 0.f;
             } else {
-                const float ang = (float)a.pos[(int64_t)i * a.n_axes + ax] * a.rope.omega[j];
-                sincosf(ang, &sn[t], &cs[t]);
+                const float ang = (float)__ldg(a.pos + (int64_t)i * a.n_axes + ax) * a.rope.omega[j];
+                rope_sincos(ang, &sn[t], &cs[t]);
             }
         }
-        const T* qrow = Q + (int64_t)i * a.ld_qkv + 8 * sub;
-        const T* krow = K + (int64_t)i * a.ld_qkv + 8 * sub;
-        const T* vrow = V + (int64_t)i * a.ld_qkv + 8 * sub;
         T* qcrow = QC + (int64_t)m * a.ld_qc + 8 * sub;
         T* ckrow = CK + (int64_t)i * a.ld_cache + 8 * sub;
         T* cvrow = CV + (int64_t)i * a.ld_cache + 8 * sub;
-        for (int hp0 = 0; hp0 < npairs; hp0 += 4) {
-            uint4 qv[4], kv[4], vv[4];
-            bool act[4];
+        if (mode == 1 && SV != nullptr) {
+            T* srow = SV + (int64_t)m * 2 * C + 8 * sub;
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                const int h = 2 * (hp0 + u) + half;
-                act[u] = (hp0 + u < npairs) && (h < a.n_heads);
+                const int h = h0 + 2 * u + half;
                 if (act[u]) {
-                    qv[u] = __ldg(reinterpret_cast<const uint4*>(qrow + h * kHeadDim));
-                    kv[u] = __ldg(reinterpret_cast<const uint4*>(krow + h * kHeadDim));
-                    vv[u] = __ldg(reinterpret_cast<const uint4*>(vrow + h * kHeadDim));
-                } else {
-                    qv[u] = kv[u] = vv[u] = make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4*>(srow + h * kHeadDim) =
+                        *reinterpret_cast<const uint4*>(ckrow + h * kHeadDim);
+                    *reinterpret_cast<uint4*>(srow + C + h * kHeadDim) =
+                        *reinterpret_cast<const uint4*>(cvrow + h * kHeadDim);
                 }
             }
-            if (mode == 1 && SV != nullptr) {
-                T* srow = SV + (int64_t)m * 2 * C + 8 * sub;
+        }
+        float w[8];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int h = 2 * (hp0 + u) + half;
-                    if (act[u]) {
-                        *reinterpret_cast<uint4*>(srow + h * kHeadDim) =
-                            *reinterpret_cast<const uint4*>(ckrow + h * kHeadDim);
-                        *reinterpret_cast<uint4*>(srow + C + h * kHeadDim) =
-                            *reinterpret_cast<const uint4*>(cvrow + h * kHeadDim);
-                    }
-                }
-            }
+        for (int e = 0; e < 8; ++e) w[e] = __ldg(a.norm_q + 8 * sub + e);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int h = 2 * (hp0 + u) + half;
-                // every lane joins the shuffles; inactive heads compute on zeros and skip the store
-                norm_rope_store<T>(qv[u], wq, a.eps, cs, sn, qcrow + h * kHeadDim, act[u]);
-                norm_rope_store<T>(kv[u], wk, a.eps, cs, sn, ckrow + h * kHeadDim, act[u]);
-                if (act[u]) *reinterpret_cast<uint4*>(cvrow + h * kHeadDim) = vv[u];
-            }
+        for (int u = 0; u < 4; ++u) {
+            // every lane joins the shuffles; inactive heads compute on zeros and skip the store
+            const int h = h0 + 2 * u + half;
+            norm_rope_store<T>(qv[u], w, a.eps, cs, sn, qcrow + h * kHeadDim, act[u]);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) w[e] = __ldg(a.norm_k + 8 * sub + e);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int h = h0 + 2 * u + half;
+            norm_rope_store<T>(kv[u], w, a.eps, cs, sn, ckrow + h * kHeadDim, act[u]);
+            if (act[u]) *reinterpret_cast<uint4*>(cvrow + h * kHeadDim) = vv[u];
         }
     }
 }

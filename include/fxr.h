@@ -159,6 +159,14 @@ int32_t fxr_output_cache_sync(void* pred, void* cache, const int32_t* mask, uint
 int32_t fxr_rms_norm(const void* x, void* y, const float* w, float eps, int64_t rows,
                      int32_t dim, int32_t dtype, void* stream);
 
+/* fp32 attention in the reference's (batch, heads, len, head_dim) layout, head_dim <= 256:
+ * out = softmax(Q K^T / sqrt(head_dim)) V with one softmax over all kv_len keys. Backs the
+ * reference-signature attention_fwd (attention_kernels.h:20-24); SIMT fp32, not the tensor-core
+ * path (fxr_attention_active). */
+int32_t fxr_attention_f32_bhsd(const float* q, const float* k, const float* v, float* out,
+                               int32_t batch, int32_t num_heads, int32_t q_len, int32_t kv_len,
+                               int32_t head_dim, void* stream);
+
 /* ---- composite ------------------------------------------------------------------------------ */
 /* One frame: compact -> gather/norm/RoPE/cache write -> attention + scatter -> restore of
  * mask==1 rows. The body of the sparse attention plugin's enqueue. Workspace: see

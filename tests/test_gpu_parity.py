@@ -40,14 +40,16 @@ def assert_close(got, ref, max_abs, mean_abs, what=""):
 
 
 def assert_bf16_close(got, ref_fp32, what=""):
-    """|got - bf16(ref)| <= 1 bf16 ulp of bf16(ref) element-wise, mean-abs <= 2e-4."""
+    """|got - bf16(ref)| <= max(1 bf16 ulp of bf16(ref), 1e-5) element-wise, mean-abs <= 2e-4.
+    The 1e-5 floor covers near-zero RoPE outputs (a*cos - b*sin cancelling), whose absolute error
+    is set by the fp32 rotation angle pos*omega (|angle| <= ~130 rad, fp32 rounding ~1e-5 rad)."""
     r = W.round_storage(ref_fp32, "bf16").astype(np.float64)
     g = got.astype(np.float64)
     assert np.isfinite(g).all(), f"{what}: non-finite values"
     mag = np.maximum(np.abs(r), 2.0 ** -126)
     ulp = 2.0 ** (np.floor(np.log2(mag)) - 7)
     err = np.abs(g - r)
-    bad = err > ulp * (1 + 1e-6)
+    bad = err > np.maximum(ulp * (1 + 1e-6), 1e-5)
     assert not bad.any(), f"{what}: {bad.sum()} elements > 1 bf16 ulp (worst {err[bad].max():.3e})"
     assert err.mean() <= 2e-4, f"{what}: mean-abs vs bf16(oracle) {err.mean():.3e} > 2e-4"
 
