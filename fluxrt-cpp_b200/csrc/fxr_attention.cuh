@@ -1,27 +1,32 @@
 // fxr_attention.cuh — active-query flash attention on the 5th-generation tensor cores (sm_100a).
 //
-// Work unit: 256 compact query rows (two 128-row tiles Q0, Q1) of one head against all N keys of
-// that head in 128-key tiles. Persistent CTAs (one per SM) walk the work units round-robin; the
-// executed-row count M is read from device memory, so the grid never depends on it.
+// Work unit: one 128-row tile of compact queries of one head against all N keys of that head,
+// in steps of 256 keys (two 128-key sub-tiles). Persistent CTAs (one per SM) walk the work units
+// round-robin; the executed-row count M is read from device memory, so the grid never depends on it.
 //
-// Warp roles (384 threads):
-//   warp 0      TMA producer: Q0+Q1, a 3-deep K ring and a 2-deep V ring (128-byte swizzle)
-//   warp 1      TMEM allocator and the single MMA-issuing thread
-//   warps 4-7   softmax / O correction / epilogue of Q0 (one thread per row = TMEM lane)
-//   warps 8-11  the same for Q1
-// Tensor memory (512 columns): S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512).
-// P_t (16-bit pairs) overwrites the first 64 columns of S_t and is the A operand of O_t += P_t V.
+// Warp roles (576 threads):
+//   warps 0-15  softmax: warpgroup g = warp/4 owns score columns [64g, 64g+64) of each step for
+//               all 128 rows (one thread per row = TMEM lane), and O columns [32g, 32g+32) for the
+//               correction and the epilogue
+//   warp 16     TMA producer: Q tile, a 3-slot K ring and a 2-slot V ring of 128-key sub-tiles
+//               (128-byte swizzle)
+//   warp 17     TMEM allocator and the single MMA-issuing thread
+// Tensor memory (512 columns): S [0,256) fp32 scores of one step, P [256,384) the 16-bit
+// probabilities of the step (pairs packed per column), O [384,512) fp32 output accumulator.
 //
-// MMA order per key tile j (ping-pong): PV0(j), QK0(j+1), PV1(j), QK1(j+1). While softmax 0 works
-// on S0(j) the tensor core runs PV1(j-1) and QK1(j); while softmax 1 works on S1(j) it runs PV0(j)
-// and QK0(j+1). tcgen05 operations of one thread execute in issue order, and a commit tracks all
-// earlier operations of the thread, so the barrier that signals S_t(j) also guarantees that
-// PV_t(j-1) finished: the softmax may rescale O_t right away.
+// Pipeline. S and P live in separate tensor memory, so the scores of step j+1 can be computed as
+// soon as the softmax has loaded S(j) into registers (barrier S_FREE), while it still works on
+// step j; the softmax only waits for PV(j-1) to finish (barrier P_FREE) right before it stores
+// P(j). Tensor-core order: QK(j+1), PV(j), QK(j+2), ... A tcgen05.mma costs ~64-72 cycles for any
+// N <= 128 (measured), so QK uses N = 128 per sub-tile and PV N = 128 (head dim) with A = P read
+// from tensor memory.
 // Softmax in the exp2 domain with lazy rescaling: O and the running sum are rescaled only when a
-// row maximum grows by more than 2^8, so p <= 256 between rescales and O / l is exact. The
-// special-function unit computes 16 exp2 per clock per SM, exactly the rate at which one SM's
-// tensor core consumes them (4*128 FLOP per score), so a quarter of the exponentials run as a
-// polynomial on the FMA pipe (ex2_poly).
+// row maximum grows by more than 2^8, so p <= 256 between rescales and O / l is exact. The four
+// warpgroups combine their partial row maxima through shared memory behind an mbarrier each step
+// (bounded waits, no named barrier that could outlive an aborted partner), and their partial row
+// sums once in the epilogue. The special-function unit computes 16 exp2 per clock per SM, the rate
+// at which the tensor core consumes them (4*128 FLOP per score), so a quarter of the
+// exponentials run as a polynomial on the FMA pipe (ex2_poly).
 // The reference's scatter is fused: the epilogue stores row m straight to out[idx[m], h*128 ...].
 // Every mbarrier wait is bounded (2 s); on timeout the kernel sets the device error word, drains
 // its outstanding copies and MMAs, frees its tensor memory and returns.
@@ -36,37 +41,41 @@
 namespace fxr {
 namespace attn {
 
-constexpr int kBM = 128;                        // query rows per tile (two tiles per work unit)
-constexpr int kUnitRows = 2 * kBM;
-constexpr int kBN = 128;                        // keys per tile
+constexpr int kBM = 128;                        // query rows per work unit
+constexpr int kSubN = 128;                      // keys per K/V sub-tile
+constexpr int kStepN = 2 * kSubN;               // keys per softmax step
 constexpr int kD = 128;                         // head dim
-constexpr int kKStages = 3;
-constexpr int kVStages = 2;
-constexpr int kThreads = 384;
+constexpr int kSlots = 5;                       // K/V sub-tile ring, filled in consumption order
+constexpr int kSoftmaxWarps = 16;
+constexpr int kProducerWarp = 16;
+constexpr int kMmaWarp = 17;
+constexpr int kThreads = 32 * (kSoftmaxWarps + 2);
+constexpr uint32_t kSoftmaxThreads = 32 * kSoftmaxWarps;
 constexpr uint32_t kHalfBytes = 128 * 128;      // 128 rows x 64 16-bit values (one swizzle span)
 constexpr uint32_t kTileBytes = 2 * kHalfBytes; // 128 x 128 16-bit tile
-constexpr uint32_t kSmemQ = 0;                  // Q0, Q1
-constexpr uint32_t kSmemK = 2 * kTileBytes;
-constexpr uint32_t kSmemV = kSmemK + kKStages * kTileBytes;
-constexpr uint32_t kSmemBar = kSmemV + kVStages * kTileBytes;
-constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;  // barriers + alignment slack
+constexpr uint32_t kSmemQ = 0;
+constexpr uint32_t kSmemRing = kTileBytes;
+constexpr uint32_t kSmemX = kSmemRing + kSlots * kTileBytes;  // exchange [2 buf][4 wg][128 rows]
+constexpr uint32_t kSmemBar = kSmemX + 2 * 4 * 128 * 4;
+constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;       // barriers + alignment slack
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
 constexpr float kRescaleThreshold = 8.0f;       // log2 units
-constexpr int kPolyPeriod = 4;                  // of every 4 score pairs ...
-constexpr int kPolyCount = 1;                   // ... this many use ex2_poly
+constexpr int kPolyPeriod = 8;                  // of every 8 score pairs ...
+constexpr int kPolyCount = 3;                   // ... this many use ex2_poly2
 
 enum Bar : uint32_t {
     kQFull = 0,
     kQEmpty,
-    kKFull,                          // + stage
-    kKEmpty = kKFull + kKStages,     // + stage
-    kVFull = kKEmpty + kKStages,     // + stage
-    kVEmpty = kVFull + kVStages,     // + stage
-    kSFull = kVEmpty + kVStages,     // + q tile
-    kPFull = kSFull + 2,             // + q tile
-    kODone = kPFull + 2,             // + q tile
-    kOFree = kODone + 2,             // + q tile
-    kDrain = kOFree + 2,
+    kFull,                           // + ring slot: sub-tile landed
+    kEmpty = kFull + kSlots,         // + ring slot: sub-tile consumed
+    kSFull = kEmpty + kSlots,        // scores of a step computed
+    kSFree,                          // scores loaded by every softmax thread
+    kPFull,                          // probabilities of a step stored
+    kPFree,                          // PV of a step finished (P and O may be touched)
+    kOFree,                          // epilogue read O
+    kXchg,                           // + (warp % 4): the four warps sharing 32 rows exchanged data
+    kDrain = kXchg + 4,
     kNumBars,
 };
 constexpr uint32_t kSlotTmem = kNumBars * 8;
@@ -115,6 +124,21 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
     return *reinterpret_cast<float2*>(&d);
 }
 
+// Two exp2 on the FMA pipe (ex2_poly in packed f32x2 form): magic-number rounding, degree-3
+// polynomial on [-0.5, 0.5], exponent-field add.
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+    x = make_float2(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f));
+    const float2 t = fadd2(x, make_float2(kMagic, kMagic));
+    const float2 n = fadd2(t, make_float2(-kMagic, -kMagic));
+    const float2 f = ffma2(n, make_float2(-1.0f, -1.0f), x);
+    float2 q = ffma2(make_float2(0.055171654f, 0.055171654f), f, make_float2(0.24261114f, 0.24261114f));
+    q = ffma2(q, f, make_float2(0.69326097f, 0.69326097f));
+    q = ffma2(q, f, make_float2(0.99992806f, 0.99992806f));
+    return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                       __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
 attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -134,30 +158,26 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     if (threadIdx.x == 0) {
         mbar_init(bar(kQFull), 1);
         mbar_init(bar(kQEmpty), 1);
-        for (int s = 0; s < kKStages; ++s) {
-            mbar_init(bar(kKFull + s), 1);
-            mbar_init(bar(kKEmpty + s), 1);
+        for (int s = 0; s < kSlots; ++s) {
+            mbar_init(bar(kFull + s), 1);
+            mbar_init(bar(kEmpty + s), 1);
         }
-        for (int s = 0; s < kVStages; ++s) {
-            mbar_init(bar(kVFull + s), 1);
-            mbar_init(bar(kVEmpty + s), 1);
-        }
-        for (int t = 0; t < 2; ++t) {
-            mbar_init(bar(kSFull + t), 1);
-            mbar_init(bar(kPFull + t), 128);
-            mbar_init(bar(kODone + t), 1);
-            mbar_init(bar(kOFree + t), 128);
-        }
+        mbar_init(bar(kSFull), 1);
+        mbar_init(bar(kSFree), kSoftmaxThreads);
+        mbar_init(bar(kPFull), kSoftmaxThreads);
+        mbar_init(bar(kPFree), 1);
+        mbar_init(bar(kOFree), kSoftmaxThreads);
+        for (int q = 0; q < 4; ++q) mbar_init(bar(kXchg + q), kSoftmaxThreads / 4);
         mbar_init(bar(kDrain), 1);
         *abort = 0;
         fence_mbar_init();
     }
-    if (warp == 0 && lane == 0) {
+    if (warp == kProducerWarp && lane == 0) {
         prefetch_tmap(&tmQ);
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
     }
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         tmem_alloc(smem_u32((const void*)tmem_slot), kTmemCols);
         tmem_relinquish();
     }
@@ -168,135 +188,110 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     const uint32_t tmem = *tmem_slot;
 
     const int32_t M = *p.count;
-    const int32_t n_units_q = (M + kUnitRows - 1) / kUnitRows;
-    const int32_t n_units = n_units_q * p.n_heads;
-    const int32_t n_kv = (p.n_tokens + kBN - 1) / kBN;
+    const int32_t n_qt = (M + kBM - 1) / kBM;
+    const int32_t n_units = n_qt * p.n_heads;
+    const int32_t n_steps = (p.n_tokens + kStepN - 1) / kStepN;
 
-    if (warp == 0) {
+    if (warp == kProducerWarp) {
         if (lane == 0) {
             // ---------------- TMA producer ----------------
-            uint32_t k_it = 0, v_it = 0, q_it = 0;
+            // Ring order = tensor-core consumption order of one unit:
+            //   K(0) K(1) | K(2j) K(2j+1) V(2j-2) V(2j-1) for j = 1..n-1 | V(2n-2) V(2n-1)
+            uint32_t it = 0, q_it = 0;
             bool ok = true;
+            auto load = [&](const CUtensorMap* tm, int32_t head, int32_t key0) -> bool {
+                const uint32_t st = it % kSlots, use = it / kSlots;
+                if (use > 0 && !mbar_wait(bar(kEmpty + st), (use - 1) & 1, abort)) return false;
+                const uint32_t dst = base + kSmemRing + st * kTileBytes;
+                mbar_arrive_expect_tx(bar(kFull + st), kTileBytes);
+                tma_load_2d(dst, tm, bar(kFull + st), head * kD, key0);
+                tma_load_2d(dst + kHalfBytes, tm, bar(kFull + st), head * kD + 64, key0);
+                ++it;
+                return true;
+            };
             for (int32_t u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
-                const int32_t head = u / n_units_q, row0 = (u % n_units_q) * kUnitRows;
+                const int32_t head = u / n_qt, row0 = (u % n_qt) * kBM;
                 if (q_it > 0 && !mbar_wait(bar(kQEmpty), (q_it - 1) & 1, abort)) { ok = false; break; }
-                mbar_arrive_expect_tx(bar(kQFull), 2 * kTileBytes);
-#pragma unroll
-                for (int t = 0; t < 2; ++t) {
-                    const uint32_t sQ = base + kSmemQ + t * kTileBytes;
-                    tma_load_2d(sQ, &tmQ, bar(kQFull), head * kD, row0 + t * kBM);
-                    tma_load_2d(sQ + kHalfBytes, &tmQ, bar(kQFull), head * kD + 64, row0 + t * kBM);
-                }
+                mbar_arrive_expect_tx(bar(kQFull), kTileBytes);
+                tma_load_2d(base + kSmemQ, &tmQ, bar(kQFull), head * kD, row0);
+                tma_load_2d(base + kSmemQ + kHalfBytes, &tmQ, bar(kQFull), head * kD + 64, row0);
                 ++q_it;
-                for (int32_t j = 0; ok && j < n_kv; ++j) {
-                    {
-                        const uint32_t st = k_it % kKStages, use = k_it / kKStages;
-                        if (use > 0 && !mbar_wait(bar(kKEmpty + st), (use - 1) & 1, abort)) { ok = false; break; }
-                        const uint32_t sK = base + kSmemK + st * kTileBytes;
-                        mbar_arrive_expect_tx(bar(kKFull + st), kTileBytes);
-                        tma_load_2d(sK, &tmK, bar(kKFull + st), head * kD, j * kBN);
-                        tma_load_2d(sK + kHalfBytes, &tmK, bar(kKFull + st), head * kD + 64, j * kBN);
-                        ++k_it;
-                    }
-                    {
-                        const uint32_t st = v_it % kVStages, use = v_it / kVStages;
-                        if (use > 0 && !mbar_wait(bar(kVEmpty + st), (use - 1) & 1, abort)) { ok = false; break; }
-                        const uint32_t sV = base + kSmemV + st * kTileBytes;
-                        mbar_arrive_expect_tx(bar(kVFull + st), kTileBytes);
-                        tma_load_2d(sV, &tmV, bar(kVFull + st), head * kD, j * kBN);
-                        tma_load_2d(sV + kHalfBytes, &tmV, bar(kVFull + st), head * kD + 64, j * kBN);
-                        ++v_it;
-                    }
-                }
+                ok = load(&tmK, head, 0) && load(&tmK, head, kSubN);
+                for (int32_t j = 1; ok && j < n_steps; ++j)
+                    ok = load(&tmK, head, j * kStepN) && load(&tmK, head, j * kStepN + kSubN) &&
+                         load(&tmV, head, (j - 1) * kStepN) && load(&tmV, head, (j - 1) * kStepN + kSubN);
+                ok = ok && load(&tmV, head, (n_steps - 1) * kStepN) &&
+                     load(&tmV, head, (n_steps - 1) * kStepN + kSubN);
             }
             if (*abort) {
                 if (q_it > 0) mbar_wait_drain(bar(kQFull), (q_it - 1) & 1);
-                for (uint32_t t = (k_it > kKStages ? k_it - kKStages : 0); t < k_it; ++t)
-                    mbar_wait_drain(bar(kKFull + t % kKStages), (t / kKStages) & 1);
-                for (uint32_t t = (v_it > kVStages ? v_it - kVStages : 0); t < v_it; ++t)
-                    mbar_wait_drain(bar(kVFull + t % kVStages), (t / kVStages) & 1);
+                for (uint32_t t = (it > kSlots ? it - kSlots : 0); t < it; ++t)
+                    mbar_wait_drain(bar(kFull + t % kSlots), (t / kSlots) & 1);
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == kMmaWarp) {
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
             constexpr uint32_t fmt = StoreT<T>::kUmmaFormat;
-            constexpr uint32_t idesc_qk = make_idesc_f16(fmt, 0, kBM, kBN);
+            constexpr uint32_t idesc_qk = make_idesc_f16(fmt, 0, kBM, kSubN);
             constexpr uint32_t idesc_pv = make_idesc_f16(fmt, 1, kBM, kD);
-            uint32_t k_it = 0, v_it = 0, q_it = 0, p_it = 0, units_done = 0;
+            uint32_t it = 0, q_it = 0, g = 0, units_done = 0;
             bool ok = true, issued = false;
-            // S_t = Q_t K^T (A, B from shared memory, both K-major)
-            auto qk = [&](int t, uint32_t st) {
-                const uint32_t sQ = base + kSmemQ + t * kTileBytes;
-                const uint32_t sK = base + kSmemK + st * kTileBytes;
-#pragma unroll
-                for (int k = 0; k < kD / 16; ++k) {
-                    const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32u;
-                    umma_ss(tmem + t * 128u, smem_desc_sw128(sQ + off, 16, 1024),
-                            smem_desc_sw128(sK + off, 16, 1024), idesc_qk, k > 0 ? 1u : 0u);
-                }
-                umma_commit(bar(kSFull + t));
+            // next ring sub-tile (in the producer's order); returns its shared-memory address or 0
+            auto next_tile = [&]() -> uint32_t {
+                const uint32_t st = it % kSlots;
+                if (!mbar_wait(bar(kFull + st), (it / kSlots) & 1, abort)) return 0;
+                tc_fence_after();
+                return base + kSmemRing + st * kTileBytes;
             };
-            // O_t (+)= P_t V (A = P from tensor memory, B = V from shared memory, MN-major)
-            auto pv = [&](int t, int32_t jj, uint32_t st) {
-                const uint32_t sV = base + kSmemV + st * kTileBytes;
+            auto release_tile = [&]() {
+                umma_commit(bar(kEmpty + it % kSlots));
+                ++it;
+            };
+            // O (+)= P V for one step (A = P from tensor memory, B = V sub-tiles, MN-major)
+            auto pv = [&](int32_t jj, uint32_t gg) -> bool {
+                if (!mbar_wait(bar(kPFull), gg & 1, abort)) return false;
+                if (jj == 0 && units_done > 0 && !mbar_wait(bar(kOFree), (units_done - 1) & 1, abort))
+                    return false;
+                tc_fence_after();
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t sV = next_tile();
+                    if (!sV) return false;
 #pragma unroll
-                for (int k = 0; k < kBN / 16; ++k) {
-                    const uint64_t bdesc = smem_desc_sw128(sV + k * 2048u, kHalfBytes, 1024);
-                    umma_ts(tmem + 256u + t * 128u, tmem + t * 128u + k * 8u, bdesc, idesc_pv,
-                            (jj > 0 || k > 0) ? 1u : 0u);
+                    for (int k = 0; k < kSubN / 16; ++k) {
+                        const uint64_t bdesc = smem_desc_sw128(sV + k * 2048u, kHalfBytes, 1024);
+                        umma_ts(tmem + kColO, tmem + kColP + (h * 8 + k) * 8u, bdesc, idesc_pv,
+                                (jj > 0 || h > 0 || k > 0) ? 1u : 0u);
+                    }
+                    release_tile();
                 }
+                umma_commit(bar(kPFree));
+                return true;
             };
             for (int32_t u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
                 if (!mbar_wait(bar(kQFull), q_it & 1, abort)) { ok = false; break; }
                 ++q_it;
-                {   // prologue: S0(0), S1(0)
-                    const uint32_t st = k_it % kKStages;
-                    if (!mbar_wait(bar(kKFull + st), (k_it / kKStages) & 1, abort)) { ok = false; break; }
-                    tc_fence_after();
-                    issued = true;
-                    qk(0, st);
-                    qk(1, st);
-                    umma_commit(bar(kKEmpty + st));
-                    if (n_kv == 1) umma_commit(bar(kQEmpty));
-                    ++k_it;
-                }
-                for (int32_t j = 0; j < n_kv; ++j) {
-                    const uint32_t vs = v_it % kVStages;
-                    // O0 += P0(j) V(j)
-                    if (!mbar_wait(bar(kPFull + 0), p_it & 1, abort)) { ok = false; break; }
-                    if (!mbar_wait(bar(kVFull + vs), (v_it / kVStages) & 1, abort)) { ok = false; break; }
-                    if (j == 0 && units_done > 0 &&
-                        !mbar_wait(bar(kOFree + 0), (units_done - 1) & 1, abort)) { ok = false; break; }
-                    tc_fence_after();
-                    pv(0, j, vs);
-                    if (j == n_kv - 1) umma_commit(bar(kODone + 0));
-                    // S0(j+1)
-                    uint32_t ks = 0;
-                    if (j + 1 < n_kv) {
-                        ks = k_it % kKStages;
-                        if (!mbar_wait(bar(kKFull + ks), (k_it / kKStages) & 1, abort)) { ok = false; break; }
-                        tc_fence_after();
-                        qk(0, ks);
+                for (int32_t j = 0; j < n_steps; ++j, ++g) {
+                    // S(j) = Q K(2j..2j+1)^T once every softmax thread has loaded S(j-1)
+                    if (g > 0 && !mbar_wait(bar(kSFree), (g - 1) & 1, abort)) { ok = false; break; }
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t sK = next_tile();
+                        if (!sK) { ok = false; break; }
+                        issued = true;
+#pragma unroll
+                        for (int k = 0; k < kD / 16; ++k) {
+                            const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32u;
+                            umma_ss(tmem + kColS + h * kSubN, smem_desc_sw128(base + kSmemQ + off, 16, 1024),
+                                    smem_desc_sw128(sK + off, 16, 1024), idesc_qk, k > 0 ? 1u : 0u);
+                        }
+                        release_tile();
                     }
-                    // O1 += P1(j) V(j)
-                    if (!mbar_wait(bar(kPFull + 1), p_it & 1, abort)) { ok = false; break; }
-                    if (j == 0 && units_done > 0 &&
-                        !mbar_wait(bar(kOFree + 1), (units_done - 1) & 1, abort)) { ok = false; break; }
-                    tc_fence_after();
-                    pv(1, j, vs);
-                    umma_commit(bar(kVEmpty + vs));
-                    ++v_it;
-                    if (j == n_kv - 1) umma_commit(bar(kODone + 1));
-                    ++p_it;
-                    // S1(j+1)
-                    if (j + 1 < n_kv) {
-                        qk(1, ks);
-                        umma_commit(bar(kKEmpty + ks));
-                        if (j + 1 == n_kv - 1) umma_commit(bar(kQEmpty));
-                        ++k_it;
-                    }
+                    if (!ok) break;
+                    umma_commit(bar(kSFull));
+                    if (j == n_steps - 1) umma_commit(bar(kQEmpty));
+                    if (j > 0 && !pv(j - 1, g - 1)) { ok = false; break; }
                 }
+                if (!ok || !pv(n_steps - 1, g - 1)) { ok = false; break; }
                 ++units_done;
             }
             if (*abort && issued) {
@@ -304,106 +299,136 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 mbar_wait_drain(bar(kDrain), 0);
             }
         }
-    } else if (warp >= 4) {
-        // ---------------- softmax / correction / epilogue (one warpgroup per Q tile) ----------------
+    } else {
+        // ---------------- softmax / correction / epilogue: 4 warpgroups ----------------
         // Waits are warp-uniform (every lane polls, then __all_sync) so that the .sync.aligned
         // tensor-memory accesses below always run on a converged warp, also when a wait gives up.
         auto wwait = [&](uint32_t b_, uint32_t par_) -> bool {
             return __all_sync(0xffffffffu, mbar_wait(b_, par_, abort));
         };
-        const int t = (warp - 4) >> 2;                            // Q tile of this warpgroup
-        const int r = (threadIdx.x - 128) & 127;                  // row in the tile = TMEM lane
+        const int wg = warp >> 2;                                 // 0..3
+        const int r = ((warp & 3) << 5) | (int)lane;              // row in the tile = TMEM lane
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t tS = tmem + lane_off + t * 128u;
-        const uint32_t tO = tmem + lane_off + 256u + t * 128u;
+        const uint32_t tS = tmem + lane_off + kColS + wg * 64u;
+        const uint32_t tP = tmem + lane_off + kColP + wg * 32u;
+        const uint32_t tO = tmem + lane_off + kColO + wg * 32u;
+        float* xch = reinterpret_cast<float*>(gbase + kSmemX);    // [buf][wg][row]
         const float c = p.scale_log2;
         const float2 c2 = make_float2(c, c);
         T* __restrict__ out = static_cast<T*>(p.out);
-        uint32_t s_it = 0, units_done = 0;
-        for (int32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
-            const int32_t head = u / n_units_q, row0 = (u % n_units_q) * kUnitRows + t * kBM;
-            float m_run = -INFINITY, l_run = 0.f;
-            bool ok = true;
-            for (int32_t j = 0; j < n_kv; ++j, ++s_it) {
-                if (!wwait(bar(kSFull + t), s_it & 1)) { ok = false; break; }
-                tc_fence_after();
-                uint32_t s[128];
-                FXR_TMEM_LD128(tS, s);
-                const int32_t kv_left = p.n_tokens - j * kBN;
-                if (kv_left < kBN) {
+        uint32_t s_it = 0, x_it = 0, units_done = 0;
+        bool ok = true;
+        // row data exchange among the four warps (one per warpgroup, same sub-partition) that hold
+        // the same 32 rows; returns the four values of this row
+        const uint32_t xbar = bar(kXchg + (warp & 3));
+        auto exchange = [&](float v, float* o4) -> bool {
+            float* xb = xch + (x_it & 1) * 512;
+            xb[wg * 128 + r] = v;
+            mbar_arrive(xbar);
+            if (!wwait(xbar, x_it & 1)) return false;
+            ++x_it;
 #pragma unroll
-                    for (int cc = 0; cc < 128; ++cc)
+            for (int k = 0; k < 4; ++k) o4[k] = xb[k * 128 + r];
+            return true;
+        };
+        for (int32_t u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+            const int32_t head = u / n_qt, row0 = (u % n_qt) * kBM;
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int32_t j = 0; j < n_steps; ++j, ++s_it) {
+                if (!wwait(bar(kSFull), s_it & 1)) { ok = false; break; }
+                tc_fence_after();
+                uint32_t s[64];
+                FXR_TMEM_LD64(tS, s);
+                tc_fence_before();
+                mbar_arrive(bar(kSFree));                         // the next QK may overwrite S
+                const int32_t kv_left = p.n_tokens - j * kStepN - wg * 64;
+                if (kv_left < 64) {
+#pragma unroll
+                    for (int cc = 0; cc < 64; ++cc)
                         if (cc >= kv_left) s[cc] = __float_as_uint(-INFINITY);
                 }
-                // row maximum: 8 independent chains of 3-input max
                 float mp[8];
 #pragma unroll
                 for (int k = 0; k < 8; ++k) mp[k] = fmaxf(__uint_as_float(s[2 * k]), __uint_as_float(s[2 * k + 1]));
 #pragma unroll
-                for (int i = 1; i < 8; ++i)
+                for (int i = 1; i < 4; ++i)
 #pragma unroll
                     for (int k = 0; k < 8; ++k)
                         mp[k] = max3f(mp[k], __uint_as_float(s[16 * i + 2 * k]), __uint_as_float(s[16 * i + 2 * k + 1]));
-                const float mx = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7])) * c;
+                float pm4[4];
+                if (!exchange(max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7])), pm4)) {
+                    ok = false;
+                    break;
+                }
+                const float mx = fmaxf(fmaxf(pm4[0], pm4[1]), fmaxf(pm4[2], pm4[3])) * c;
+                float alpha = 1.f;
+                bool rescale = false;
                 if (j == 0) {
                     m_run = mx;
                 } else if (__any_sync(0xffffffffu, mx > m_run + kRescaleThreshold)) {
-                    // S_t(j) is complete, hence so is PV_t(j-1): O_t may be rewritten now.
                     const float m_new = fmaxf(m_run, mx);
-                    const float alpha = ex2_approx(m_run - m_new);
+                    alpha = ex2_approx(m_run - m_new);
                     l_run *= alpha;
                     m_run = m_new;
-#pragma unroll
-                    for (int h2 = 0; h2 < 4; ++h2) {
-                        uint32_t o[32];
-                        FXR_TMEM_LD32(tO + h2 * 32u, o);
-#pragma unroll
-                        for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-                        FXR_TMEM_ST32(tO + h2 * 32u, o);
-                    }
+                    rescale = true;
                 }
                 const float2 nm2 = make_float2(-m_run, -m_run);
                 float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                                  make_float2(0.f, 0.f)};
-                // P overwrites the score registers pairwise (pk[k] from s[2k], s[2k+1]); one
-                // 64-column store and one store wait per tile.
+                // P overwrites the score registers pairwise (pk[k] from s[2k], s[2k+1]).
                 uint32_t* pk = s;
 #pragma unroll
-                for (int k = 0; k < 64; ++k) {
+                for (int k = 0; k < 32; ++k) {
                     const float2 x = ffma2(make_float2(__uint_as_float(s[2 * k]), __uint_as_float(s[2 * k + 1])),
                                            c2, nm2);
                     float2 e;
                     if ((k % kPolyPeriod) < kPolyCount) {
-                        e = make_float2(ex2_poly(x.x), ex2_poly(x.y));
+                        e = ex2_poly2(x);
                     } else {
                         e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
                     }
                     acc[k & 3] = fadd2(acc[k & 3], e);
                     pk[k] = StoreT<T>::pack2(e.x, e.y);
                 }
-                FXR_TMEM_ST64(tS, pk);
                 const float2 a01 = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
                 l_run += a01.x + a01.y;
+                // P and O may be touched once the previous step's PV has finished
+                if (s_it > 0 && !wwait(bar(kPFree), (s_it - 1) & 1)) { ok = false; break; }
+                tc_fence_after();
+                if (rescale) {
+#pragma unroll 1
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        uint32_t o[16];
+                        FXR_TMEM_LD16(tO + h2 * 16u, o);
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+                        FXR_TMEM_ST16(tO + h2 * 16u, o);
+                    }
+                }
+                FXR_TMEM_ST32(tP, pk);
                 tc_fence_before();
-                mbar_arrive(bar(kPFull + t));
+                mbar_arrive(bar(kPFull));
             }
             if (!ok) break;
-            // epilogue: O_t is final once its last PV completed
-            if (!wwait(bar(kODone + t), units_done & 1)) break;
+            // epilogue: O is final once the last PV finished
+            if (!wwait(bar(kPFree), (s_it - 1) & 1)) { ok = false; break; }
             tc_fence_after();
-            uint32_t o[128];
-            FXR_TMEM_LD128(tO, o);
+            uint32_t o[32];
+            FXR_TMEM_LD32(tO, o);
             tc_fence_before();
-            mbar_arrive(bar(kOFree + t));
+            mbar_arrive(bar(kOFree));
             ++units_done;
+            float l4[4];
+            if (!exchange(l_run, l4)) { ok = false; break; }
+            const float l_tot = (l4[0] + l4[1]) + (l4[2] + l4[3]);
             const int32_t m = row0 + r;
             if (m < M) {
                 const int32_t i = p.idx[m];
                 if (i >= 0 && i < p.n_tokens) {
-                    const float inv = 1.0f / l_run;
-                    uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)i * p.ld_out + (int64_t)head * kD);
+                    const float inv = 1.0f / l_tot;
+                    uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)i * p.ld_out + (int64_t)head * kD + wg * 32);
 #pragma unroll
-                    for (int k = 0; k < 16; ++k) {
+                    for (int k = 0; k < 4; ++k) {
                         uint4 v;
                         v.x = StoreT<T>::pack2(__uint_as_float(o[8 * k + 0]) * inv, __uint_as_float(o[8 * k + 1]) * inv);
                         v.y = StoreT<T>::pack2(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv);
@@ -421,7 +446,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     __syncwarp();  // role warps ran their loops on one lane; reconverge before the CTA barrier
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }

@@ -222,7 +222,7 @@ int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
     p.n_heads = d->n_heads;
     const float scale = d->softmax_scale > 0.f ? d->softmax_scale : 1.0f / std::sqrt((float)d->head_dim);
     p.scale_log2 = scale * 1.4426950408889634f;
-    const int64_t max_tiles = (N + fxr::attn::kUnitRows - 1) / fxr::attn::kUnitRows * d->n_heads;
+    const int64_t max_tiles = (N + fxr::attn::kBM - 1) / fxr::attn::kBM * d->n_heads;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_tiles, sm_count()));
     fxr::attn::attention_kernel<T><<<grid, fxr::attn::kThreads, fxr::attn::kSmemBytes, stream>>>(
         tq, tk, tv, p);

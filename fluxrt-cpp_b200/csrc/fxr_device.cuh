@@ -273,6 +273,27 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(uint32_t ab_format, uint32
           "r"(r[62]), "r"(r[63])                                                                   \
         : "memory")
 
+// 32 lanes x 32-bit, 16 consecutive columns per thread: load + wait, and store + wait.
+#define FXR_TMEM_LD16(taddr, r)                                                                    \
+    asm volatile(                                                                                  \
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "                                                  \
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"                      \
+        "tcgen05.wait::ld.sync.aligned;"                                                           \
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),      \
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),  \
+          "=r"(r[14]), "=r"(r[15])                                                                 \
+        : "r"(taddr)                                                                               \
+        : "memory")
+#define FXR_TMEM_ST16(taddr, r)                                                                    \
+    asm volatile(                                                                                  \
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "                                            \
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n\t"                            \
+        "tcgen05.wait::st.sync.aligned;"                                                           \
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),            \
+          "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]),          \
+          "r"(r[13]), "r"(r[14]), "r"(r[15])                                                       \
+        : "memory")
+
 // 32 lanes x 32-bit, 32 consecutive columns per thread, load + wait in one statement.
 #define FXR_TMEM_LD32(taddr, r)                                                                    \
     asm volatile(                                                                                  \
