@@ -8,8 +8,8 @@
 //   warps 0-15  softmax: warpgroup g = warp/4 owns score columns [64g, 64g+64) of each step for
 //               all 128 rows (one thread per row = TMEM lane), and O columns [32g, 32g+32) for the
 //               correction and the epilogue
-//   warp 16     TMA producer: Q tile, a 3-slot K ring and a 2-slot V ring of 128-key sub-tiles
-//               (128-byte swizzle)
+//   warp 16     TMA producer: Q tile and a 5-slot ring of 128-key K and V sub-tiles filled in
+//               the tensor core's consumption order (128-byte swizzle)
 //   warp 17     TMEM allocator and the single MMA-issuing thread
 // Tensor memory (512 columns): S [0,256) fp32 scores of one step, P [256,384) the 16-bit
 // probabilities of the step (pairs packed per column), O [384,512) fp32 output accumulator.
@@ -22,11 +22,12 @@
 // from tensor memory.
 // Softmax in the exp2 domain with lazy rescaling: O and the running sum are rescaled only when a
 // row maximum grows by more than 2^8, so p <= 256 between rescales and O / l is exact. The four
-// warpgroups combine their partial row maxima through shared memory behind an mbarrier each step
-// (bounded waits, no named barrier that could outlive an aborted partner), and their partial row
-// sums once in the epilogue. The special-function unit computes 16 exp2 per clock per SM, the rate
-// at which the tensor core consumes them (4*128 FLOP per score), so a quarter of the
-// exponentials run as a polynomial on the FMA pipe (ex2_poly).
+// warps that hold the same 32 rows (one per warpgroup, same SM sub-partition) combine their
+// partial row maxima through shared memory behind an mbarrier each step (bounded waits, no named
+// barrier that could outlive an aborted partner), and their partial row sums once in the epilogue.
+// The special-function unit computes 16 exp2 per clock per SM, the rate at which the tensor core
+// consumes them (4*128 FLOP per score), so a quarter of the exponentials run as a polynomial on
+// the FMA pipe (ex2_poly2).
 // The reference's scatter is fused: the epilogue stores row m straight to out[idx[m], h*128 ...].
 // Every mbarrier wait is bounded (2 s); on timeout the kernel sets the device error word, drains
 // its outstanding copies and MMAs, frees its tensor memory and returns.
@@ -62,7 +63,7 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
 constexpr float kRescaleThreshold = 8.0f;       // log2 units
 constexpr int kPolyPeriod = 8;                  // of every 8 score pairs ...
-constexpr int kPolyCount = 3;                   // ... this many use ex2_poly2
+constexpr int kPolyCount = 2;                   // ... this many use ex2_poly2
 
 enum Bar : uint32_t {
     kQFull = 0,
