@@ -17,6 +17,12 @@
 #include "fxr_device.cuh"
 #include "fxr_mem_kernels.cuh"
 
+// Built-in frame scratch of fxr_frame_forward_noalloc (see that function). 96 MiB holds the
+// workspace of a 1024x1024 frame (4608 tokens, 24 heads, 16-bit storage: ~85 MB). Every GPU that
+// loads this library keeps this array for the life of the process.
+constexpr size_t kNoAllocScratchBytes = size_t(96) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
 namespace {
 
 thread_local std::string t_last_error;
@@ -301,6 +307,47 @@ int32_t fxr_check_device_error(void* stream, uint32_t* word_out) {
 size_t fxr_workspace_size(const fxr_frame_desc* desc) {
     if (!desc || dtype_bytes(desc->dtype) == 0 || desc->n_heads <= 0 || desc->head_dim <= 0) return 0;
     return carve(desc, nullptr).total;
+}
+
+// Device address of g_noalloc_scratch on the current device. The first call on a device resolves
+// it with cudaGetSymbolAddress (with that device current); later calls reuse the stored address.
+// The host-side name g_noalloc_scratch is only a stand-in and must never be handed to a kernel.
+static int32_t noalloc_scratch(void** out) {
+    static std::mutex mu;
+    static void* addr[kMaxDevices] = {nullptr};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) return fail(FXR_ERR_UNSUPPORTED, "device ordinal %d too large", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(frame scratch)");
+        if (!p) return fail(FXR_ERR_CUDA, "cudaGetSymbolAddress returned a null frame scratch");
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return FXR_OK;
+}
+
+int32_t fxr_frame_forward_noalloc(const fxr_frame_desc* desc, const void* q, const void* k,
+                                  const void* v, int32_t* mask, const uint8_t* valid,
+                                  const int32_t* pos, const float* norm_q, const float* norm_k,
+                                  void* cache_k, void* cache_v, void* out, void* stream) {
+    int32_t st = check_desc(desc, true);
+    if (st != FXR_OK) return st;
+    if (desc->n_tokens == 0) return FXR_OK;
+    const size_t need = carve(desc, nullptr).total;
+    if (need > kNoAllocScratchBytes)
+        return fail(FXR_ERR_WORKSPACE,
+                    "frame needs %zu bytes of scratch but the built-in scratch of "
+                    "fxr_frame_forward_noalloc holds %zu; use fxr_frame_forward with a caller workspace",
+                    need, kNoAllocScratchBytes);
+    void* scratch = nullptr;
+    if ((st = noalloc_scratch(&scratch)) != FXR_OK) return st;
+    return fxr_frame_forward(desc, q, k, v, mask, valid, pos, norm_q, norm_k, cache_k, cache_v, out,
+                             scratch, kNoAllocScratchBytes, stream);
 }
 
 int32_t fxr_workspace_views(const fxr_frame_desc* desc, void* workspace, int32_t** idx,

@@ -178,6 +178,26 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc,
                           void* cache_k, void* cache_v, void* out,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/* fxr_frame_forward without a workspace argument, for callers that cannot allocate device memory
+ * when they run a frame: for example a plugin enqueue inside an inference engine that owns every
+ * device allocation, or a latency-critical loop that must not risk the device-wide
+ * synchronisation an allocation can cause. This entry point has no counterpart in the reference.
+ *   - Scratch: a fixed 96 MiB array inside this library (every GPU that loads the library holds it
+ *     until the process exits). Frames whose fxr_workspace_size() exceeds 96 MiB are rejected with
+ *     FXR_ERR_WORKSPACE; a 1024x1024 frame (4608 tokens, 24 heads, bf16/fp16) needs about 85 MB.
+ *   - No cudaMalloc, cudaFree or other allocating call is made. The first call on a device looks up
+ *     the scratch address for that device (once, with that device current); make that first call
+ *     before any stream capture.
+ *   - Every call on a device shares the same scratch, and each frame overwrites it completely
+ *     before reading it (nothing has to start at zero). Calls whose work overlaps on the GPU (two
+ *     streams, or two host threads) race on it: serialise them on one stream.
+ * Arguments, layouts, results and errors are those of fxr_frame_forward. */
+int32_t fxr_frame_forward_noalloc(const fxr_frame_desc* desc,
+                                  const void* q, const void* k, const void* v,
+                                  int32_t* mask, const uint8_t* valid, const int32_t* pos,
+                                  const float* norm_q, const float* norm_k,
+                                  void* cache_k, void* cache_v, void* out, void* stream);
+
 /* Device pointers into the workspace (for callers that want idx / count / compact Q). */
 int32_t fxr_workspace_views(const fxr_frame_desc* desc, void* workspace, int32_t** idx,
                             int32_t** count, void** qc, int64_t* ld_qc, void** save);
