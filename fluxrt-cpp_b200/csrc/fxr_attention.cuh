@@ -188,6 +188,10 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // Everything above overlapped the previous kernel (programmatic dependent launch); the compact
+    // queries, indices and count it wrote are read below.
+    pdl_launch_dependents();
+    pdl_wait();
     const int32_t M = *p.count;
     const int32_t n_qt = (M + kBM - 1) / kBM;
     const int32_t n_units = n_qt * p.n_heads;

@@ -50,6 +50,25 @@ int32_t cuda_status(cudaError_t e, const char* what) {
 
 constexpr int kMaxDevices = 64;
 
+// Launch with programmatic stream serialisation: the kernel may begin (prologue only, until its
+// griddepcontrol.wait) while the previous kernel on the stream finishes. Used for the four frame
+// kernels, each of which waits before touching data shared with its predecessor.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 int sm_count() {
     static int counts[kMaxDevices] = {0};
     int dev = 0;
@@ -230,9 +249,9 @@ int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
     p.scale_log2 = scale * 1.4426950408889634f;
     const int64_t max_tiles = (N + fxr::attn::kBM - 1) / fxr::attn::kBM * d->n_heads;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_tiles, sm_count()));
-    fxr::attn::attention_kernel<T><<<grid, fxr::attn::kThreads, fxr::attn::kSmemBytes, stream>>>(
-        tq, tk, tv, p);
-    FXR_CHECK_LAUNCH("attention_kernel launch");
+    cudaError_t e = launch_pdl(fxr::attn::attention_kernel<T>, dim3(grid), dim3(fxr::attn::kThreads),
+                               fxr::attn::kSmemBytes, stream, tq, tk, tv, p);
+    if (e != cudaSuccess) return cuda_status(e, "attention_kernel launch");
     return FXR_OK;
 }
 
@@ -266,8 +285,9 @@ int32_t launch_gather(const fxr_frame_desc* d, const void* q, const void* k, con
     const int64_t groups = (d->n_heads + fxr::kGatherHeadsPerItem - 1) / fxr::kGatherHeadsPerItem;
     const int64_t need = ((int64_t)d->n_tokens * groups + 7) / 8;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, (int64_t)sm_count() * fxr::kGatherMinBlocks));
-    fxr::gather_norm_rope_kernel<T><<<grid, fxr::kGatherThreads, 0, stream>>>(a);
-    FXR_CHECK_LAUNCH("gather_norm_rope_kernel launch");
+    cudaError_t e = launch_pdl(fxr::gather_norm_rope_kernel<T>, dim3(grid), dim3(fxr::kGatherThreads), 0,
+                               stream, a);
+    if (e != cudaSuccess) return cuda_status(e, "gather_norm_rope_kernel launch");
     return FXR_OK;
 }
 
@@ -366,9 +386,9 @@ int32_t fxr_mask_compact(int32_t* mask, const uint8_t* valid, int32_t n_tokens, 
                          int32_t* count, void* stream) {
     if (n_tokens < 0) return fail(FXR_ERR_INVALID, "n_tokens < 0");
     if (!count || (n_tokens > 0 && (!mask || !idx))) return fail(FXR_ERR_INVALID, "null pointer");
-    fxr::compact_kernel<<<1, fxr::kCompactThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        mask, valid, n_tokens, idx, count);
-    FXR_CHECK_LAUNCH("compact_kernel launch");
+    cudaError_t e = launch_pdl(fxr::compact_kernel, dim3(1), dim3(fxr::kCompactThreads), 0,
+                               static_cast<cudaStream_t>(stream), mask, valid, n_tokens, idx, count);
+    if (e != cudaSuccess) return cuda_status(e, "compact_kernel launch");
     return FXR_OK;
 }
 
@@ -432,11 +452,12 @@ int32_t fxr_restore_rows(const fxr_frame_desc* desc, const int32_t* mask, const 
     if (!aligned16(save) || !aligned16(cache_k) || !aligned16(cache_v))
         return fail(FXR_ERR_INVALID, "save/cache must be 16-byte aligned");
     const int64_t row_bytes = (int64_t)desc->n_heads * desc->head_dim * (int64_t)dtype_bytes(desc->dtype);
-    fxr::restore_rows_kernel<<<grid_rows(desc->n_tokens, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        mask, idx, count, static_cast<const uint4*>(save), static_cast<char*>(cache_k),
-        static_cast<char*>(cache_v), desc->ld_cache * (int64_t)dtype_bytes(desc->dtype),
-        (int32_t)(row_bytes / 16), desc->n_tokens);
-    FXR_CHECK_LAUNCH("restore_rows_kernel launch");
+    cudaError_t e = launch_pdl(fxr::restore_rows_kernel, dim3(grid_rows(desc->n_tokens, 8)), dim3(256), 0,
+                               static_cast<cudaStream_t>(stream), mask, idx, count,
+                               static_cast<const uint4*>(save), static_cast<char*>(cache_k),
+                               static_cast<char*>(cache_v), desc->ld_cache * (int64_t)dtype_bytes(desc->dtype),
+                               (int32_t)(row_bytes / 16), desc->n_tokens);
+    if (e != cudaSuccess) return cuda_status(e, "restore_rows_kernel launch");
     return FXR_OK;
 }
 

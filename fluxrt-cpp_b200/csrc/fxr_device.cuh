@@ -25,6 +25,14 @@ __device__ uint32_t g_error_word = 0;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s: far above any legitimate wait here
 constexpr uint32_t kWaitLimitPolls = 1u << 26;
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialisation may start
+// while its predecessor in the stream still runs; it must call pdl_wait() before it touches memory
+// the predecessor reads or writes. pdl_launch_dependents() lets the next kernel start early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -33,6 +33,8 @@ compact_kernel(int32_t* __restrict__ mask, const uint8_t* __restrict__ valid, in
     __shared__ int32_t chunk_tot;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t lt = (1u << lane) - 1u;
+    pdl_launch_dependents();
+    pdl_wait();  // the previous frame's kernels may still read mask / idx / count
     int32_t base = 0;
     for (int32_t c0 = 0; c0 < n; c0 += kCompactChunk) {
         uint32_t ballot[kCompactGroups];
@@ -172,6 +174,8 @@ __global__ void __launch_bounds__(kGatherThreads, kGatherMinBlocks)
 gather_norm_rope_kernel(const __grid_constant__ GatherArgs a) {
     const int lane = threadIdx.x & 31, half = lane >> 4, sub = lane & 15;
     const int warps_per_cta = kGatherThreads / 32;
+    pdl_launch_dependents();
+    pdl_wait();  // count / idx come from the compaction
     const int32_t M = *a.count;
     const int64_t C = (int64_t)a.n_heads * kHeadDim;
     const int groups = (a.n_heads + kGatherHeadsPerItem - 1) / kGatherHeadsPerItem;
@@ -269,6 +273,8 @@ restore_rows_kernel(const int32_t* __restrict__ mask, const int32_t* __restrict_
                     char* __restrict__ cache_k, char* __restrict__ cache_v, int64_t ld_cache_bytes,
                     int32_t row_vec, int32_t n_tokens) {
     const int lane = threadIdx.x & 31;
+    pdl_launch_dependents();
+    pdl_wait();  // the attention must have finished reading the cache rows
     const int32_t M = *count;
     for (int32_t m = blockIdx.x * 8 + (threadIdx.x >> 5); m < M; m += gridDim.x * 8) {
         const int32_t i = idx[m];
