@@ -452,7 +452,9 @@ int32_t fxr_restore_rows(const fxr_frame_desc* desc, const int32_t* mask, const 
     if (!aligned16(save) || !aligned16(cache_k) || !aligned16(cache_v))
         return fail(FXR_ERR_INVALID, "save/cache must be 16-byte aligned");
     const int64_t row_bytes = (int64_t)desc->n_heads * desc->head_dim * (int64_t)dtype_bytes(desc->dtype);
-    cudaError_t e = launch_pdl(fxr::restore_rows_kernel, dim3(grid_rows(desc->n_tokens, 8)), dim3(256), 0,
+    // one CTA per SM at most: usually no row has mask 1 and the kernel only scans M mask values
+    const int grid = std::min(grid_rows(desc->n_tokens, 8), sm_count());
+    cudaError_t e = launch_pdl(fxr::restore_rows_kernel, dim3(grid), dim3(256), 0,
                                static_cast<cudaStream_t>(stream), mask, idx, count,
                                static_cast<const uint4*>(save), static_cast<char*>(cache_k),
                                static_cast<char*>(cache_v), desc->ld_cache * (int64_t)dtype_bytes(desc->dtype),

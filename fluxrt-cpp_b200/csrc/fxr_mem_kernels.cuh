@@ -15,41 +15,43 @@
 namespace fxr {
 
 // ---------------------------------------------------------------------------------------------
-// Compaction. One CTA of 1024 threads walks the mask in chunks of 16384 tokens: each warp owns 16
-// consecutive 32-token groups of a chunk, takes one ballot per group, and a block scan of the 32
-// warp totals gives every warp its output offset. Output order is ascending token index.
-// Restates preprocess_mask_kernel (spatial_kv_cache.cu:12-19) and adds the compaction the
-// reference leaves to the host.
+// Compaction. One CTA of 8 warps walks the mask in chunks of up to 8 x 32 groups of 32 tokens;
+// each warp owns a contiguous run of groups (18 groups per warp for 4608 tokens), takes one ballot
+// per group, and a scan of the 8 warp totals gives every warp its output offset. Output order is
+// ascending token index. Restates preprocess_mask_kernel (spatial_kv_cache.cu:12-19) and adds the
+// compaction the reference leaves to the host.
 // ---------------------------------------------------------------------------------------------
-constexpr int kCompactThreads = 1024;
-constexpr int kCompactGroups = 16;
-constexpr int kCompactChunk = kCompactThreads * kCompactGroups;
+constexpr int kCompactThreads = 256;
+constexpr int kCompactWarps = kCompactThreads / 32;
+constexpr int kCompactGroups = 32;                              // per warp and chunk, at most
+constexpr int kCompactChunk = kCompactWarps * kCompactGroups * 32;
 
 __global__ void __launch_bounds__(kCompactThreads, 1)
 compact_kernel(int32_t* __restrict__ mask, const uint8_t* __restrict__ valid, int32_t n,
                int32_t* __restrict__ idx, int32_t* __restrict__ count) {
-    __shared__ int32_t warp_tot[32];
-    __shared__ int32_t warp_off[32];
-    __shared__ int32_t chunk_tot;
+    __shared__ int32_t warp_tot[kCompactWarps];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t lt = (1u << lane) - 1u;
     pdl_launch_dependents();
     pdl_wait();  // the previous frame's kernels may still read mask / idx / count
     int32_t base = 0;
     for (int32_t c0 = 0; c0 < n; c0 += kCompactChunk) {
+        const int32_t n_chunk = min(n - c0, kCompactChunk);
+        const int32_t groups = (n_chunk + 31) >> 5;
+        const int32_t gpw = (groups + kCompactWarps - 1) / kCompactWarps;   // groups per warp
+        const int32_t e0 = c0 + warp * gpw * 32 + lane;
         uint32_t ballot[kCompactGroups];
         int32_t mval[kCompactGroups];
-        const int32_t e0 = c0 + warp * (kCompactGroups * 32) + lane;
 #pragma unroll
         for (int g = 0; g < kCompactGroups; ++g) {
             const int32_t e = e0 + g * 32;
-            mval[g] = (e < n) ? mask[e] : 0;
+            mval[g] = (g < gpw && e < c0 + n_chunk) ? mask[e] : 0;
         }
         int32_t tot = 0;
 #pragma unroll
         for (int g = 0; g < kCompactGroups; ++g) {
             const int32_t e = e0 + g * 32;
-            if (valid != nullptr && e < n && valid[e] == 0) {
+            if (valid != nullptr && g < gpw && e < c0 + n_chunk && valid[e] == 0) {
                 if (mval[g] != 2) mask[e] = 2;
                 mval[g] = 2;
             }
@@ -58,19 +60,13 @@ compact_kernel(int32_t* __restrict__ mask, const uint8_t* __restrict__ valid, in
         }
         if (lane == 0) warp_tot[warp] = tot;
         __syncthreads();
-        if (warp == 0) {
-            const int32_t v = warp_tot[lane];
-            int32_t incl = v;
+        int32_t off = base, chunk_tot = 0;
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += t;
-            }
-            warp_off[lane] = incl - v;
-            if (lane == 31) chunk_tot = incl;
+        for (int w = 0; w < kCompactWarps; ++w) {
+            const int32_t t = warp_tot[w];
+            off += (w < warp) ? t : 0;
+            chunk_tot += t;
         }
-        __syncthreads();
-        int32_t off = base + warp_off[warp];
 #pragma unroll
         for (int g = 0; g < kCompactGroups; ++g) {
             if ((ballot[g] >> lane) & 1u) idx[off + __popc(ballot[g] & lt)] = e0 + g * 32;
@@ -165,7 +161,7 @@ __device__ __forceinline__ void norm_rope_store(const uint4& x, const float* w, 
 
 // Work item = (executed row m, group of up to 8 heads); one warp per item. All 12 of a lane's
 // 16-byte loads (Q, K, V of 4 head pairs) are issued before any arithmetic so that every warp keeps
-// 6 KB in flight; 2 CTAs of 8 warps per SM keep ~96 KB in flight per SM.
+// 6 KB in flight; 2 CTAs of 8 warps per SM (measured faster than 4-head items at 3 CTAs per SM).
 constexpr int kGatherHeadsPerItem = 8;
 constexpr int kGatherMinBlocks = 2;
 
@@ -200,10 +196,11 @@ gather_norm_rope_kernel(const __grid_constant__ GatherArgs a) {
         const T* qrow = Q + (int64_t)i * a.ld_qkv + 8 * sub;
         const T* krow = K + (int64_t)i * a.ld_qkv + 8 * sub;
         const T* vrow = V + (int64_t)i * a.ld_qkv + 8 * sub;
-        uint4 qv[4], kv[4], vv[4];
-        bool act[4];
+        constexpr int kU = kGatherHeadsPerItem / 2;  // head pairs per item
+        uint4 qv[kU], kv[kU], vv[kU];
+        bool act[kU];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kU; ++u) {
             const int h = h0 + 2 * u + half;
             act[u] = h < a.n_heads;
             if (act[u]) {
@@ -234,7 +231,7 @@ gather_norm_rope_kernel(const __grid_constant__ GatherArgs a) {
         if (mode == 1 && SV != nullptr) {
             T* srow = SV + (int64_t)m * 2 * C + 8 * sub;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < kU; ++u) {
                 const int h = h0 + 2 * u + half;
                 if (act[u]) {
                     *reinterpret_cast<uint4*>(srow + h * kHeadDim) =
@@ -248,7 +245,7 @@ gather_norm_rope_kernel(const __grid_constant__ GatherArgs a) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) w[e] = __ldg(a.norm_q + 8 * sub + e);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kU; ++u) {
             // every lane joins the shuffles; inactive heads compute on zeros and skip the store
             const int h = h0 + 2 * u + half;
             norm_rope_store<T>(qv[u], w, a.eps, cs, sn, qcrow + h * kHeadDim, act[u]);
@@ -256,7 +253,7 @@ gather_norm_rope_kernel(const __grid_constant__ GatherArgs a) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) w[e] = __ldg(a.norm_k + 8 * sub + e);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kU; ++u) {
             const int h = h0 + 2 * u + half;
             norm_rope_store<T>(kv[u], w, a.eps, cs, sn, ckrow + h * kHeadDim, act[u]);
             if (act[u]) *reinterpret_cast<uint4*>(cvrow + h * kHeadDim) = vv[u];
