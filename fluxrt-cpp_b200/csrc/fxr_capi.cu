@@ -402,6 +402,20 @@ int32_t fxr_preprocess_mask(int32_t* mask, const uint8_t* valid, int32_t n_token
     return FXR_OK;
 }
 
+int32_t fxr_mark_updated(const int32_t* mask, uint8_t* valid, int32_t n_text, int32_t n_tokens,
+                         void* stream) {
+    if (n_tokens < 0 || n_text < 0) return fail(FXR_ERR_INVALID, "negative size");
+    if (n_tokens <= n_text) return FXR_OK;
+    if (!mask || !valid) return fail(FXR_ERR_INVALID, "null pointer");
+    const int32_t n_img = n_tokens - n_text;
+    fxr::mark_updated_kernel<<<(n_img + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        mask, valid, n_text, n_tokens);
+    FXR_CHECK_LAUNCH("mark_updated_kernel launch");
+    return FXR_OK;
+}
+
+void fxr_internal_set_error(const char* msg) { t_last_error = msg ? msg : ""; }
+
 int32_t fxr_gather_norm_rope(const fxr_frame_desc* desc, const void* q, const void* k,
                              const void* v, const int32_t* mask, const int32_t* idx,
                              const int32_t* count, const int32_t* pos, const float* norm_q,

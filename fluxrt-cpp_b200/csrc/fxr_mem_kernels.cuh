@@ -84,6 +84,15 @@ __global__ void preprocess_mask_kernel(int32_t* __restrict__ mask, const uint8_t
     if (i < n && valid[i] == 0) mask[i] = 2;
 }
 
+// valid[i] = 1 for image tokens (i >= n_text) whose cache row was updated (mask 2): the validity
+// update of sync_output_cache_kernel (spatial_kv_cache.cu:49-51); text tokens stay invalid, so the
+// preprocess executes them every frame.
+__global__ void mark_updated_kernel(const int32_t* __restrict__ mask, uint8_t* __restrict__ valid,
+                                    int32_t n_text, int32_t n) {
+    const int32_t i = n_text + blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n && mask[i] == 2) valid[i] = 1;
+}
+
 // ---------------------------------------------------------------------------------------------
 // Fused gather + QK-RMSNorm + RoPE + cache-row write.
 // One warp per executed token; the two half-warps take two heads at a time; lane `sub` of a half

@@ -23,20 +23,39 @@ FXR_ERR_NCCL = 6
 
 FXR_F32, FXR_F16, FXR_BF16 = 0, 1, 2
 
-# Every symbol include/fxr.h declares (checked by the CPU test suite).
+# Every symbol include/fxr.h and include/fxr_plugin.h declare (checked by the CPU test suite).
 EXPORTED = [
     "fxr_abi_version", "fxr_build_info", "fxr_last_error_string", "fxr_check_device_error",
     "fxr_workspace_size", "fxr_workspace_views", "fxr_mask_compact", "fxr_preprocess_mask",
-    "fxr_gather_norm_rope", "fxr_attention_active", "fxr_restore_rows", "fxr_gather_rows",
-    "fxr_scatter_rows", "fxr_kv_sync", "fxr_output_cache_sync", "fxr_rms_norm",
-    "fxr_frame_forward",
+    "fxr_mark_updated", "fxr_gather_norm_rope", "fxr_attention_active", "fxr_restore_rows",
+    "fxr_gather_rows", "fxr_scatter_rows", "fxr_kv_sync", "fxr_output_cache_sync",
+    "fxr_rms_norm", "fxr_attention_f32_bhsd", "fxr_frame_forward", "fxr_frame_forward_noalloc",
+    "fxr_plugin_create", "fxr_plugin_clone", "fxr_plugin_destroy", "fxr_plugin_name",
+    "fxr_plugin_version", "fxr_plugin_namespace", "fxr_plugin_fields", "fxr_plugin_output_desc",
+    "fxr_plugin_supports", "fxr_plugin_configure", "fxr_plugin_workspace_size",
+    "fxr_plugin_enqueue", "fxr_plugin_cache",
 ]
+
+FXR_FIELD_FLOAT32, FXR_FIELD_INT32, FXR_FIELD_CHAR = 1, 3, 6
+FXR_DTYPE_INT32 = 3
 
 
 class FxrError(RuntimeError):
     def __init__(self, status: int, msg: str):
         super().__init__(f"fxr status {status}: {msg}")
         self.status = status
+
+
+class PluginField(ctypes.Structure):
+    """Mirror of fxr_plugin_field (include/fxr_plugin.h)."""
+    _fields_ = [("name", ctypes.c_char_p), ("data", ctypes.c_void_p), ("type", ctypes.c_int32),
+                ("length", ctypes.c_int32)]
+
+
+class TensorDesc(ctypes.Structure):
+    """Mirror of fxr_tensor_desc (include/fxr_plugin.h)."""
+    _fields_ = [("nb_dims", ctypes.c_int32), ("dtype", ctypes.c_int32),
+                ("dims", ctypes.c_int64 * 8)]
 
 
 class FrameDesc(ctypes.Structure):
@@ -97,6 +116,29 @@ def load(path: str | None = None) -> ctypes.CDLL:
     L.fxr_rms_norm.argtypes = [_vp, _vp, _vp, ctypes.c_float, _i64, _i32, _i32, _vp]
     L.fxr_frame_forward.argtypes = [ctypes.POINTER(FrameDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]
+    L.fxr_frame_forward_noalloc.argtypes = [ctypes.POINTER(FrameDesc)] + [_vp] * 12
+    L.fxr_mark_updated.argtypes = [_vp, _vp, _i32, _i32, _vp]
+    L.fxr_attention_f32_bhsd.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp]
+    _pf = ctypes.POINTER(PluginField)
+    _pt = ctypes.POINTER(TensorDesc)
+    L.fxr_plugin_create.argtypes = [_pf, _i32]
+    L.fxr_plugin_create.restype = _vp
+    L.fxr_plugin_clone.argtypes = [_vp]
+    L.fxr_plugin_clone.restype = _vp
+    L.fxr_plugin_destroy.argtypes = [_vp]
+    L.fxr_plugin_destroy.restype = None
+    for fn in (L.fxr_plugin_name, L.fxr_plugin_version, L.fxr_plugin_namespace):
+        fn.restype = ctypes.c_char_p
+    L.fxr_plugin_fields.argtypes = [_vp, _pf, _i32]
+    L.fxr_plugin_output_desc.argtypes = [_vp, _pt, _i32, _pt, _i32]
+    L.fxr_plugin_supports.argtypes = [_vp, _i32, _pt, _i32, _i32]
+    L.fxr_plugin_configure.argtypes = [_vp, _pt, _i32, _pt, _i32]
+    L.fxr_plugin_workspace_size.argtypes = [_vp, _pt, _i32]
+    L.fxr_plugin_workspace_size.restype = ctypes.c_size_t
+    L.fxr_plugin_enqueue.argtypes = [_vp, _pt, _pt, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp,
+                                     ctypes.c_size_t, _vp]
+    L.fxr_plugin_cache.argtypes = [_vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
+                                   ctypes.POINTER(_vp)]
     for name in EXPORTED:
         f = getattr(L, name)
         if f.restype is ctypes.c_int:  # default
@@ -250,3 +292,150 @@ def frame_forward(cfg: FrameConfig, q, k, v, mask, valid, pos, norm_q, norm_k, c
                                     _ptr(valid), _ptr(pos), _ptr(norm_q), _ptr(norm_k),
                                     _ptr(cache_k), _ptr(cache_v), _ptr(out), _ptr(workspace),
                                     workspace.numel() * workspace.element_size(), _stream(stream)))
+
+
+def frame_forward_noalloc(cfg: FrameConfig, q, k, v, mask, valid, pos, norm_q, norm_k, cache_k,
+                          cache_v, out, stream=None):
+    d = cfg.desc()
+    _check(load().fxr_frame_forward_noalloc(ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(mask),
+                                            _ptr(valid), _ptr(pos), _ptr(norm_q), _ptr(norm_k),
+                                            _ptr(cache_k), _ptr(cache_v), _ptr(out),
+                                            _stream(stream)))
+
+
+def mark_updated(mask, valid, n_text: int, stream=None):
+    _check(load().fxr_mark_updated(_ptr(mask), _ptr(valid), n_text, mask.numel(), _stream(stream)))
+
+
+def attention_f32_bhsd(q, k, v, out, stream=None):
+    """out = softmax(q k^T / sqrt(d)) v for fp32 [B, H, S, D] tensors (SIMT path)."""
+    B, H, S, D = q.shape
+    _check(load().fxr_attention_f32_bhsd(_ptr(q), _ptr(k), _ptr(v), _ptr(out), B, H, S,
+                                         k.shape[2], D, _stream(stream)))
+
+
+def tensor_desc(shape, dtype_code_: int) -> TensorDesc:
+    t = TensorDesc()
+    t.nb_dims = len(shape)
+    t.dtype = dtype_code_
+    for i, n in enumerate(shape):
+        t.dims[i] = int(n)
+    return t
+
+
+def _tensor_code(t) -> int:
+    import torch
+    return FXR_DTYPE_INT32 if t.dtype == torch.int32 else dtype_code(t.dtype)
+
+
+class SparseAttnPlugin:
+    """Python handle on the plugin core of include/fxr_plugin.h (Flux2SparseAttnPlugin).
+
+    Fields are given as keyword arguments: num_heads, head_dim, n_txt, layer_idx (int),
+    rope_axes (sequence of 1-4 ints), rope_theta, eps (float).
+    """
+
+    _INT = ("num_heads", "head_dim", "n_txt", "layer_idx")
+    _FLOAT = ("rope_theta", "eps")
+
+    def __init__(self, _handle=None, **fields):
+        L = load()
+        if _handle is None:
+            keep, arr = [], (PluginField * max(len(fields), 1))()
+            for i, (name, val) in enumerate(fields.items()):
+                if name == "rope_axes":
+                    buf = (ctypes.c_int32 * len(val))(*val)
+                    ftype, n = FXR_FIELD_INT32, len(val)
+                elif name in self._FLOAT:
+                    buf, ftype, n = (ctypes.c_float * 1)(val), FXR_FIELD_FLOAT32, 1
+                else:
+                    buf, ftype, n = (ctypes.c_int32 * 1)(val), FXR_FIELD_INT32, 1
+                keep.append(buf)
+                arr[i] = PluginField(name.encode(), ctypes.cast(buf, ctypes.c_void_p), ftype, n)
+            _handle = L.fxr_plugin_create(arr, len(fields))
+            if not _handle:
+                raise FxrError(FXR_ERR_INVALID, L.fxr_last_error_string().decode())
+        self._h = _handle
+        self._L = L
+
+    def __del__(self):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            self._L.fxr_plugin_destroy(h)
+
+    def clone(self) -> "SparseAttnPlugin":
+        return SparseAttnPlugin(_handle=self._L.fxr_plugin_clone(self._h))
+
+    def fields(self) -> dict:
+        n = self._L.fxr_plugin_fields(self._h, None, 0)
+        arr = (PluginField * n)()
+        self._L.fxr_plugin_fields(self._h, arr, n)
+        out = {}
+        for f in arr:
+            if f.type == FXR_FIELD_FLOAT32:
+                vals = list(ctypes.cast(f.data, ctypes.POINTER(ctypes.c_float))[:f.length])
+            else:
+                vals = list(ctypes.cast(f.data, ctypes.POINTER(ctypes.c_int32))[:f.length])
+            out[f.name.decode()] = vals if f.name == b"rope_axes" else vals[0]
+        return out
+
+    @staticmethod
+    def _descs(tensors):
+        arr = (TensorDesc * len(tensors))()
+        for i, t in enumerate(tensors):
+            arr[i] = tensor_desc(t.shape, _tensor_code(t)) if not isinstance(t, TensorDesc) else t
+        return arr
+
+    def output_desc(self, inputs) -> TensorDesc:
+        out = TensorDesc()
+        _check_plugin(self._L.fxr_plugin_output_desc(self._h, self._descs(inputs), len(inputs),
+                                                     ctypes.byref(out), 1))
+        return out
+
+    def supports(self, pos: int, io) -> bool:
+        return self._L.fxr_plugin_supports(self._h, pos, self._descs(io), len(io) - 1, 1) == 1
+
+    def configure(self, inputs, output=None):
+        outs = self._descs([output]) if output is not None else None
+        _check_plugin(self._L.fxr_plugin_configure(self._h, self._descs(inputs), len(inputs), outs,
+                                                   1 if output is not None else 0))
+
+    def workspace_size(self, inputs) -> int:
+        return self._L.fxr_plugin_workspace_size(self._h, self._descs(inputs), len(inputs))
+
+    def enqueue(self, inputs, output, workspace, stream=None):
+        ins = self._descs(inputs)
+        outd = self._descs([output])
+        ptrs = (ctypes.c_void_p * len(inputs))(*[t.data_ptr() for t in inputs])
+        optrs = (ctypes.c_void_p * 1)(output.data_ptr())
+        _check_plugin(self._L.fxr_plugin_enqueue(self._h, ins, outd, ptrs, optrs, _ptr(workspace),
+                                                 workspace.numel() * workspace.element_size(),
+                                                 _stream(stream)))
+
+    def cache(self, b: int):
+        """Device pointers (cache_k, cache_v, valid) of edit stream b."""
+        k, v, valid = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        _check_plugin(self._L.fxr_plugin_cache(self._h, b, ctypes.byref(k), ctypes.byref(v),
+                                               ctypes.byref(valid)))
+        return k.value, v.value, valid.value
+
+    def cache_tensors(self, b: int, n_tokens: int, channels: int, dtype):
+        """Torch views (no copy) of stream b's K cache [N, C], V cache [N, C] and valid [N]."""
+        k, v, valid = self.cache(b)
+        return (_device_view(k, (n_tokens, channels), "<u2").view(dtype),
+                _device_view(v, (n_tokens, channels), "<u2").view(dtype),
+                _device_view(valid, (n_tokens,), "|u1"))
+
+
+def _device_view(ptr: int, shape, typestr: str):
+    import torch
+
+    class _Mem:
+        __cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                    "data": (ptr, False), "version": 2}
+    return torch.as_tensor(_Mem(), device="cuda")
+
+
+def _check_plugin(status: int):
+    if status != 0:
+        raise FxrError(status, load().fxr_last_error_string().decode())

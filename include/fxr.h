@@ -100,6 +100,11 @@ int32_t fxr_mask_compact(int32_t* mask, const uint8_t* valid, int32_t n_tokens,
 /* Reference preprocess alone (spatial_kv_cache.cu:12-19): mask[i] = 2 where !valid[i]. */
 int32_t fxr_preprocess_mask(int32_t* mask, const uint8_t* valid, int32_t n_tokens, void* stream);
 
+/* Validity update after a frame (sync_output_cache_kernel's valid write, spatial_kv_cache.cu:49-51):
+ * valid[i] = 1 for image tokens i in [n_text, n_tokens) with mask[i] == 2. */
+int32_t fxr_mark_updated(const int32_t* mask, uint8_t* valid, int32_t n_text, int32_t n_tokens,
+                         void* stream);
+
 /* Fused gather + per-head QK-RMSNorm + multi-axis RoPE + cache-row write.
  * Replaces gather_tokens (gather_scatter_kernels.cu:15-41) + rms_norm (flux2_kernels.cu:58-90,
  * per head) + the K/V merge/update of sync_kv_cache_kernel (spatial_kv_cache.cu:55-87) restricted

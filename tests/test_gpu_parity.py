@@ -367,3 +367,32 @@ def test_rms_norm_standalone(cuda, dtype, dim):
         assert_close(host(dy), ref, what="rmsnorm", max_abs=2e-5, mean_abs=2e-6)
     else:
         check_qk(host(dy), ref, dtype, "rmsnorm")
+
+
+@pytest.mark.parametrize("B,H,S,L,D", [(1, 2, 37, 300, 128), (2, 3, 64, 64, 64), (1, 1, 5, 1, 32)])
+def test_attention_f32_bhsd_vs_torch(cuda, B, H, S, L, D):
+    """The fp32 SIMT attention behind the reference-signature attention_fwd: joint softmax over all
+    kv_len keys, checked against torch's fp32 scaled-dot-product attention."""
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + S)
+    q = torch.randn(B, H, S, D, device="cuda", generator=g)
+    k = torch.randn(B, H, L, D, device="cuda", generator=g)
+    v = torch.randn(B, H, L, D, device="cuda", generator=g)
+    out = torch.empty_like(q)
+    fxr.attention_f32_bhsd(q, k, v, out)
+    sync_ok()
+    ref = torch.nn.functional.scaled_dot_product_attention(q.double(), k.double(), v.double())
+    assert_close(host(out), ref.float().cpu().numpy(), what="attention f32", max_abs=2e-5,
+                 mean_abs=2e-6)
+
+
+def test_mark_updated_bit_exact(cuda):
+    rng = np.random.default_rng(77)
+    T, N = 17, 1000
+    mask = rng.choice([0, 1, 2], size=N).astype(np.int32)
+    valid = (rng.random(N) < 0.3).astype(np.uint8)
+    dv = torch.from_numpy(valid).cuda()
+    fxr.mark_updated(dev(mask, "i32"), dv, T)
+    sync_ok()
+    exp = valid.copy()
+    exp[T:][mask[T:] == 2] = 1
+    assert np.array_equal(host(dv), exp)

@@ -1,0 +1,196 @@
+"""The sparse attention plugin core (include/fxr_plugin.h): the IPluginV3 lifecycle of the
+reference's plugins (flux2_plugin_base.h:30-141) without TensorRT types.
+
+CPU tests: creation from fields, serialisation round trip, shape/type/format rules, workspace,
+errors. GPU tests: enqueue over B independent edit streams for consecutive frames, against the
+frame entry point with the validity bookkeeping done by hand, and against the oracle."""
+import numpy as np
+import pytest
+
+import fxr
+import workloads as W
+
+F16, BF16, F32, I32 = fxr.FXR_F16, fxr.FXR_BF16, fxr.FXR_F32, fxr.FXR_DTYPE_INT32
+
+
+def descs(B, N, heads, dtype=BF16, n_axes=3):
+    C = heads * 128
+    td = fxr.tensor_desc
+    return [td((B, N, C), dtype), td((B, N, C), dtype), td((B, N, C), dtype), td((B, N), I32),
+            td((N, n_axes), I32), td((128,), F32), td((128,), F32)]
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return fxr.load()
+
+
+def test_identity_and_defaults(lib):
+    p = fxr.SparseAttnPlugin()
+    assert lib.fxr_plugin_name() == b"Flux2SparseAttnPlugin"
+    assert lib.fxr_plugin_version() == b"1"
+    assert lib.fxr_plugin_namespace() == b"fluxrt"
+    f = p.fields()
+    assert f["num_heads"] == 24 and f["head_dim"] == 128 and f["n_txt"] == 0
+    assert f["rope_axes"] == [16, 56, 56]
+    assert f["rope_theta"] == pytest.approx(10000.0) and f["eps"] == pytest.approx(1e-6)
+
+
+def test_fields_round_trip_and_clone(lib):
+    kw = dict(num_heads=6, n_txt=256, layer_idx=3, rope_axes=[32, 32, 32, 32], rope_theta=2000.0,
+              eps=1e-5)
+    p = fxr.SparseAttnPlugin(**kw)
+    f = p.fields()
+    for k, v in kw.items():
+        assert f[k] == pytest.approx(v), k
+    q = fxr.SparseAttnPlugin(**f)          # serialise -> deserialise
+    assert q.fields() == f
+    assert p.clone().fields() == f
+
+
+@pytest.mark.parametrize("bad", [dict(bogus=1), dict(head_dim=64), dict(num_heads=0),
+                                 dict(rope_axes=[16, 55, 57]), dict(rope_axes=[64, 64, 64]),
+                                 dict(n_txt=-1), dict(rope_theta=0.0)])
+def test_bad_fields_rejected(lib, bad):
+    with pytest.raises(fxr.FxrError):
+        fxr.SparseAttnPlugin(**bad)
+    assert lib.fxr_last_error_string()
+
+
+def test_output_desc_and_shape_rules(lib):
+    p = fxr.SparseAttnPlugin(num_heads=4, n_txt=512)
+    ins = descs(2, 1536, 4)
+    o = p.output_desc(ins)
+    assert o.nb_dims == 3 and list(o.dims[:3]) == [2, 1536, 512] and o.dtype == BF16
+    bad = list(ins)
+    bad[1] = fxr.tensor_desc((2, 1536, 512), F16)        # K type differs from Q
+    with pytest.raises(fxr.FxrError):
+        p.output_desc(bad)
+    bad = list(ins)
+    bad[4] = fxr.tensor_desc((1536, 2), I32)             # wrong number of RoPE axes
+    with pytest.raises(fxr.FxrError):
+        p.output_desc(bad)
+    with pytest.raises(fxr.FxrError):                    # C != num_heads * 128
+        p.output_desc(descs(2, 1536, 3))
+    with pytest.raises(fxr.FxrError):                    # N must exceed n_txt
+        p.output_desc(descs(1, 512, 4))
+
+
+def test_supports_format_combination(lib):
+    p = fxr.SparseAttnPlugin(num_heads=4, n_txt=512)
+    for dt in (BF16, F16):
+        io = descs(1, 1536, 4, dt) + [fxr.tensor_desc((1, 1536, 512), dt)]
+        assert all(p.supports(i, io) for i in range(8))
+    io = descs(1, 1536, 4, F32) + [fxr.tensor_desc((1, 1536, 512), F32)]
+    assert not p.supports(0, io)
+    io = descs(1, 1536, 4, BF16) + [fxr.tensor_desc((1, 1536, 512), F16)]
+    assert not p.supports(7, io)
+    io = descs(1, 1536, 4, BF16)
+    io[3] = fxr.tensor_desc((1, 1536), F32)
+    assert not p.supports(3, io + [fxr.tensor_desc((1, 1536, 512), BF16)])
+
+
+def test_workspace_is_frame_workspace_plus_mask_copy(lib):
+    p = fxr.SparseAttnPlugin(num_heads=24, n_txt=512)
+    ws = p.workspace_size(descs(4, 4608, 24))
+    frame = fxr.workspace_size(fxr.FrameConfig(n_tokens=4608, n_text=512))
+    assert ws == frame + (4608 * 4 + 255) // 256 * 256
+    assert p.workspace_size(descs(4, 4608, 23)) == 0
+
+
+def test_enqueue_and_cache_need_configure(lib):
+    p = fxr.SparseAttnPlugin(num_heads=4, n_txt=512)
+    ins = (fxr.TensorDesc * 7)(*descs(1, 1536, 4))
+    out = (fxr.TensorDesc * 1)(fxr.tensor_desc((1, 1536, 512), BF16))
+    st = lib.fxr_plugin_enqueue(p._h, ins, out, None, None, None, 0, None)
+    assert st == -1 and b"configure" in lib.fxr_last_error_string()
+    with pytest.raises(fxr.FxrError):
+        p.cache(0)
+
+
+# ---------------------------------------------------------------------------------------------
+def _host(t):
+    return t.float().cpu().numpy() if t.is_floating_point() else t.cpu().numpy()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_plugin_streams_match_frame_entry_and_oracle(cuda, dtype):
+    import torch
+    import oracle as O
+    td = {"bf16": torch.bfloat16, "f16": torch.float16}[dtype]
+    base = W.C1
+    w = W.Workload("c1_h4", base.grid_h, base.grid_w, base.n_text, 4, 128, dtype, base.active,
+                   base.pattern, base.rope_axes, base.rope_theta)
+    B, N, C = 2, w.n_tokens, 4 * 128
+    p = fxr.SparseAttnPlugin(num_heads=4, n_txt=w.n_text, rope_axes=list(w.rope_axes),
+                             rope_theta=float(w.rope_theta))
+    frames = [[W.make_frame(w, seed=100 * f + b, p=0.3 if f else None) for b in range(B)]
+              for f in range(2)]
+    pos = torch.from_numpy(frames[0][0]["pos"]).cuda()
+    nq = torch.from_numpy(frames[0][0]["norm_q"]).cuda()
+    nk = torch.from_numpy(frames[0][0]["norm_k"]).cuda()
+    out0 = np.stack([frames[0][b]["out"] for b in range(B)])
+    out = torch.from_numpy(out0).cuda().to(td)
+
+    def stack(f, key, ty):
+        return torch.from_numpy(np.stack([frames[f][b][key] for b in range(B)])).cuda().to(ty)
+
+    ins0 = [stack(0, "q", td), stack(0, "k", td), stack(0, "v", td), stack(0, "mask", torch.int32),
+            pos, nq, nk]
+    p.configure(ins0, out)
+    ws = torch.empty(p.workspace_size(ins0), dtype=torch.uint8, device="cuda")
+    for b in range(B):                       # a fresh plugin's caches: all rows invalid, zero
+        k, v, valid = p.cache_tensors(b, N, C, td)
+        assert not k.any() and not v.any() and not valid.any()
+
+    # by hand: fxr_frame_forward + validity bookkeeping, and the oracle
+    cfg = fxr.FrameConfig(n_tokens=N, n_text=w.n_text, n_heads=4, dtype=dtype,
+                          rope_axes=w.rope_axes, rope_theta=w.rope_theta)
+    fws = torch.empty(fxr.workspace_size(cfg), dtype=torch.uint8, device="cuda")
+    h_valid = [torch.zeros(N, dtype=torch.uint8, device="cuda") for _ in range(B)]
+    h_ck = [torch.zeros(N, C, dtype=td, device="cuda") for _ in range(B)]
+    h_cv = [torch.zeros(N, C, dtype=td, device="cuda") for _ in range(B)]
+    h_out = [torch.from_numpy(out0[b]).cuda().to(td) for b in range(B)]
+    o_valid = [np.zeros(N, np.uint8) for _ in range(B)]
+    o_ck = [np.zeros((N, C), np.float32) for _ in range(B)]
+    o_cv = [np.zeros((N, C), np.float32) for _ in range(B)]
+    o_out = [out0[b].copy() for b in range(B)]
+
+    for f in range(2):
+        ins = [stack(f, "q", td), stack(f, "k", td), stack(f, "v", td),
+               stack(f, "mask", torch.int32), pos, nq, nk]
+        mask_before = ins[3].clone()
+        p.enqueue(ins, out, ws)
+        torch.cuda.synchronize()
+        assert fxr.check_device_error() == 0
+        assert torch.equal(ins[3], mask_before)          # the engine's input stays read-only
+        for b in range(B):
+            fr = frames[f][b]
+            m = torch.from_numpy(fr["mask"]).cuda()
+            fxr.frame_forward(cfg, ins[0][b], ins[1][b], ins[2][b], m, h_valid[b], pos, nq, nk,
+                              h_ck[b], h_cv[b], h_out[b], fws)
+            fxr.mark_updated(m, h_valid[b], w.n_text)
+            r = O.frame_forward(fr["q"], fr["k"], fr["v"], fr["mask"], o_valid[b], fr["pos"],
+                                frames[0][0]["norm_q"], frames[0][0]["norm_k"], o_ck[b], o_cv[b],
+                                o_out[b], 4, 128,
+                                w.rope_axes, w.rope_theta)
+            upd = (r["mask"] == 2) & (np.arange(N) >= w.n_text)
+            o_valid[b] = o_valid[b] | upd.astype(np.uint8)
+            o_ck[b] = W.round_storage(r["cache_k"], dtype)      # the caches hold storage values
+            o_cv[b] = W.round_storage(r["cache_v"], dtype)
+            o_out[b] = W.round_storage(r["out"], dtype)
+            ex = r["idx"]
+            torch.cuda.synchronize()
+            pk, pv, pvalid = p.cache_tensors(b, N, C, td)
+            assert torch.equal(out[b], h_out[b]), (f, b)           # same kernels: bit-exact
+            assert torch.equal(pk, h_ck[b]) and torch.equal(pv, h_cv[b]), (f, b)
+            assert torch.equal(pvalid, h_valid[b]), (f, b)
+            assert np.array_equal(_host(pvalid), o_valid[b]), (f, b)
+            tol = 2e-3 if dtype == "f16" else 4e-3
+            err = np.abs(_host(out[b])[ex] - r["out"][ex])
+            assert err.max() <= tol and err.mean() <= 2e-4, (f, b, err.max(), err.mean())
+            if f == 0:
+                assert ex.size == N                                # empty cache: everything runs
+            else:
+                assert ex.size < N
