@@ -47,7 +47,14 @@ def parse():
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
-    return ap.parse_args()
+    ap.add_argument("--split", choices=["replicas", "heads"], default=None,
+                    help="multi-GPU mode: independent streams per GPU (default except c5) or one "
+                         "frame split by heads with the O all-gather fused into the attention "
+                         "epilogue (default for c5)")
+    a = ap.parse_args()
+    if a.split is None:
+        a.split = "heads" if a.config == "c5" else "replicas"
+    return a
 
 
 def workload(args):
@@ -543,10 +550,195 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+# ---------------------------------------------------------------------------------------------
+# one frame split by heads over the GPUs (peer stores + arrival wait)
+# ---------------------------------------------------------------------------------------------
+def run_heads(args):
+    """A step is one frame of all heads, split across the ranks by heads; every rank's attention
+    epilogue stores its heads' O rows into every rank's output over NVLink, then each rank waits
+    for all arrivals. value = whole-frame attention FLOP / max-over-ranks time (strong scaling)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import fxr
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    fxr.load()
+    w = workload(args)
+    cfg = frame_cfg(w)
+    pk = peaks()
+    g = fxr.head_group(world, rank, w.n_heads, w.n_tokens)
+    N, C = w.n_tokens, w.n_heads * HEAD_DIM
+    c0, c1 = g.head0 * HEAD_DIM, (g.head0 + g.n_heads) * HEAD_DIM
+    dt = torch.bfloat16 if w.dtype == "bf16" else torch.float16
+
+    # rotating input sets: this rank's K/V cache shard of every set together exceeds twice the L2
+    shard_bytes = 2 * N * (c1 - c0) * 2
+    n_sets = int(min(12, max(2, -(-2 * L2_BYTES // max(shard_bytes, 1)))))
+    frames = []
+    for s_ in range(n_sets):
+        fr = make_device_frame(w, args.seed + 7919 * s_, device)   # same inputs on every rank
+        fr["cache_k"] = fr["cache_k"][:, c0:c1].contiguous()
+        fr["cache_v"] = fr["cache_v"][:, c0:c1].contiguous()
+        if s_ > 0:
+            del fr["out"]
+        frames.append(fr)
+    out_bytes = N * C * 2
+    buf = fxr.IpcBuffer(out_bytes + 256)
+    out = fxr.device_view(buf.ptr.value, (N, C), dt)
+    out.copy_(frames[0]["out"])
+    mapped = []
+    handles = [buf.handle_bytes()]
+    if world > 1:
+        handles = [None] * world
+        dist.all_gather_object(handles, buf.handle_bytes())
+    for r in range(world):
+        ptr = buf.ptr.value if r == rank else fxr.ipc_open(handles[r])
+        if r != rank:
+            mapped.append(ptr)
+        g.out[r] = ptr
+        g.arrive[r] = ptr + out_bytes
+    ws = [torch.empty(fxr.workspace_size(cfg), dtype=torch.uint8, device=device)
+          for _ in range(n_sets)]
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    def frame(i):
+        fr = frames[i % n_sets]
+        fxr.frame_forward_heads(cfg, g, fr["q"], fr["k"], fr["v"], fr["mask"], None, fr["pos"],
+                                fr["norm_q"], fr["norm_k"], fr["cache_k"], fr["cache_v"],
+                                ws[i % n_sets])
+        fxr.head_group_wait(g)
+
+    for i in range(max(args.warmup, 3)):
+        frame(i)
+    torch.cuda.synchronize()
+    if fxr.check_device_error() != 0:
+        raise RuntimeError("device error during warm-up")
+    use_graph = not args.no_graph
+    graphs = []
+    if use_graph:
+        for s_ in range(n_sets):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                frame(s_)
+            graphs.append(gr)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        for s_ in range(n_sets):
+            graphs[s_].replay()
+        torch.cuda.synchronize()
+
+    def step(i):
+        if use_graph:
+            graphs[i % n_sets].replay()
+        else:
+            frame(i)
+
+    stream = torch.cuda.current_stream()
+    clocks = Clocks(local)
+    clocks.start()
+    if world > 1:
+        dist.barrier()
+    n_soak = 0
+    t_end = time.time() + 1.0
+    while True:                      # every rank runs the same number of soak frames
+        for _ in range(16):
+            step(n_soak)
+            n_soak += 1
+        torch.cuda.synchronize()
+        more = torch.tensor([1 if time.time() < t_end else 0], device=device)
+        if world > 1:
+            dist.all_reduce(more, op=dist.ReduceOp.MIN)
+        if not int(more.item()):
+            break
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    err = fxr.check_device_error()
+    if world > 1:
+        t = torch.tensor([t_ms, float(err != 0)], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_ms, bad = float(t[0].item()), bool(t[1].item())
+    else:
+        bad = err != 0
+    if bad:
+        raise RuntimeError("device error during the timed region")
+    flops = sum(attn_flops(w, frames[i % n_sets]["M"]) for i in range(args.steps))
+    ms_per_step = t_ms / args.steps
+    value = flops / (t_ms * 1e-3) / 1e12
+    M_avg = statistics.mean(fr["M"] for fr in frames)
+    # roofline of the fused attention + all-gather: the slower of the tensor-core time of this
+    # rank's heads and the NVLink time of the O slices it sends to the other ranks
+    flop_rank = attn_flops(w, M_avg) * g.n_heads / w.n_heads
+    nvlink_bytes = M_avg * (c1 - c0) * 2 * (world - 1)
+    t_tensor = flop_rank / (pk["bf16_tflops"] * 1e12)
+    t_link = nvlink_bytes / 770e9
+    out_line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+        "us_per_frame": round(ms_per_step * 1e3, 2), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": w.dtype, "impl": "ours",
+        "data": "synthetic: N(0,1) Q/K/V/cache, N(1,0.1) norm weights, Bernoulli mask (seeded)",
+        "config": {"workload": w.name, "frame_px": w.grid_h * 16, "n_tokens": N,
+                   "n_text": w.n_text, "active": w.active, "M_avg": M_avg, "heads": w.n_heads,
+                   "heads_per_gpu": [int(x) for x in _heads_split(w.n_heads, world)],
+                   "parallelism": f"heads{world}",
+                   "l2": f"{n_sets} rotating input sets, cache shards {n_sets * shard_bytes / 2**20:.0f} MiB > L2",
+                   "graph": use_graph},
+        "roofline": {"bound": "tensor" if t_tensor >= t_link else "nvlink",
+                     "kernel": "fxr::attn::attention_kernel (epilogue stores to every rank)",
+                     "target_us": round(max(t_tensor, t_link) * 1e6, 2),
+                     "achieved_frac": round(max(t_tensor, t_link) * 1e3 / ms_per_step, 4),
+                     "peak_tensor": pk["bf16_tflops"], "peak_nvlink_gbs": 770.0,
+                     "nvlink_bytes_per_rank": nvlink_bytes,
+                     "note": "frac = roofline time of one frame / measured frame time (whole frame, 5 kernels)"},
+        "e2e": None,
+        "gpu_launches": 5 * args.steps,
+        "clocks": clk,
+    }
+    if rank == 0:
+        print(json.dumps(out_line), flush=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()             # no rank unmaps or frees while a peer could still store
+    for gr in graphs:
+        del gr
+    graphs.clear()
+    for p_ in mapped:
+        fxr.ipc_close(p_)
+    buf.free()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _heads_split(n_heads, world):
+    return [n_heads // world + (1 if r < n_heads % world else 0) for r in range(world)]
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.split == "heads":
+        run_heads(args)
     else:
         run_ours(args)
 

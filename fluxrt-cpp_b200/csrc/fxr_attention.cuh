@@ -84,14 +84,19 @@ constexpr uint32_t kSlotAbort = kSlotTmem + 4;
 static_assert(kSlotAbort + 4 <= 256, "barrier area overflow");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
+constexpr int kMaxOut = 8;   // destinations of a head-sharded frame: one per GPU of the group
+
 struct Params {
     const int32_t* count;
     const int32_t* idx;
-    void* out;
     int64_t ld_out;
     int32_t n_tokens;
     int32_t n_heads;
     float scale_log2;   // softmax scale * log2(e)
+    int32_t n_out;      // O destinations (1: this GPU only)
+    int32_t src_rank;   // arrival slot this GPU increments at every destination
+    void* out[kMaxOut];          // O row bases (this GPU's buffer and peers' mapped buffers)
+    uint32_t* arrive[kMaxOut];   // arrival slots of each destination; null: no signalling
 };
 
 __device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
@@ -320,7 +325,6 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         float* xch = reinterpret_cast<float*>(gbase + kSmemX);    // [buf][wg][row]
         const float c = p.scale_log2;
         const float2 c2 = make_float2(c, c);
-        T* __restrict__ out = static_cast<T*>(p.out);
         uint32_t s_it = 0, x_it = 0, units_done = 0;
         bool ok = true;
         // row data exchange among the four warps (one per warpgroup, same sub-partition) that hold
@@ -431,15 +435,24 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 const int32_t i = p.idx[m];
                 if (i >= 0 && i < p.n_tokens) {
                     const float inv = 1.0f / l_tot;
-                    uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)i * p.ld_out + (int64_t)head * kD + wg * 32);
+                    const int64_t off = (int64_t)i * p.ld_out + (int64_t)head * kD + wg * 32;
+                    uint4 v[4];
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
-                        uint4 v;
-                        v.x = StoreT<T>::pack2(__uint_as_float(o[8 * k + 0]) * inv, __uint_as_float(o[8 * k + 1]) * inv);
-                        v.y = StoreT<T>::pack2(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv);
-                        v.z = StoreT<T>::pack2(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv);
-                        v.w = StoreT<T>::pack2(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv);
-                        dst[k] = v;
+                        v[k].x = StoreT<T>::pack2(__uint_as_float(o[8 * k + 0]) * inv, __uint_as_float(o[8 * k + 1]) * inv);
+                        v[k].y = StoreT<T>::pack2(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv);
+                        v[k].z = StoreT<T>::pack2(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv);
+                        v[k].w = StoreT<T>::pack2(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv);
+                    }
+                    // the fused all-gather + scatter: the same 64 bytes go to every destination
+                    // (peer buffers are written over NVLink by these plain stores)
+#pragma unroll
+                    for (int t = 0; t < kMaxOut; ++t) {
+                        if (t < p.n_out) {
+                            uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.out[t]) + off);
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) dst[k] = v[k];
+                        }
                     }
                 } else {
                     atomicOr(&g_error_word, kErrBounds);
@@ -449,11 +462,20 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     }
 
     __syncwarp();  // role warps ran their loops on one lane; reconverge before the CTA barrier
+    const bool signal = p.arrive[0] != nullptr;
+    if (signal) __threadfence_system();   // this thread's O stores, visible to every GPU first
     tc_fence_before();
     __syncthreads();
     if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
+    }
+    // One arrival per CTA at every destination, also after an abort, so that the destinations'
+    // bounded waits end (the abort itself is reported through the error word).
+    if (signal && threadIdx.x == 0) {
+#pragma unroll
+        for (int t = 0; t < kMaxOut; ++t)
+            if (t < p.n_out) red_release_sys_add(p.arrive[t] + p.src_rank, 1u);
     }
 }
 

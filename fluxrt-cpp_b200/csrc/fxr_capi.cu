@@ -217,10 +217,25 @@ int grid_rows(int64_t rows, int rows_per_cta) {
     return (int)std::max<int64_t>(1, std::min(need, cap));
 }
 
+// Where the attention epilogue stores O: one buffer (a single-GPU frame), or every rank's buffer
+// of a head group plus the arrival slots it increments there.
+struct OutSet {
+    int32_t n = 1;
+    int32_t src_rank = 0;
+    void* out[fxr::attn::kMaxOut] = {};
+    uint32_t* arrive[fxr::attn::kMaxOut] = {};
+};
+
+int64_t attention_ctas(int64_t n_tokens, int64_t n_heads) {
+    if (n_tokens <= 0 || n_heads <= 0) return 0;
+    const int64_t max_tiles = (n_tokens + fxr::attn::kBM - 1) / fxr::attn::kBM * n_heads;
+    return std::max<int64_t>(1, std::min<int64_t>(max_tiles, sm_count()));
+}
+
 template <typename T>
 int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
                          const int32_t* count, const void* ck, const void* cv, const int32_t* idx,
-                         void* out, cudaStream_t stream) {
+                         const OutSet& os, cudaStream_t stream) {
     static bool configured[kMaxDevices] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -241,14 +256,18 @@ int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
     fxr::attn::Params p{};
     p.count = count;
     p.idx = idx;
-    p.out = out;
+    p.n_out = os.n;
+    p.src_rank = os.src_rank;
+    for (int t = 0; t < fxr::attn::kMaxOut; ++t) {
+        p.out[t] = os.out[t];
+        p.arrive[t] = os.arrive[t];
+    }
     p.ld_out = d->ld_out;
     p.n_tokens = d->n_tokens;
     p.n_heads = d->n_heads;
     const float scale = d->softmax_scale > 0.f ? d->softmax_scale : 1.0f / std::sqrt((float)d->head_dim);
     p.scale_log2 = scale * 1.4426950408889634f;
-    const int64_t max_tiles = (N + fxr::attn::kBM - 1) / fxr::attn::kBM * d->n_heads;
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_tiles, sm_count()));
+    const int grid = (int)attention_ctas(N, d->n_heads);
     cudaError_t e = launch_pdl(fxr::attn::attention_kernel<T>, dim3(grid), dim3(fxr::attn::kThreads),
                                fxr::attn::kSmemBytes, stream, tq, tk, tv, p);
     if (e != cudaSuccess) return cuda_status(e, "attention_kernel launch");
@@ -450,9 +469,11 @@ int32_t fxr_attention_active(const fxr_frame_desc* desc, const void* qc, int64_t
         (ld_qc % 8) || ld_qc < (int64_t)desc->n_heads * desc->head_dim)
         return fail(FXR_ERR_INVALID, "qc/cache/out must be 16-byte aligned with ld_qc >= C, %% 8");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    OutSet os;
+    os.out[0] = out;
     if (desc->dtype == FXR_BF16)
-        return launch_attention<__nv_bfloat16>(desc, qc, ld_qc, count, cache_k, cache_v, idx, out, s);
-    return launch_attention<__half>(desc, qc, ld_qc, count, cache_k, cache_v, idx, out, s);
+        return launch_attention<__nv_bfloat16>(desc, qc, ld_qc, count, cache_k, cache_v, idx, os, s);
+    return launch_attention<__half>(desc, qc, ld_qc, count, cache_k, cache_v, idx, os, s);
 }
 
 int32_t fxr_restore_rows(const fxr_frame_desc* desc, const int32_t* mask, const int32_t* idx,
@@ -657,6 +678,138 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void*
                                    stream)) != FXR_OK)
         return st;
     return fxr_restore_rows(desc, mask, w.idx, w.count, w.save, cache_k, cache_v, stream);
+}
+
+int32_t fxr_head_group_init(fxr_head_group* g, int32_t world, int32_t rank, int32_t n_heads,
+                            int32_t n_tokens) {
+    if (!g) return fail(FXR_ERR_INVALID, "null head group");
+    if (world < 1 || world > FXR_MAX_RANKS || rank < 0 || rank >= world || n_heads <= 0 || n_tokens < 0)
+        return fail(FXR_ERR_INVALID, "bad head group: world=%d rank=%d n_heads=%d n_tokens=%d", world,
+                    rank, n_heads, n_tokens);
+    std::memset(g, 0, sizeof(*g));
+    g->world = world;
+    g->rank = rank;
+    const int32_t base = n_heads / world, extra = n_heads % world;
+    int32_t h = 0;
+    for (int32_t r = 0; r < world; ++r) {
+        const int32_t hn = base + (r < extra ? 1 : 0);
+        if (r == rank) {
+            g->head0 = h;
+            g->n_heads = hn;
+        }
+        g->ctas[r] = (int32_t)attention_ctas(n_tokens, hn);
+        h += hn;
+    }
+    return FXR_OK;
+}
+
+int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g, const void* q,
+                                const void* k, const void* v, int32_t* mask, const uint8_t* valid,
+                                const int32_t* pos, const float* norm_q, const float* norm_k,
+                                void* cache_k, void* cache_v, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+    int32_t st = check_desc(desc, true);
+    if (st != FXR_OK) return st;
+    if (!g || g->world < 1 || g->world > FXR_MAX_RANKS || g->rank < 0 || g->rank >= g->world)
+        return fail(FXR_ERR_INVALID, "head group not initialised");
+    if (g->n_heads < 0 || g->head0 < 0 || g->head0 + g->n_heads > desc->n_heads)
+        return fail(FXR_ERR_INVALID, "head group heads [%d, %d) outside the frame's %d heads", g->head0,
+                    g->head0 + g->n_heads, desc->n_heads);
+    if (desc->n_tokens == 0 || g->n_heads == 0) return FXR_OK;
+    if ((int64_t)g->ctas[g->rank] != attention_ctas(desc->n_tokens, g->n_heads))
+        return fail(FXR_ERR_INVALID, "head group was initialised for another frame size");
+    const bool signal = g->world > 1 || g->arrive[0] != nullptr;
+    for (int32_t r = 0; r < g->world; ++r) {
+        if (!g->out[r]) return fail(FXR_ERR_INVALID, "head group out[%d] is null", r);
+        if (signal && !g->arrive[r]) return fail(FXR_ERR_INVALID, "head group arrive[%d] is null", r);
+        if (!aligned16(g->out[r])) return fail(FXR_ERR_INVALID, "head group out[%d] not 16-byte aligned", r);
+    }
+    if (!workspace) return fail(FXR_ERR_INVALID, "null workspace");
+    // this rank's slice of the frame: its heads, read from and written to the full-width rows
+    fxr_frame_desc sd = *desc;
+    sd.n_heads = g->n_heads;
+    sd.ld_cache = (int64_t)g->n_heads * desc->head_dim;
+    const Views w = carve(&sd, workspace);
+    if (workspace_bytes < w.total)
+        return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, w.total);
+    if (!aligned16(workspace)) return fail(FXR_ERR_INVALID, "workspace must be 16-byte aligned");
+    const size_t col = (size_t)g->head0 * desc->head_dim * dtype_bytes(desc->dtype);
+    const char* qh = static_cast<const char*>(q) + col;
+    const char* kh = static_cast<const char*>(k) + col;
+    const char* vh = static_cast<const char*>(v) + col;
+    if (!q || !k || !v) return fail(FXR_ERR_INVALID, "null q/k/v");
+    OutSet os;
+    os.n = g->world;
+    os.src_rank = g->rank;
+    for (int32_t r = 0; r < g->world; ++r) {
+        os.out[r] = static_cast<char*>(g->out[r]) + col;
+        os.arrive[r] = signal ? g->arrive[r] : nullptr;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if ((st = fxr_mask_compact(mask, valid, sd.n_tokens, w.idx, w.count, stream)) != FXR_OK) return st;
+    if ((st = fxr_gather_norm_rope(&sd, qh, kh, vh, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc,
+                                   w.ld_qc, cache_k, cache_v, w.save, stream)) != FXR_OK)
+        return st;
+    if (!cache_k || !cache_v || !aligned16(cache_k) || !aligned16(cache_v))
+        return fail(FXR_ERR_INVALID, "cache must be non-null and 16-byte aligned");
+    st = sd.dtype == FXR_BF16
+             ? launch_attention<__nv_bfloat16>(&sd, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s)
+             : launch_attention<__half>(&sd, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s);
+    if (st != FXR_OK) return st;
+    if (signal) g->epoch += 1;
+    return fxr_restore_rows(&sd, mask, w.idx, w.count, w.save, cache_k, cache_v, stream);
+}
+
+int32_t fxr_head_group_wait(const fxr_head_group* g, void* stream) {
+    if (!g || g->world < 1 || g->world > FXR_MAX_RANKS || g->rank < 0 || g->rank >= g->world)
+        return fail(FXR_ERR_INVALID, "head group not initialised");
+    uint32_t* slots = g->arrive[g->rank];
+    if (!slots) return g->world == 1 ? FXR_OK : fail(FXR_ERR_INVALID, "head group arrive[rank] is null");
+    fxr::ArrivalCounts c{};
+    for (int32_t r = 0; r < g->world; ++r) c.ctas[r] = (uint32_t)g->ctas[r];
+    fxr::arrival_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(slots, c, g->world);
+    FXR_CHECK_LAUNCH("arrival_wait_kernel launch");
+    return FXR_OK;
+}
+
+int32_t fxr_ipc_alloc(size_t bytes, void** ptr, fxr_ipc_handle* handle) {
+    static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(fxr_ipc_handle), "IPC handle size");
+    if (!ptr || !handle || bytes == 0) return fail(FXR_ERR_INVALID, "bad fxr_ipc_alloc arguments");
+    *ptr = nullptr;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return cuda_status(e, "cudaMalloc (IPC buffer)");
+    e = cudaMemset(p, 0, bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_status(e, "cudaIpcGetMemHandle");
+    }
+    std::memcpy(handle->bytes, &h, sizeof(h));
+    *ptr = p;
+    return FXR_OK;
+}
+
+int32_t fxr_ipc_open(const fxr_ipc_handle* handle, void** ptr) {
+    if (!handle || !ptr) return fail(FXR_ERR_INVALID, "bad fxr_ipc_open arguments");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle->bytes, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_status(e, "cudaIpcOpenMemHandle");
+    return FXR_OK;
+}
+
+int32_t fxr_ipc_close(void* ptr) {
+    if (!ptr) return FXR_OK;
+    cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? FXR_OK : cuda_status(e, "cudaIpcCloseMemHandle");
+}
+
+int32_t fxr_ipc_free(void* ptr) {
+    if (!ptr) return FXR_OK;
+    cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? FXR_OK : cuda_status(e, "cudaFree (IPC buffer)");
 }
 
 }  // extern "C"

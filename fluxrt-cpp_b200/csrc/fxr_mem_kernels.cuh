@@ -297,6 +297,41 @@ restore_rows_kernel(const int32_t* __restrict__ mask, const int32_t* __restrict_
 }
 
 // ---------------------------------------------------------------------------------------------
+// Arrival wait of a head-sharded frame. slots[0..8): arrivals from each source GPU (one per
+// attention CTA of that GPU per frame); slots[8]: frames this GPU has waited for, kept on the
+// device so that a CUDA graph of the frame can be replayed. Thread s waits (bounded) until slot s
+// reaches (frames + 1) * ctas[s]; the acquire at system scope makes the O rows that GPU s stored
+// here before its increments visible to the kernels after this one.
+// ---------------------------------------------------------------------------------------------
+struct ArrivalCounts {
+    uint32_t ctas[8];
+};
+
+__global__ void __launch_bounds__(32)
+arrival_wait_kernel(uint32_t* __restrict__ slots, ArrivalCounts c, int32_t n) {
+    const int s = threadIdx.x;
+    uint32_t per_frame = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+        if (k == s) per_frame = c.ctas[k];
+    const uint32_t frame = *reinterpret_cast<volatile uint32_t*>(slots + 8) + 1u;
+    __syncwarp();
+    if (s < n) {
+        const uint32_t target = frame * per_frame;
+        const uint64_t t0 = global_timer_ns();
+        while ((int32_t)(ld_acquire_sys(slots + s) - target) < 0) {
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(&g_error_word, kErrTimeout);
+                break;
+            }
+            __nanosleep(256);
+        }
+    }
+    __syncwarp();
+    if (s == 0) slots[8] = frame;
+}
+
+// ---------------------------------------------------------------------------------------------
 // Byte-exact indexed row copy: gather (dst[m] = src[idx[m]]) or scatter (dst[idx[m]] = src[m]).
 // ---------------------------------------------------------------------------------------------
 template <typename V, bool kScatter>

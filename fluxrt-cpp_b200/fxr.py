@@ -33,8 +33,11 @@ EXPORTED = [
     "fxr_plugin_create", "fxr_plugin_clone", "fxr_plugin_destroy", "fxr_plugin_name",
     "fxr_plugin_version", "fxr_plugin_namespace", "fxr_plugin_fields", "fxr_plugin_output_desc",
     "fxr_plugin_supports", "fxr_plugin_configure", "fxr_plugin_workspace_size",
-    "fxr_plugin_enqueue", "fxr_plugin_cache",
+    "fxr_plugin_enqueue", "fxr_plugin_cache", "fxr_head_group_init", "fxr_frame_forward_heads",
+    "fxr_head_group_wait", "fxr_ipc_alloc", "fxr_ipc_open", "fxr_ipc_close", "fxr_ipc_free",
 ]
+
+FXR_MAX_RANKS = 8
 
 FXR_FIELD_FLOAT32, FXR_FIELD_INT32, FXR_FIELD_CHAR = 1, 3, 6
 FXR_DTYPE_INT32 = 3
@@ -56,6 +59,19 @@ class TensorDesc(ctypes.Structure):
     """Mirror of fxr_tensor_desc (include/fxr_plugin.h)."""
     _fields_ = [("nb_dims", ctypes.c_int32), ("dtype", ctypes.c_int32),
                 ("dims", ctypes.c_int64 * 8)]
+
+
+class HeadGroup(ctypes.Structure):
+    """Mirror of fxr_head_group (include/fxr.h)."""
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("head0", ctypes.c_int32),
+                ("n_heads", ctypes.c_int32), ("ctas", ctypes.c_int32 * 8),
+                ("epoch", ctypes.c_uint32), ("reserved0", ctypes.c_int32),
+                ("out", ctypes.c_void_p * 8), ("arrive", ctypes.c_void_p * 8)]
+
+
+class IpcHandle(ctypes.Structure):
+    """Mirror of fxr_ipc_handle (include/fxr.h)."""
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
 
 
 class FrameDesc(ctypes.Structure):
@@ -117,6 +133,15 @@ def load(path: str | None = None) -> ctypes.CDLL:
     L.fxr_frame_forward.argtypes = [ctypes.POINTER(FrameDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]
     L.fxr_frame_forward_noalloc.argtypes = [ctypes.POINTER(FrameDesc)] + [_vp] * 12
+    _hg = ctypes.POINTER(HeadGroup)
+    L.fxr_head_group_init.argtypes = [_hg, _i32, _i32, _i32, _i32]
+    L.fxr_frame_forward_heads.argtypes = [ctypes.POINTER(FrameDesc), _hg] + [_vp] * 11 + \
+        [ctypes.c_size_t, _vp]
+    L.fxr_head_group_wait.argtypes = [_hg, _vp]
+    L.fxr_ipc_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(_vp), ctypes.POINTER(IpcHandle)]
+    L.fxr_ipc_open.argtypes = [ctypes.POINTER(IpcHandle), ctypes.POINTER(_vp)]
+    L.fxr_ipc_close.argtypes = [_vp]
+    L.fxr_ipc_free.argtypes = [_vp]
     L.fxr_mark_updated.argtypes = [_vp, _vp, _i32, _i32, _vp]
     L.fxr_attention_f32_bhsd.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp]
     _pf = ctypes.POINTER(PluginField)
@@ -439,3 +464,66 @@ def _device_view(ptr: int, shape, typestr: str):
 def _check_plugin(status: int):
     if status != 0:
         raise FxrError(status, load().fxr_last_error_string().decode())
+
+
+# ---- head-sharded frames ------------------------------------------------------------------------
+def head_group(world: int, rank: int, n_heads: int, n_tokens: int) -> HeadGroup:
+    """fxr_head_group_init: this rank's heads and every rank's attention CTA count."""
+    g = HeadGroup()
+    _check(load().fxr_head_group_init(ctypes.byref(g), world, rank, n_heads, n_tokens))
+    return g
+
+
+def frame_forward_heads(cfg: FrameConfig, g: HeadGroup, q, k, v, mask, valid, pos, norm_q, norm_k,
+                        cache_k, cache_v, workspace, stream=None):
+    """One frame of this rank's heads (cfg describes the full frame); see fxr_frame_forward_heads."""
+    d = cfg.desc()
+    _check(load().fxr_frame_forward_heads(ctypes.byref(d), ctypes.byref(g), _ptr(q), _ptr(k),
+                                          _ptr(v), _ptr(mask), _ptr(valid), _ptr(pos),
+                                          _ptr(norm_q), _ptr(norm_k), _ptr(cache_k),
+                                          _ptr(cache_v), _ptr(workspace),
+                                          workspace.numel() * workspace.element_size(),
+                                          _stream(stream)))
+
+
+def head_group_wait(g: HeadGroup, stream=None):
+    _check(load().fxr_head_group_wait(ctypes.byref(g), _stream(stream)))
+
+
+class IpcBuffer:
+    """Zero-filled device memory of this process, shareable with the other processes of the node."""
+
+    def __init__(self, nbytes: int):
+        self.ptr = ctypes.c_void_p()
+        self.handle = IpcHandle()
+        _check(load().fxr_ipc_alloc(nbytes, ctypes.byref(self.ptr), ctypes.byref(self.handle)))
+        self.nbytes = nbytes
+
+    def handle_bytes(self) -> bytes:
+        return bytes(self.handle.bytes)
+
+    def free(self):
+        if self.ptr:
+            _check(load().fxr_ipc_free(self.ptr))
+            self.ptr = ctypes.c_void_p()
+
+
+def ipc_open(handle: bytes) -> int:
+    h = IpcHandle()
+    ctypes.memmove(h.bytes, handle, 64)
+    p = ctypes.c_void_p()
+    _check(load().fxr_ipc_open(ctypes.byref(h), ctypes.byref(p)))
+    return p.value
+
+
+def ipc_close(ptr: int):
+    _check(load().fxr_ipc_close(ptr))
+
+
+def device_view(ptr: int, shape, dtype):
+    """Torch tensor over device memory this library allocated or mapped (no copy)."""
+    import torch
+    code = {torch.bfloat16: "<u2", torch.float16: "<u2", torch.int32: "<i4", torch.uint8: "|u1",
+            torch.float32: "<f4"}[dtype]
+    t = _device_view(ptr, shape, code)
+    return t.view(dtype) if dtype in (torch.bfloat16, torch.float16) else t

@@ -10,7 +10,7 @@
  * Conventions (all entry points):
  *   - plain C: pointers, sizes, an opaque stream handle (a cudaStream_t passed as void*);
  *   - every pointer argument except the descriptor is DEVICE memory owned by the caller;
- *     nothing allocates device memory;
+ *     nothing allocates device memory except fxr_ipc_alloc (set-up of multi-GPU buffers);
  *   - asynchronous on `stream`; nothing synchronises the host, so a sequence of calls can be
  *     captured into a CUDA graph;
  *   - the number of executed tokens M is produced on the device by fxr_mask_compact and read on
@@ -206,6 +206,72 @@ int32_t fxr_frame_forward_noalloc(const fxr_frame_desc* desc,
 /* Device pointers into the workspace (for callers that want idx / count / compact Q). */
 int32_t fxr_workspace_views(const fxr_frame_desc* desc, void* workspace, int32_t** idx,
                             int32_t** count, void** qc, int64_t* ld_qc, void** save);
+
+/* ---- one frame split by attention heads over the GPUs of one node ------------------------------
+ * The reference runs a frame on one GPU. Here a high-resolution frame can be split by heads: rank r
+ * (one process per GPU) owns heads [head0, head0 + n_heads), gathers, normalises and rotates its
+ * heads of every executed token, keeps its heads' K/V cache locally (no cache traffic), and its
+ * attention epilogue stores each finished O row slice into the full-frame output of EVERY rank
+ * through peer mappings (an all-gather fused with the scatter, over NVLink, tile by tile). Each
+ * attention CTA then adds one arrival to slot `rank` of every rank's arrival counters;
+ * fxr_head_group_wait makes a rank's stream wait (bounded) until all ranks' arrivals of the frame
+ * are in, after which its output holds every head. */
+#define FXR_MAX_RANKS 8
+
+typedef struct fxr_head_group {
+    int32_t world;                      /* ranks sharing the frame, 1..FXR_MAX_RANKS */
+    int32_t rank;                       /* this rank */
+    int32_t head0, n_heads;             /* this rank's heads (set by fxr_head_group_init) */
+    int32_t ctas[FXR_MAX_RANKS];        /* attention CTAs (arrivals sent) per frame, per rank */
+    uint32_t epoch;                     /* frames issued by this rank (host count, informational) */
+    int32_t reserved0;
+    void* out[FXR_MAX_RANKS];           /* each rank's full-frame O [n_tokens, ld_out], mapped here */
+    uint32_t* arrive[FXR_MAX_RANKS];    /* each rank's FXR_HEAD_GROUP_SLOTS arrival words,
+                                           zero-initialised, mapped here */
+} fxr_head_group;
+
+/* uint32 words of a rank's arrival area: [0, FXR_MAX_RANKS) arrivals from each rank, then the
+ * number of frames the rank has waited for (kept on the device, so a CUDA graph holding the frame
+ * and its wait can be replayed). 64 bytes. */
+#define FXR_HEAD_GROUP_SLOTS 16
+
+/* Fills world, rank, the contiguous balanced head split (ranks < n_heads % world get one more
+ * head), the per-rank CTA counts for frames of n_tokens tokens (all GPUs are assumed to have this
+ * GPU's SM count), epoch = 0, and clears out[] / arrive[] (the caller sets them). */
+int32_t fxr_head_group_init(fxr_head_group* g, int32_t world, int32_t rank, int32_t n_heads,
+                            int32_t n_tokens);
+
+/* One frame of this rank's heads. desc describes the FULL frame (n_heads = all heads, ld_qkv and
+ * ld_out over all heads); q/k/v are the full-frame inputs; cache_k/cache_v hold this rank's heads
+ * only, [n_tokens, g->n_heads * head_dim] packed. Workspace: fxr_workspace_size(desc) suffices.
+ * Issues compaction, gather/norm/RoPE, attention with the peer stores and arrivals, and the
+ * mask==1 cache restore; it does not wait for the other ranks (fxr_head_group_wait does), so a
+ * single GPU may emulate several ranks by issuing every rank's frame before any rank's wait.
+ * Callers must not let a rank start frame f+1 while another rank still reads frame f's output. */
+int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g,
+                                const void* q, const void* k, const void* v,
+                                int32_t* mask, const uint8_t* valid, const int32_t* pos,
+                                const float* norm_q, const float* norm_k,
+                                void* cache_k, void* cache_v,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* Stream-ordered, bounded (2 s) wait until every rank's arrivals for this rank's next frame are
+ * in (one wait per frame, after the frame); a timeout is reported by fxr_check_device_error
+ * (bit 1). */
+int32_t fxr_head_group_wait(const fxr_head_group* g, void* stream);
+
+/* Device memory shareable between the processes of one node (CUDA IPC), for the output buffers and
+ * arrival counters of a head group. fxr_ipc_alloc zero-fills `bytes` on the current device and
+ * returns a 64-byte handle; fxr_ipc_open maps another process's handle (peer access enabled on
+ * first use); fxr_ipc_close unmaps it; fxr_ipc_free releases an allocation of this process. */
+typedef struct fxr_ipc_handle {
+    unsigned char bytes[64];
+} fxr_ipc_handle;
+
+int32_t fxr_ipc_alloc(size_t bytes, void** ptr, fxr_ipc_handle* handle);
+int32_t fxr_ipc_open(const fxr_ipc_handle* handle, void** ptr);
+int32_t fxr_ipc_close(void* ptr);
+int32_t fxr_ipc_free(void* ptr);
 
 #ifdef __cplusplus
 }
