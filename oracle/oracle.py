@@ -235,3 +235,40 @@ def frame_forward(q, k, v, mask, valid, pos, norm_q, norm_k, cache_k, cache_v, o
                                 theta, eps, scale)
     return {"M": int(M), "mask": mask, "idx": idx[:M].copy(), "qc": qc[:M].copy(),
             "cache_k": ck, "cache_v": cv, "out": o}
+
+
+# ---------------------------------------------------------------------------------------------
+# The reference's own CUDA kernels (oracle/_ref/libfxr_refkernels.so, built from the reference
+# sources by oracle/build_ref.sh). Test infrastructure: a bit-exact cross-check of the copy and
+# cache steps and a timing baseline on the GPU. Arguments are device pointers (ints).
+# ---------------------------------------------------------------------------------------------
+REF_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ref", "libfxr_refkernels.so")
+_ref_lib = None
+
+
+def ref_kernels():
+    """ctypes handle on the reference kernels, or None when they were not built."""
+    global _ref_lib
+    if _ref_lib is not None:
+        return _ref_lib
+    if not os.path.exists(REF_LIB_PATH):
+        return None
+    L = ctypes.CDLL(REF_LIB_PATH)
+    vp, i32 = ctypes.c_void_p, ctypes.c_int32
+    for f in (L.ref_gather_tokens, L.ref_scatter_tokens):
+        f.argtypes = [vp, vp, vp, i32, i32, vp]
+        f.restype = None
+    L.ref_rms_norm.argtypes = [vp, vp, vp, ctypes.c_float, i32, i32, vp]
+    L.ref_rms_norm.restype = None
+    L.ref_attention_fwd.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]
+    L.ref_attention_fwd.restype = None
+    L.ref_cache_create.argtypes = [ctypes.c_int] * 7
+    L.ref_cache_create.restype = vp
+    L.ref_cache_destroy.argtypes = [vp]
+    L.ref_cache_destroy.restype = None
+    L.ref_cache_reset.argtypes = [vp, vp]
+    L.ref_cache_preprocess_mask.argtypes = [vp, vp, vp]
+    L.ref_cache_sync_output.argtypes = [vp, vp, vp, vp]
+    L.ref_cache_sync_kv.argtypes = [vp, vp, vp, vp, ctypes.c_int, ctypes.c_int, vp]
+    _ref_lib = L
+    return L
