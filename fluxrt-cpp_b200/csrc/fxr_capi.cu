@@ -301,12 +301,29 @@ int32_t launch_gather(const fxr_frame_desc* d, const void* q, const void* k, con
     a.n_axes = d->rope_n_axes;
     a.eps = d->eps;
     fill_rope(d, &a.rope);
-    const int64_t groups = (d->n_heads + fxr::kGatherHeadsPerItem - 1) / fxr::kGatherHeadsPerItem;
-    const int64_t need = ((int64_t)d->n_tokens * groups + 7) / 8;
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, (int64_t)sm_count() * fxr::kGatherMinBlocks));
-    cudaError_t e = launch_pdl(fxr::gather_norm_rope_kernel<T>, dim3(grid), dim3(fxr::kGatherThreads), 0,
-                               stream, a);
-    if (e != cudaSuccess) return cuda_status(e, "gather_norm_rope_kernel launch");
+    // bulk-copy pipeline: stages of 3 rows, ~160 KB of rows in flight per SM
+    const size_t row_bytes = (size_t)d->n_heads * d->head_dim * sizeof(T);
+    fxr::BulkLayout lay{};
+    lay.stage_bytes = (uint32_t)align_up(3 * row_bytes, 128);
+    const size_t budget = 160 * 1024;
+    lay.stages = (uint32_t)std::max<size_t>(2, std::min<size_t>(fxr::kBulkMaxStages, budget / lay.stage_bytes));
+    const size_t smem = (size_t)lay.stages * lay.stage_bytes + (size_t)lay.stages * fxr::kBulkInfoWords * 4 +
+                        (size_t)lay.stages * 16;
+    if (smem > 220 * 1024)
+        return fail(FXR_ERR_UNSUPPORTED, "gather rows of %zu bytes do not fit the bulk pipeline", row_bytes);
+    static bool configured[kMaxDevices] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < kMaxDevices && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(fxr::gather_bulk_kernel<T>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gather)");
+        configured[dev] = true;
+    }
+    const int grid = std::max(1, std::min<int>(sm_count(), d->n_tokens));
+    cudaError_t e = launch_pdl(fxr::gather_bulk_kernel<T>, dim3(grid), dim3(fxr::kBulkThreads), smem,
+                               stream, a, lay);
+    if (e != cudaSuccess) return cuda_status(e, "gather_bulk_kernel launch");
     return FXR_OK;
 }
 

@@ -127,6 +127,70 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     return false;
 }
 
+// As mbar_wait, for waits that may last microseconds (a whole DRAM round trip or more): each
+// try_wait may suspend the thread until the phase completes (suspend-time hint 20 us) instead of
+// spinning, which keeps waiting warps off the issue slots of the working ones.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(20000u)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_suspend(uint32_t bar, uint32_t parity, volatile int* abort) {
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait_suspend(bar, parity)) {
+        if (*abort) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(&g_error_word, kErrTimeout);
+            *abort = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+// Bounded wait that ignores the abort flag: after an abort, for an asynchronous copy this thread
+// issued, so that nothing lands in the CTA's shared memory after it exits.
+__device__ __forceinline__ void mbar_wait_drain_bounded(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) break;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Untiled bulk copies (cp.async.bulk): global -> shared completing on an mbarrier, and
+// shared -> global in bulk groups. Addresses 16-byte aligned, sizes multiples of 16 bytes.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                 ::"l"(dst), "r"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// shared-memory sources of every committed bulk store have been read
+__device__ __forceinline__ void bulk_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// every committed bulk store has completed
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// orders this thread's generic-proxy memory accesses before its later async-proxy (bulk) ones
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
+
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor): plain per-CTA tile loads.
 // ---------------------------------------------------------------------------------------------

@@ -1,6 +1,8 @@
 // fxr_mem_kernels.cuh — HBM-bound kernels of the sparse attention path (sm_100a):
 //   compact_kernel           mask preprocess + ascending index compaction (warp ballot + block scan)
-//   gather_norm_rope_kernel  executed-row gather, per-head RMSNorm + multi-axis RoPE, cache-row write
+//   gather_bulk_kernel       executed-row gather (bulk copies through shared memory), per-head
+//                            RMSNorm + multi-axis RoPE, cache-row write
+//   arrival_wait_kernel      end of a head-split frame: waits for every GPU's O rows
 //   restore_rows_kernel      puts back the cache rows of mask==1 tokens after the attention
 //   rows_copy_kernel         byte-exact indexed row gather / scatter
 //   kv_sync_kernel           reference full-frame K/V merge + update
@@ -94,11 +96,10 @@ __global__ void mark_updated_kernel(const int32_t* __restrict__ mask, uint8_t* _
 }
 
 // ---------------------------------------------------------------------------------------------
-// Fused gather + QK-RMSNorm + RoPE + cache-row write.
-// One warp per executed token; the two half-warps take two heads at a time; lane `sub` of a half
-// owns elements [8*sub, 8*sub+8) of a 128-wide head row (one 16-byte vector), so each rotary pair
-// is lane-local and the RMS reduction is a 4-step half-warp shuffle. cos/sin of a token's 4 pairs
-// per lane are computed once and reused for every head of Q and K.
+// Fused gather + QK-RMSNorm + RoPE + cache-row write: shared definitions.
+// Lane `sub` of a half-warp owns elements [8*sub, 8*sub+8) of a 128-wide head row (one 16-byte
+// vector), so each rotary pair is lane-local and the RMS reduction is a 4-step half-warp shuffle;
+// cos/sin of a token's 4 pairs per lane are computed once and reused for every head of Q and K.
 // ---------------------------------------------------------------------------------------------
 constexpr int kHeadDim = 128;
 constexpr int kPairs = kHeadDim / 2;
@@ -128,8 +129,6 @@ struct GatherArgs {
     RopeTable rope;
 };
 
-constexpr int kGatherThreads = 256;
-
 // sin/cos of a rotary angle (|angle| up to a few thousand radians): Cody-Waite reduction by 2*pi
 // with the constant split into an exactly representable head (6.28125) and a tail, then the
 // hardware sine/cosine on [-pi, pi] (absolute error ~4e-7 there).
@@ -140,133 +139,251 @@ __device__ __forceinline__ void rope_sincos(float ang, float* s, float* c) {
     __sincosf(r, s, c);
 }
 
+// RMSNorm + RoPE of one lane's 8 elements of a 128-wide head vector (16 lanes per head; the sum of
+// squares is reduced over the half-warp), stored as 16 bytes. The element products run in packed
+// f32x2 form (two values of a 64-bit register pair per instruction); the rotation stays scalar.
+__device__ __forceinline__ float2 f2mul(float2 a, float2 b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d)
+        : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
+    return *reinterpret_cast<float2*>(&d);
+}
+__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d)
+        : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+          "l"(*reinterpret_cast<uint64_t*>(&c)));
+    return *reinterpret_cast<float2*>(&d);
+}
+
 template <typename T>
-__device__ __forceinline__ void norm_rope_store(const uint4& x, const float* w, float eps,
-                                                const float* cs, const float* sn, T* dst,
-                                                bool active) {
+__device__ __forceinline__ void norm_rope_store_x2(const uint4& x, const float2* w2, float eps,
+                                                   const float* cs, const float* sn, T* dst,
+                                                   bool active) {
     const uint32_t u[4] = {x.x, x.y, x.z, x.w};
-    float f[8];
+    float2 p[4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        const float2 p = StoreT<T>::unpack2(u[t]);
-        f[2 * t] = p.x;
-        f[2 * t + 1] = p.y;
-    }
-    float ss = 0.f;
+    for (int t = 0; t < 4; ++t) p[t] = StoreT<T>::unpack2(u[t]);
+    float2 s2 = f2mul(p[0], p[0]);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+    for (int t = 1; t < 4; ++t) s2 = f2fma(p[t], p[t], s2);
+    float ss = s2.x + s2.y;
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float r = rsqrtf(ss * (1.0f / kHeadDim) + eps);
+    const float2 r2 = make_float2(r, r);
     uint32_t outw[4];
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-        const float a = f[2 * t] * r * w[2 * t];
-        const float b = f[2 * t + 1] * r * w[2 * t + 1];
-        outw[t] = StoreT<T>::pack2(a * cs[t] - b * sn[t], b * cs[t] + a * sn[t]);
+        const float2 ab = f2mul(p[t], f2mul(w2[t], r2));
+        outw[t] = StoreT<T>::pack2(ab.x * cs[t] - ab.y * sn[t], ab.y * cs[t] + ab.x * sn[t]);
     }
     if (active) *reinterpret_cast<uint4*>(dst) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
 }
 
-// Work item = (executed row m, group of up to 8 heads); one warp per item. All 12 of a lane's
-// 16-byte loads (Q, K, V of 4 head pairs) are issued before any arithmetic so that every warp keeps
-// 6 KB in flight; 2 CTAs of 8 warps per SM (measured faster than 4-head items at 3 CTAs per SM).
-constexpr int kGatherHeadsPerItem = 8;
-constexpr int kGatherMinBlocks = 2;
+// ---------------------------------------------------------------------------------------------
+// The gather step as a bulk-copy pipeline. One persistent CTA per SM walks its
+// executed rows r = blockIdx.x, +gridDim.x, ...; a producer warp reads the indices of 32 rows at a
+// time and streams each row's Q, K and V (C contiguous elements each) into a ring of shared-memory
+// stages with cp.async.bulk, then posts the row's token, mode and position ids (second arrival on
+// the stage's full barrier, so that those loads overlap the row copies). Four groups of four
+// consumer warps take every fourth row: in a group, warps 0-1 normalise and rotate the row's Q
+// heads and warps 2-3 its K heads out of shared memory (a half-warp per 128-wide head vector,
+// 16-byte lanes, its heads h, h+4, h+8, ... in one unrolled batch), store Q' compact and K' into
+// the cache row, and one lane writes the V row back to the cache with a bulk store. Rows with
+// mode 1 first copy their old cache rows to the save buffer.
+// ---------------------------------------------------------------------------------------------
+constexpr int kBulkGroupWarps = 4;
+constexpr int kBulkGroups = 4;
+constexpr int kBulkProducerWarp = kBulkGroupWarps * kBulkGroups;
+constexpr int kBulkThreads = (kBulkProducerWarp + 1) * 32;
+constexpr int kBulkMaxStages = 32;
+constexpr int kBulkInfoWords = 8;   // per stage: token, mode, position ids[4], pad
+
+struct BulkLayout {
+    uint32_t stage_bytes;   // 3 rows (Q, K, V) of C elements, 128-byte aligned
+    uint32_t stages;
+};
 
 template <typename T>
-__global__ void __launch_bounds__(kGatherThreads, kGatherMinBlocks)
-gather_norm_rope_kernel(const __grid_constant__ GatherArgs a) {
-    const int lane = threadIdx.x & 31, half = lane >> 4, sub = lane & 15;
-    const int warps_per_cta = kGatherThreads / 32;
+__global__ void __launch_bounds__(kBulkThreads, 1)
+gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
+    extern __shared__ __align__(128) uint8_t bsm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t S = lay.stages;
+    uint8_t* ring = bsm;
+    int32_t* info = reinterpret_cast<int32_t*>(bsm + S * lay.stage_bytes);
+    const uint32_t bars = smem_u32(info + S * kBulkInfoWords);     // full[S], empty[S]
+    __shared__ int abort_flag;
+    auto full = [&](uint32_t st) { return bars + st * 8u; };
+    auto empty = [&](uint32_t st) { return bars + (S + st) * 8u; };
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (uint32_t st = 0; st < S; ++st) {
+            mbar_init(full(st), 2);                  // copies (expect_tx) + bookkeeping
+            mbar_init(empty(st), kBulkGroupWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    volatile int* abort = &abort_flag;
     pdl_launch_dependents();
-    pdl_wait();  // count / idx come from the compaction
+    pdl_wait();  // count / idx / mask come from the compaction
+
     const int32_t M = *a.count;
     const int64_t C = (int64_t)a.n_heads * kHeadDim;
-    const int groups = (a.n_heads + kGatherHeadsPerItem - 1) / kGatherHeadsPerItem;
-    const int64_t items = (int64_t)M * groups;
-    const T* __restrict__ Q = static_cast<const T*>(a.q);
-    const T* __restrict__ K = static_cast<const T*>(a.k);
-    const T* __restrict__ V = static_cast<const T*>(a.v);
-    T* __restrict__ QC = static_cast<T*>(a.qc);
-    T* __restrict__ CK = static_cast<T*>(a.cache_k);
-    T* __restrict__ CV = static_cast<T*>(a.cache_v);
-    T* __restrict__ SV = static_cast<T*>(a.save);
+    const uint32_t row_bytes = (uint32_t)(C * (int64_t)sizeof(T));
+    const int32_t rows_here =
+        M > (int32_t)blockIdx.x ? (M - 1 - (int32_t)blockIdx.x) / (int32_t)gridDim.x + 1 : 0;
 
-    for (int64_t it = (int64_t)blockIdx.x * warps_per_cta + (threadIdx.x >> 5); it < items;
-         it += (int64_t)gridDim.x * warps_per_cta) {
-        const int32_t m = (int32_t)(it / groups);
-        const int h0 = (int)(it - (int64_t)m * groups) * kGatherHeadsPerItem;
-        const int32_t i = __ldg(a.idx + m);
-        if (i < 0 || i >= a.n_tokens) {
-            if (lane == 0) atomicOr(&g_error_word, kErrBounds);
-            continue;
-        }
-        const T* qrow = Q + (int64_t)i * a.ld_qkv + 8 * sub;
-        const T* krow = K + (int64_t)i * a.ld_qkv + 8 * sub;
-        const T* vrow = V + (int64_t)i * a.ld_qkv + 8 * sub;
-        constexpr int kU = kGatherHeadsPerItem / 2;  // head pairs per item
-        uint4 qv[kU], kv[kU], vv[kU];
-        bool act[kU];
+    if (warp == kBulkProducerWarp) {
+        // ---------------- producer warp ----------------
+        bool ok = true;
+        int32_t issued = 0;
+        for (int32_t kb = 0; ok && kb < rows_here; kb += 32) {
+            const int32_t kl = kb + lane;
+            int32_t i = -1;
+            if (kl < rows_here) {
+                i = __ldg(a.idx + (int32_t)blockIdx.x + kl * (int32_t)gridDim.x);
+                if (i < 0 || i >= a.n_tokens) i = -1;
+            }
+            // bookkeeping loads of the 32 rows, in flight while the row copies are issued
+            int32_t mode = 0, p[4] = {0, 0, 0, 0};
+            if (i >= 0) {
+                mode = __ldg(a.mask + i);
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const int h = h0 + 2 * u + half;
-            act[u] = h < a.n_heads;
-            if (act[u]) {
-                qv[u] = __ldg(reinterpret_cast<const uint4*>(qrow + h * kHeadDim));
-                kv[u] = __ldg(reinterpret_cast<const uint4*>(krow + h * kHeadDim));
-                vv[u] = __ldg(reinterpret_cast<const uint4*>(vrow + h * kHeadDim));
-            } else {
-                qv[u] = kv[u] = vv[u] = make_uint4(0, 0, 0, 0);
+                for (int ax = 0; ax < 4; ++ax)
+                    if (ax < a.n_axes) p[ax] = __ldg(a.pos + (int64_t)i * a.n_axes + ax);
+            }
+            const int32_t nb = min(32, rows_here - kb);
+            for (int32_t j = 0; j < nb; ++j) {
+                const int32_t k = kb + j;
+                const uint32_t st = (uint32_t)k % S, use = (uint32_t)k / S;
+                if (use > 0 && !__all_sync(0xffffffffu, mbar_wait_suspend(empty(st), (use - 1) & 1, abort))) {
+                    ok = false;
+                    break;
+                }
+                const int32_t ti = __shfl_sync(0xffffffffu, i, j);
+                if (lane == 0) {
+                    if (ti >= 0) {
+                        const uint32_t dst = smem_u32(ring + st * lay.stage_bytes);
+                        const int64_t off = (int64_t)ti * a.ld_qkv;
+                        mbar_arrive_expect_tx(full(st), 3u * row_bytes);
+                        bulk_load(dst, static_cast<const T*>(a.q) + off, row_bytes, full(st));
+                        bulk_load(dst + row_bytes, static_cast<const T*>(a.k) + off, row_bytes, full(st));
+                        bulk_load(dst + 2 * row_bytes, static_cast<const T*>(a.v) + off, row_bytes, full(st));
+                    } else {
+                        atomicOr(&g_error_word, kErrBounds);
+                        mbar_arrive(full(st));
+                    }
+                }
+                const int32_t tm = __shfl_sync(0xffffffffu, mode, j);
+                int32_t tp[4];
+#pragma unroll
+                for (int ax = 0; ax < 4; ++ax) tp[ax] = __shfl_sync(0xffffffffu, p[ax], j);
+                if (lane == 0) {
+                    int32_t* inf = info + st * kBulkInfoWords;
+                    inf[0] = ti;
+                    inf[1] = tm;
+#pragma unroll
+                    for (int ax = 0; ax < 4; ++ax) inf[2 + ax] = tp[ax];
+                    mbar_arrive(full(st));
+                }
+                __syncwarp();
+                ++issued;
             }
         }
-        const int32_t mode = __ldg(a.mask + i);
-        float cs[4], sn[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            const int j = 4 * sub + t;
-            const int ax = a.rope.axis[j];
-            if (ax < 0) {
-                cs[t] = 1.f;
-                sn[t] = 0.f;
-            } else {
-                const float ang = (float)__ldg(a.pos + (int64_t)i * a.n_axes + ax) * a.rope.omega[j];
-                rope_sincos(ang, &sn[t], &cs[t]);
-            }
+        if (lane == 0 && *abort) {
+            // after an abort: the copies of the last stages may still be in flight
+            for (int32_t k = max(0, issued - (int32_t)S); k < issued; ++k)
+                mbar_wait_drain_bounded(full((uint32_t)k % S), ((uint32_t)k / S) & 1);
         }
-        T* qcrow = QC + (int64_t)m * a.ld_qc + 8 * sub;
-        T* ckrow = CK + (int64_t)i * a.ld_cache + 8 * sub;
-        T* cvrow = CV + (int64_t)i * a.ld_cache + 8 * sub;
-        if (mode == 1 && SV != nullptr) {
-            T* srow = SV + (int64_t)m * 2 * C + 8 * sub;
+    } else {
+        // ---------------- consumer groups ----------------
+        const int grp = warp / kBulkGroupWarps, gw = warp % kBulkGroupWarps;
+        const int half = lane >> 4, sub = lane & 15;
+        const bool isq = gw < kBulkGroupWarps / 2;           // warp-uniform: Q or K heads
+        constexpr int kHeadStride = kBulkGroupWarps;         // half-warps per tensor
+        const int hw0 = (gw % (kBulkGroupWarps / 2)) * 2;     // first head of this warp
+        float2 w2[4];
+        {
+            const float* wsrc = (isq ? a.norm_q : a.norm_k) + 8 * sub;
 #pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int h = h0 + 2 * u + half;
-                if (act[u]) {
-                    *reinterpret_cast<uint4*>(srow + h * kHeadDim) =
-                        *reinterpret_cast<const uint4*>(ckrow + h * kHeadDim);
-                    *reinterpret_cast<uint4*>(srow + C + h * kHeadDim) =
-                        *reinterpret_cast<const uint4*>(cvrow + h * kHeadDim);
+            for (int t = 0; t < 4; ++t) w2[t] = make_float2(__ldg(wsrc + 2 * t), __ldg(wsrc + 2 * t + 1));
+        }
+        T* __restrict__ QC = static_cast<T*>(a.qc);
+        T* __restrict__ CK = static_cast<T*>(a.cache_k);
+        T* __restrict__ CV = static_cast<T*>(a.cache_v);
+        T* __restrict__ SV = static_cast<T*>(a.save);
+        const bool bulk_lane = gw == 0 && lane == 0;
+        const int gtid = gw * 32 + lane;
+        for (int32_t k = grp; k < rows_here; k += kBulkGroups) {
+            const uint32_t st = (uint32_t)k % S, use = (uint32_t)k / S;
+            if (!__all_sync(0xffffffffu, mbar_wait_suspend(full(st), use & 1, abort))) break;
+            const int32_t* inf = info + st * kBulkInfoWords;
+            const int32_t i = inf[0], mode = inf[1];
+            const int32_t r = (int32_t)blockIdx.x + k * (int32_t)gridDim.x;
+            const uint8_t* stage = ring + st * lay.stage_bytes;
+            if (i >= 0) {
+                if (mode == 1 && SV != nullptr) {
+                    // keep the old cache rows: the attention reads the fresh ones, the restore
+                    // puts these back afterwards
+                    const int64_t nvec = C * (int64_t)sizeof(T) / 16;
+                    const uint4* okr = reinterpret_cast<const uint4*>(CK + (int64_t)i * a.ld_cache);
+                    const uint4* ovr = reinterpret_cast<const uint4*>(CV + (int64_t)i * a.ld_cache);
+                    uint4* sk = reinterpret_cast<uint4*>(SV + (int64_t)r * 2 * C);
+                    uint4* svv = reinterpret_cast<uint4*>(SV + (int64_t)r * 2 * C + C);
+                    for (int64_t e = gtid; e < nvec; e += kBulkGroupWarps * 32) {
+                        sk[e] = okr[e];
+                        svv[e] = ovr[e];
+                    }
+                    named_barrier_sync(1 + grp, kBulkGroupWarps * 32);
+                }
+                if (bulk_lane) {
+                    if (mode == 1) fence_proxy_async();   // old V row read before it is overwritten
+                    bulk_store(CV + (int64_t)i * a.ld_cache, smem_u32(stage + 2 * row_bytes), row_bytes);
+                    bulk_commit();
+                }
+                float cs[4], sn[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int j = 4 * sub + t;
+                    const int ax = a.rope.axis[j];
+                    if (ax < 0) {
+                        cs[t] = 1.f;
+                        sn[t] = 0.f;
+                    } else {
+                        rope_sincos((float)inf[2 + ax] * a.rope.omega[j], &sn[t], &cs[t]);
+                    }
+                }
+                // kUnitBatch independent head vectors per half-warp at a time (6 x 4 = 24 heads
+                // of a row): their loads, shuffles and stores interleave
+                constexpr int kUnitBatch = 6;
+                const uint8_t* src = stage + (isq ? 0 : row_bytes) + (size_t)(8 * sub) * sizeof(T);
+                T* dst = (isq ? QC + (int64_t)r * a.ld_qc : CK + (int64_t)i * a.ld_cache) + 8 * sub;
+                // warp-uniform loop bound: both half-warps join every shuffle
+                for (int hw = hw0; hw < a.n_heads; hw += kUnitBatch * kHeadStride) {
+                    const int h0 = hw + half;
+                    uint4 x[kUnitBatch];
+                    bool act[kUnitBatch];
+#pragma unroll
+                    for (int b = 0; b < kUnitBatch; ++b) {
+                        const int h = h0 + b * kHeadStride;
+                        act[b] = h < a.n_heads;
+                        x[b] = act[b] ? *reinterpret_cast<const uint4*>(src + (size_t)h * kHeadDim * sizeof(T))
+                                      : make_uint4(0, 0, 0, 0);
+                    }
+#pragma unroll
+                    for (int b = 0; b < kUnitBatch; ++b)
+                        norm_rope_store_x2<T>(x[b], w2, a.eps, cs, sn,
+                                              dst + (int64_t)(h0 + b * kHeadStride) * kHeadDim, act[b]);
                 }
             }
+            if (bulk_lane) bulk_wait_read_all();   // the V stage has been read by its bulk store
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty(st));
         }
-        float w[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) w[e] = __ldg(a.norm_q + 8 * sub + e);
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            // every lane joins the shuffles; inactive heads compute on zeros and skip the store
-            const int h = h0 + 2 * u + half;
-            norm_rope_store<T>(qv[u], w, a.eps, cs, sn, qcrow + h * kHeadDim, act[u]);
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) w[e] = __ldg(a.norm_k + 8 * sub + e);
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const int h = h0 + 2 * u + half;
-            norm_rope_store<T>(kv[u], w, a.eps, cs, sn, ckrow + h * kHeadDim, act[u]);
-            if (act[u]) *reinterpret_cast<uint4*>(cvrow + h * kHeadDim) = vv[u];
-        }
+        if (bulk_lane) bulk_wait_all();
     }
 }
 
