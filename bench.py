@@ -47,10 +47,11 @@ def parse():
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
-    ap.add_argument("--split", choices=["replicas", "heads"], default=None,
+    ap.add_argument("--split", choices=["replicas", "heads", "heads_nccl"], default=None,
                     help="multi-GPU mode: independent streams per GPU (default except c5) or one "
                          "frame split by heads with the O all-gather fused into the attention "
-                         "epilogue (default for c5)")
+                         "epilogue (default for c5), or the same split with the O exchange as "
+                         "one NCCL all-gather + scatter (heads_nccl)")
     a = ap.parse_args()
     if a.split is None:
         a.split = "heads" if a.config == "c5" else "replicas"
@@ -650,29 +651,45 @@ def run_heads(args):
         if s_ > 0:
             del fr["out"]
         frames.append(fr)
+    nccl = args.split == "heads_nccl"
     out_bytes = N * C * 2
-    buf = fxr.IpcBuffer(out_bytes + 256)
-    out = fxr.device_view(buf.ptr.value, (N, C), dt)
-    out.copy_(frames[0]["out"])
-    mapped = []
-    handles = [buf.handle_bytes()]
-    if world > 1:
-        handles = [None] * world
-        dist.all_gather_object(handles, buf.handle_bytes())
-    for r in range(world):
-        ptr = buf.ptr.value if r == rank else fxr.ipc_open(handles[r])
-        if r != rank:
-            mapped.append(ptr)
-        g.out[r] = ptr
-        g.arrive[r] = ptr + out_bytes
-    ws = [torch.empty(fxr.workspace_size(cfg), dtype=torch.uint8, device=device)
-          for _ in range(n_sets)]
+    mapped, buf, comm = [], None, None
+    if nccl:
+        uid = [fxr.nccl_unique_id() if rank == 0 else None]
+        if world > 1:
+            dist.broadcast_object_list(uid, src=0)
+        comm = fxr.nccl_comm_init(world, rank, uid[0])
+        out = frames[0]["out"]
+        m_cap = max(fr["M"] for fr in frames)
+        ws = [torch.empty(fxr.heads_nccl_workspace_size(cfg, g, m_cap), dtype=torch.uint8,
+                          device=device) for _ in range(n_sets)]
+    else:
+        buf = fxr.IpcBuffer(out_bytes + 256)
+        out = fxr.device_view(buf.ptr.value, (N, C), dt)
+        out.copy_(frames[0]["out"])
+        handles = [buf.handle_bytes()]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, buf.handle_bytes())
+        for r in range(world):
+            ptr = buf.ptr.value if r == rank else fxr.ipc_open(handles[r])
+            if r != rank:
+                mapped.append(ptr)
+            g.out[r] = ptr
+            g.arrive[r] = ptr + out_bytes
+        ws = [torch.empty(fxr.workspace_size(cfg), dtype=torch.uint8, device=device)
+              for _ in range(n_sets)]
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
 
     def frame(i):
         fr = frames[i % n_sets]
+        if nccl:
+            fxr.frame_forward_heads_nccl(cfg, g, comm, m_cap, fr["q"], fr["k"], fr["v"], fr["mask"],
+                                         None, fr["pos"], fr["norm_q"], fr["norm_k"],
+                                         fr["cache_k"], fr["cache_v"], out, ws[i % n_sets])
+            return
         fxr.frame_forward_heads(cfg, g, fr["q"], fr["k"], fr["v"], fr["mask"], None, fr["pos"],
                                 fr["norm_q"], fr["norm_k"], fr["cache_k"], fr["cache_v"],
                                 ws[i % n_sets])
@@ -760,18 +777,19 @@ def run_heads(args):
         "config": {"workload": w.name, "frame_px": w.grid_h * 16, "n_tokens": N,
                    "n_text": w.n_text, "active": w.active, "M_avg": M_avg, "heads": w.n_heads,
                    "heads_per_gpu": [int(x) for x in _heads_split(w.n_heads, world)],
-                   "parallelism": f"heads{world}",
+                   "parallelism": f"heads{world}" + ("-nccl" if nccl else "-p2p"),
                    "l2": f"{n_sets} rotating input sets, cache shards {n_sets * shard_bytes / 2**20:.0f} MiB > L2",
                    "graph": use_graph},
         "roofline": {"bound": "tensor" if t_tensor >= t_link else "nvlink",
-                     "kernel": "fxr::attn::attention_kernel (epilogue stores to every rank)",
+                     "kernel": ("fxr::attn::attention_kernel + NCCL all-gather + heads_scatter_kernel"
+                                if nccl else "fxr::attn::attention_kernel (epilogue stores to every rank)"),
                      "target_us": round(max(t_tensor, t_link) * 1e6, 2),
                      "achieved_frac": round(max(t_tensor, t_link) * 1e3 / ms_per_step, 4),
                      "peak_tensor": pk["bf16_tflops"], "peak_nvlink_gbs": 770.0,
                      "nvlink_bytes_per_rank": nvlink_bytes,
                      "note": "frac = roofline time of one frame / measured frame time (whole frame, 5 kernels)"},
         "e2e": None,
-        "gpu_launches": 5 * args.steps,
+        "gpu_launches": (6 if nccl else 5) * args.steps,   # + NCCL's own kernel per frame when nccl
         "clocks": clk,
     }
     if rank == 0:
@@ -784,7 +802,10 @@ def run_heads(args):
     graphs.clear()
     for p_ in mapped:
         fxr.ipc_close(p_)
-    buf.free()
+    if buf is not None:
+        buf.free()
+    if comm is not None:
+        fxr.nccl_comm_destroy(comm)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -798,7 +819,7 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
-    elif args.split == "heads":
+    elif args.split in ("heads", "heads_nccl"):
         run_heads(args)
     else:
         run_ours(args)

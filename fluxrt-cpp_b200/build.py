@@ -24,7 +24,7 @@ NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompil
 # Translation units: all CUDA kernels live in fxr_capi.cu (one device error word); the C++ mirror
 # of the reference interfaces and the plugin harness are host-only files.
 CU_SOURCES = ["fxr_capi.cu"]
-CPP_SOURCES = ["fxr_reference_api.cpp", "fxr_sparse_attn_plugin.cpp"]
+CPP_SOURCES = ["fxr_reference_api.cpp", "fxr_sparse_attn_plugin.cpp", "fxr_nccl.cpp"]
 
 
 def nvcc() -> str:

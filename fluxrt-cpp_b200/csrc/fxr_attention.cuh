@@ -342,6 +342,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         };
         for (int32_t u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
             const int32_t head = u / n_qt, row0 = (u % n_qt) * kBM;
+            const bool live = row0 + r < M;
             float m_run = -INFINITY, l_run = 0.f;
             for (int32_t j = 0; j < n_steps; ++j, ++s_it) {
                 if (!wwait(bar(kSFull), s_it & 1)) { ok = false; break; }
@@ -374,7 +375,9 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 bool rescale = false;
                 if (j == 0) {
                     m_run = mx;
-                } else if (__any_sync(0xffffffffu, mx > m_run + kRescaleThreshold)) {
+                } else if (__any_sync(0xffffffffu, live && mx > m_run + kRescaleThreshold)) {
+                    // warp-uniform decision over the rows that will be stored: the padding rows of
+                    // the last tile (stale compact-Q rows) must not change how live rows round
                     const float m_new = fmaxf(m_run, mx);
                     alpha = ex2_approx(m_run - m_new);
                     l_run *= alpha;

@@ -789,6 +789,150 @@ int32_t fxr_head_group_wait(const fxr_head_group* g, void* stream) {
     return FXR_OK;
 }
 
+int32_t fxr_internal_nccl_allgather(const void* send, void* recv, size_t bytes, void* comm, void* stream);
+
+struct NcclViews {
+    Views frame;
+    int32_t* iota;
+    void* o_local;
+    void* gathered;
+    size_t row_bytes;
+    size_t total;
+};
+
+static bool group_ok(const fxr_head_group* g) {
+    return g && g->world >= 1 && g->world <= FXR_MAX_RANKS && g->rank >= 0 && g->rank < g->world;
+}
+
+// Heads of every rank (the balanced split of fxr_head_group_init, recomputed from the group's
+// world and the frame's heads).
+static void split_heads(int32_t n_heads, int32_t world, int32_t* head0, int32_t* nh) {
+    const int32_t base = n_heads / world, extra = n_heads % world;
+    int32_t h = 0;
+    for (int32_t r = 0; r < world; ++r) {
+        nh[r] = base + (r < extra ? 1 : 0);
+        head0[r] = h;
+        h += nh[r];
+    }
+}
+
+static NcclViews carve_nccl(const fxr_frame_desc* d, const fxr_head_group* g, int32_t m_cap, void* ws) {
+    NcclViews v{};
+    fxr_frame_desc sd = *d;
+    sd.n_heads = g->n_heads;
+    v.frame = carve(&sd, ws);
+    const int32_t hmax = (d->n_heads + g->world - 1) / g->world;
+    v.row_bytes = (size_t)hmax * d->head_dim * dtype_bytes(d->dtype);
+    char* b = static_cast<char*>(ws);
+    size_t off = v.frame.total;
+    v.iota = reinterpret_cast<int32_t*>(b ? b + off : nullptr);
+    off = align_up(off + (size_t)std::max(d->n_tokens, 1) * sizeof(int32_t), 256);
+    v.o_local = b ? b + off : nullptr;
+    off = align_up(off + (size_t)std::max(m_cap, 1) * v.row_bytes, 256);
+    v.gathered = b ? b + off : nullptr;
+    off = align_up(off + (size_t)g->world * std::max(m_cap, 1) * v.row_bytes, 256);
+    v.total = off;
+    return v;
+}
+
+size_t fxr_heads_nccl_workspace_size(const fxr_frame_desc* desc, const fxr_head_group* g, int32_t m_cap) {
+    if (check_desc(desc, false) != FXR_OK || !group_ok(g) || m_cap < 0) return 0;
+    return carve_nccl(desc, g, m_cap, nullptr).total;
+}
+
+int32_t fxr_allgather_heads(const fxr_frame_desc* desc, const fxr_head_group* g, void* nccl_comm,
+                            const void* o_local, int32_t m_cap, void* gathered, const int32_t* idx,
+                            const int32_t* count, void* out, void* stream) {
+    int32_t st = check_desc(desc, false);
+    if (st != FXR_OK) return st;
+    if (!group_ok(g)) return fail(FXR_ERR_INVALID, "head group not initialised");
+    if (m_cap < 0 || m_cap > desc->n_tokens) return fail(FXR_ERR_INVALID, "m_cap %d outside [0, n_tokens]", m_cap);
+    if (desc->n_tokens == 0 || m_cap == 0) return FXR_OK;
+    if (!nccl_comm || !o_local || !gathered || !idx || !count || !out)
+        return fail(FXR_ERR_INVALID, "null pointer argument");
+    if (!aligned16(o_local) || !aligned16(gathered) || !aligned16(out))
+        return fail(FXR_ERR_INVALID, "buffers must be 16-byte aligned");
+    const int32_t eb = (int32_t)dtype_bytes(desc->dtype);
+    const int32_t hmax = (desc->n_heads + g->world - 1) / g->world;
+    const int64_t row_bytes = (int64_t)hmax * desc->head_dim * eb;
+    if ((st = fxr_internal_nccl_allgather(o_local, gathered, (size_t)m_cap * row_bytes, nccl_comm, stream)) != FXR_OK)
+        return st;
+    fxr::HeadsScatterArgs a{};
+    a.gathered = static_cast<const char*>(gathered);
+    a.idx = idx;
+    a.count = count;
+    a.out = static_cast<char*>(out);
+    a.row_bytes = row_bytes;
+    a.ld_out_bytes = desc->ld_out * eb;
+    a.m_cap = m_cap;
+    a.world = g->world;
+    a.n_tokens = desc->n_tokens;
+    int32_t head0[FXR_MAX_RANKS], nh[FXR_MAX_RANKS];
+    split_heads(desc->n_heads, g->world, head0, nh);
+    for (int32_t r = 0; r < g->world; ++r) {
+        a.col_bytes[r] = head0[r] * desc->head_dim * eb;
+        a.vecs[r] = nh[r] * desc->head_dim * eb / 16;
+    }
+    // a plain launch: the all-gather before it may be a copy rather than a kernel, and programmatic
+    // dependent launch only orders kernel after kernel
+    const int grid = grid_rows((int64_t)m_cap * g->world, 8);
+    fxr::heads_scatter_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    FXR_CHECK_LAUNCH("heads_scatter_kernel launch");
+    return FXR_OK;
+}
+
+int32_t fxr_frame_forward_heads_nccl(const fxr_frame_desc* desc, const fxr_head_group* g,
+                                     void* nccl_comm, int32_t m_cap, const void* q, const void* k,
+                                     const void* v, int32_t* mask, const uint8_t* valid,
+                                     const int32_t* pos, const float* norm_q, const float* norm_k,
+                                     void* cache_k, void* cache_v, void* out, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+    int32_t st = check_desc(desc, true);
+    if (st != FXR_OK) return st;
+    if (!group_ok(g)) return fail(FXR_ERR_INVALID, "head group not initialised");
+    int32_t head0[FXR_MAX_RANKS], nh[FXR_MAX_RANKS];
+    split_heads(desc->n_heads, g->world, head0, nh);
+    if (g->head0 != head0[g->rank] || g->n_heads != nh[g->rank])
+        return fail(FXR_ERR_INVALID, "head group was initialised for another head count");
+    if (m_cap < 0 || m_cap > desc->n_tokens) return fail(FXR_ERR_INVALID, "m_cap %d outside [0, n_tokens]", m_cap);
+    if (desc->n_tokens == 0) return FXR_OK;
+    if (!q || !k || !v || !out || !workspace) return fail(FXR_ERR_INVALID, "null pointer argument");
+    const NcclViews w = carve_nccl(desc, g, m_cap, workspace);
+    if (workspace_bytes < w.total)
+        return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, w.total);
+    if (!aligned16(workspace) || !aligned16(out)) return fail(FXR_ERR_INVALID, "workspace/out must be 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    fxr_frame_desc sd = *desc;
+    sd.n_heads = g->n_heads;
+    sd.ld_cache = (int64_t)g->n_heads * desc->head_dim;
+    const size_t col = (size_t)g->head0 * desc->head_dim * dtype_bytes(desc->dtype);
+    if ((st = fxr_mask_compact(mask, valid, sd.n_tokens, w.frame.idx, w.frame.count, stream)) != FXR_OK) return st;
+    if (g->n_heads > 0) {
+        if ((st = fxr_gather_norm_rope(&sd, static_cast<const char*>(q) + col, static_cast<const char*>(k) + col,
+                                       static_cast<const char*>(v) + col, mask, w.frame.idx, w.frame.count, pos,
+                                       norm_q, norm_k, w.frame.qc, w.frame.ld_qc, cache_k, cache_v, w.frame.save,
+                                       stream)) != FXR_OK)
+            return st;
+        fxr::iota_rows_kernel<<<std::max(1, std::min(grid_rows(desc->n_tokens, 256), sm_count())), 256, 0, s>>>(
+            w.iota, m_cap, desc->n_tokens);
+        FXR_CHECK_LAUNCH("iota_rows_kernel launch");
+        fxr_frame_desc od = sd;                          // compact O output: row m, local heads
+        od.ld_out = (int64_t)((desc->n_heads + g->world - 1) / g->world) * desc->head_dim;
+        if (!cache_k || !cache_v || !aligned16(cache_k) || !aligned16(cache_v))
+            return fail(FXR_ERR_INVALID, "cache must be non-null and 16-byte aligned");
+        OutSet os;
+        os.out[0] = w.o_local;
+        st = od.dtype == FXR_BF16
+                 ? launch_attention<__nv_bfloat16>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, w.iota, os, s)
+                 : launch_attention<__half>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, w.iota, os, s);
+        if (st != FXR_OK) return st;
+        if ((st = fxr_restore_rows(&sd, mask, w.frame.idx, w.frame.count, w.frame.save, cache_k, cache_v, stream)) != FXR_OK)
+            return st;
+    }
+    return fxr_allgather_heads(desc, g, nccl_comm, w.o_local, m_cap, w.gathered, w.frame.idx, w.frame.count,
+                               out, stream);
+}
+
 int32_t fxr_ipc_alloc(size_t bytes, void** ptr, fxr_ipc_handle* handle) {
     static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(fxr_ipc_handle), "IPC handle size");
     if (!ptr || !handle || bytes == 0) return fail(FXR_ERR_INVALID, "bad fxr_ipc_alloc arguments");

@@ -396,8 +396,11 @@ restore_rows_kernel(const int32_t* __restrict__ mask, const int32_t* __restrict_
                     char* __restrict__ cache_k, char* __restrict__ cache_v, int64_t ld_cache_bytes,
                     int32_t row_vec, int32_t n_tokens) {
     const int lane = threadIdx.x & 31;
-    pdl_launch_dependents();
+    // The last kernel of a frame: it lets its successor start only once the attention is over, since
+    // that successor may be code outside this library (a collective, a copy) that reads the frame's
+    // output without a programmatic-dependency wait of its own.
     pdl_wait();  // the attention must have finished reading the cache rows
+    pdl_launch_dependents();
     const int32_t M = *count;
     for (int32_t m = blockIdx.x * 8 + (threadIdx.x >> 5); m < M; m += gridDim.x * 8) {
         const int32_t i = idx[m];
@@ -446,6 +449,53 @@ arrival_wait_kernel(uint32_t* __restrict__ slots, ArrivalCounts c, int32_t n) {
     }
     __syncwarp();
     if (s == 0) slots[8] = frame;
+}
+
+// ---------------------------------------------------------------------------------------------
+// NCCL variant of the head-split frame: compact-row index list for the attention's compact O
+// output (m < m_cap: m; beyond: -1, which the attention skips and reports), and the scatter of the
+// all-gathered compact rows of every rank into the full-frame output.
+// ---------------------------------------------------------------------------------------------
+__global__ void iota_rows_kernel(int32_t* __restrict__ idx, int32_t m_cap, int32_t n) {
+    for (int32_t m = blockIdx.x * blockDim.x + threadIdx.x; m < n; m += gridDim.x * blockDim.x)
+        idx[m] = m < m_cap ? m : -1;
+}
+
+struct HeadsScatterArgs {
+    const char* gathered;      // [world][m_cap][row_bytes]
+    const int32_t* idx;
+    const int32_t* count;
+    char* out;
+    int64_t row_bytes;         // hmax * head_dim * element size
+    int64_t ld_out_bytes;
+    int32_t m_cap, world, n_tokens;
+    int32_t col_bytes[8];      // each rank's first column in bytes (head0 * head_dim * element size)
+    int32_t vecs[8];           // each rank's 16-byte vectors per row (n_heads * head_dim * size / 16)
+};
+
+__global__ void __launch_bounds__(256) heads_scatter_kernel(const __grid_constant__ HeadsScatterArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int32_t M = min(*a.count, a.m_cap);
+    if (blockIdx.x == 0 && threadIdx.x == 0 && *a.count > a.m_cap) atomicOr(&g_error_word, kErrBounds);
+    const int64_t units = (int64_t)M * a.world;
+    for (int64_t u = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); u < units; u += (int64_t)gridDim.x * 8) {
+        const int32_t m = (int32_t)(u / a.world), r = (int32_t)(u % a.world);
+        const int32_t i = a.idx[m];
+        if (i < 0 || i >= a.n_tokens) {
+            if (lane == 0) atomicOr(&g_error_word, kErrBounds);
+            continue;
+        }
+        int32_t col = 0, nv = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (k == r) {
+                col = a.col_bytes[k];
+                nv = a.vecs[k];
+            }
+        const uint4* src = reinterpret_cast<const uint4*>(a.gathered + ((int64_t)r * a.m_cap + m) * a.row_bytes);
+        uint4* dst = reinterpret_cast<uint4*>(a.out + (int64_t)i * a.ld_out_bytes + col);
+        for (int32_t e = lane; e < nv; e += 32) dst[e] = src[e];
+    }
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -35,6 +35,8 @@ EXPORTED = [
     "fxr_plugin_supports", "fxr_plugin_configure", "fxr_plugin_workspace_size",
     "fxr_plugin_enqueue", "fxr_plugin_cache", "fxr_head_group_init", "fxr_frame_forward_heads",
     "fxr_head_group_wait", "fxr_ipc_alloc", "fxr_ipc_open", "fxr_ipc_close", "fxr_ipc_free",
+    "fxr_nccl_unique_id", "fxr_nccl_comm_init", "fxr_nccl_comm_destroy",
+    "fxr_heads_nccl_workspace_size", "fxr_allgather_heads", "fxr_frame_forward_heads_nccl",
 ]
 
 FXR_MAX_RANKS = 8
@@ -138,6 +140,15 @@ def load(path: str | None = None) -> ctypes.CDLL:
     L.fxr_frame_forward_heads.argtypes = [ctypes.POINTER(FrameDesc), _hg] + [_vp] * 11 + \
         [ctypes.c_size_t, _vp]
     L.fxr_head_group_wait.argtypes = [_hg, _vp]
+    L.fxr_nccl_unique_id.argtypes = [ctypes.c_char_p]
+    L.fxr_nccl_comm_init.argtypes = [_i32, _i32, ctypes.c_char_p, ctypes.POINTER(_vp)]
+    L.fxr_nccl_comm_destroy.argtypes = [_vp]
+    L.fxr_heads_nccl_workspace_size.argtypes = [ctypes.POINTER(FrameDesc), _hg, _i32]
+    L.fxr_heads_nccl_workspace_size.restype = ctypes.c_size_t
+    L.fxr_allgather_heads.argtypes = [ctypes.POINTER(FrameDesc), _hg, _vp, _vp, _i32, _vp, _vp, _vp,
+                                      _vp, _vp]
+    L.fxr_frame_forward_heads_nccl.argtypes = [ctypes.POINTER(FrameDesc), _hg, _vp, _i32] + \
+        [_vp] * 12 + [ctypes.c_size_t, _vp]
     L.fxr_ipc_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(_vp), ctypes.POINTER(IpcHandle)]
     L.fxr_ipc_open.argtypes = [ctypes.POINTER(IpcHandle), ctypes.POINTER(_vp)]
     L.fxr_ipc_close.argtypes = [_vp]
@@ -527,3 +538,36 @@ def device_view(ptr: int, shape, dtype):
             torch.float32: "<f4"}[dtype]
     t = _device_view(ptr, shape, code)
     return t.view(dtype) if dtype in (torch.bfloat16, torch.float16) else t
+
+
+# ---- NCCL variant of the head split -----------------------------------------------------------
+def nccl_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(128)
+    _check(load().fxr_nccl_unique_id(buf))
+    return buf.raw
+
+
+def nccl_comm_init(world: int, rank: int, uid: bytes) -> int:
+    comm = ctypes.c_void_p()
+    _check(load().fxr_nccl_comm_init(world, rank, uid, ctypes.byref(comm)))
+    return comm.value
+
+
+def nccl_comm_destroy(comm: int):
+    _check(load().fxr_nccl_comm_destroy(comm))
+
+
+def heads_nccl_workspace_size(cfg: FrameConfig, g: HeadGroup, m_cap: int) -> int:
+    d = cfg.desc()
+    return load().fxr_heads_nccl_workspace_size(ctypes.byref(d), ctypes.byref(g), m_cap)
+
+
+def frame_forward_heads_nccl(cfg: FrameConfig, g: HeadGroup, comm: int, m_cap: int, q, k, v, mask,
+                             valid, pos, norm_q, norm_k, cache_k, cache_v, out, workspace,
+                             stream=None):
+    d = cfg.desc()
+    _check(load().fxr_frame_forward_heads_nccl(
+        ctypes.byref(d), ctypes.byref(g), comm, m_cap, _ptr(q), _ptr(k), _ptr(v), _ptr(mask),
+        _ptr(valid), _ptr(pos), _ptr(norm_q), _ptr(norm_k), _ptr(cache_k), _ptr(cache_v),
+        _ptr(out), _ptr(workspace), workspace.numel() * workspace.element_size(),
+        _stream(stream)))

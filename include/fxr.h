@@ -260,6 +260,38 @@ int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g,
  * (bit 1). */
 int32_t fxr_head_group_wait(const fxr_head_group* g, void* stream);
 
+/* The same split with the O exchange as one NCCL all-gather instead of peer stores (the
+ * collective-library baseline of the fused path). Each rank's attention writes compact O rows of
+ * its heads, [m_cap, hmax * head_dim] (hmax = ceil(heads / world)); fxr_allgather_heads gathers
+ * them from every rank over `nccl_comm` (an ncclComm_t of the group's ranks, rank order = g->rank)
+ * and scatters them into the full-frame output rows out[idx[m]]. m_cap is a host-side upper bound
+ * of the executed-token count (n_tokens is always safe; a tighter bound moves fewer bytes); a frame
+ * with more executed tokens sets the device error word (bit 2) and leaves the excess rows out.
+ * NCCL is resolved at run time (the libnccl.so.2 already in the process, else the loader's). */
+int32_t fxr_nccl_unique_id(unsigned char id_out[128]);
+int32_t fxr_nccl_comm_init(int32_t world, int32_t rank, const unsigned char id[128], void** comm);
+int32_t fxr_nccl_comm_destroy(void* comm);
+
+/* Workspace of fxr_frame_forward_heads_nccl (frame workspace + compact O + gather buffer). */
+size_t fxr_heads_nccl_workspace_size(const fxr_frame_desc* desc, const fxr_head_group* g,
+                                     int32_t m_cap);
+
+/* All-gather of compact O rows + scatter into out. o_local: [m_cap, hmax*head_dim] of this rank;
+ * gathered: [world, m_cap, hmax*head_dim]; idx/count: the frame's compaction; out: full frame. */
+int32_t fxr_allgather_heads(const fxr_frame_desc* desc, const fxr_head_group* g, void* nccl_comm,
+                            const void* o_local, int32_t m_cap, void* gathered,
+                            const int32_t* idx, const int32_t* count, void* out, void* stream);
+
+/* fxr_frame_forward_heads with the NCCL exchange: out is this rank's full-frame output; g->out and
+ * g->arrive are not used. Returns when the all-gather and scatter are enqueued on `stream`. */
+int32_t fxr_frame_forward_heads_nccl(const fxr_frame_desc* desc, const fxr_head_group* g,
+                                     void* nccl_comm, int32_t m_cap,
+                                     const void* q, const void* k, const void* v,
+                                     int32_t* mask, const uint8_t* valid, const int32_t* pos,
+                                     const float* norm_q, const float* norm_k,
+                                     void* cache_k, void* cache_v, void* out,
+                                     void* workspace, size_t workspace_bytes, void* stream);
+
 /* Device memory shareable between the processes of one node (CUDA IPC), for the output buffers and
  * arrival counters of a head group. fxr_ipc_alloc zero-fills `bytes` on the current device and
  * returns a 64-byte handle; fxr_ipc_open maps another process's handle (peer access enabled on

@@ -396,3 +396,22 @@ def test_mark_updated_bit_exact(cuda):
     exp = valid.copy()
     exp[T:][mask[T:] == 2] = 1
     assert np.array_equal(host(dv), exp)
+
+
+@pytest.mark.parametrize("fill", [0x00, 0x7F, 0xFF])
+def test_frame_output_independent_of_stale_workspace(cuda, fill):
+    """The padding rows of the last query tile read stale compact-Q rows of the workspace; they must
+    not change a single bit of the stored rows (0x7F7F.. = large finite bf16, 0xFFFF.. = NaN)."""
+    w = small(W.C2, 6)
+    fr = W.make_frame(w, seed=91)
+    cfg = cfg_of(w)
+    outs = []
+    for f in (0x00, fill):
+        t = _frame_tensors(w, fr)
+        ws = torch.full((fxr.workspace_size(cfg),), f, dtype=torch.uint8, device="cuda")
+        fxr.frame_forward(cfg, t["q"], t["k"], t["v"], t["mask"], None, t["pos"], t["norm_q"],
+                          t["norm_k"], t["cache_k"], t["cache_v"], t["out"], ws)
+        sync_ok()
+        outs.append(t)
+    for k in ("out", "cache_k", "cache_v"):
+        assert torch.equal(outs[0][k], outs[1][k]), k

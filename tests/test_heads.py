@@ -48,6 +48,22 @@ def test_head_group_rejects_bad_arguments():
     assert st == fxr.FXR_ERR_INVALID and b"out[0]" in L.fxr_last_error_string()
 
 
+def test_nccl_variant_workspace_and_argument_checks():
+    L = fxr.load()
+    cfg = fxr.FrameConfig(n_tokens=16896, n_text=512)
+    g = fxr.head_group(8, 3, 24, 16896)
+    frame = fxr.workspace_size(fxr.FrameConfig(n_tokens=16896, n_text=512, n_heads=3))
+    ws = fxr.heads_nccl_workspace_size(cfg, g, 3000)
+    # shard frame workspace + iota + compact O [3000, 3*128] + gathered [8, 3000, 3*128]
+    assert ws >= frame + 16896 * 4 + 9 * 3000 * 384 * 2
+    assert fxr.heads_nccl_workspace_size(cfg, g, -1) == 0
+    st = L.fxr_frame_forward_heads_nccl(cfg.desc(), g, None, 16897, *([None] * 12), 0, None)
+    assert st == fxr.FXR_ERR_INVALID and b"m_cap" in L.fxr_last_error_string()
+    g2 = fxr.head_group(8, 3, 16, 16896)                       # split of another head count
+    st = L.fxr_frame_forward_heads_nccl(cfg.desc(), g2, None, 100, *([None] * 12), 0, None)
+    assert st == fxr.FXR_ERR_INVALID
+
+
 def _shard_worker(rank, world, port, n_heads, result_path):
     import torch
     import torch.distributed as dist
@@ -163,6 +179,38 @@ def test_heads_emulated_on_one_gpu_match_the_frame(cuda, world, dtype):
             assert slots[r, :world].tolist() == expect and slots[r, 8].item() == f + 1
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("m_cap_kind", ["exact", "n_tokens"])
+def test_nccl_variant_single_rank_matches_the_frame(cuda, m_cap_kind):
+    import torch
+    w = W.Workload("c2_h6", 64, 64, 512, 6, 128, "bf16", 0.25, "bernoulli", (16, 56, 56), 10000.0)
+    cfg = fxr.FrameConfig(n_tokens=w.n_tokens, n_text=w.n_text, n_heads=w.n_heads, dtype="bf16",
+                          rope_axes=w.rope_axes, rope_theta=w.rope_theta)
+    fr = W.make_frame(w, seed=71)
+    a, b = _frame_tensors(w, fr), _frame_tensors(w, fr)
+    M = int((fr["mask"] != 0).sum())
+    m_cap = M if m_cap_kind == "exact" else w.n_tokens
+    g = fxr.head_group(1, 0, w.n_heads, w.n_tokens)
+    comm = fxr.nccl_comm_init(1, 0, fxr.nccl_unique_id())
+    try:
+        ws = torch.empty(fxr.heads_nccl_workspace_size(cfg, g, m_cap), dtype=torch.uint8,
+                         device="cuda")
+        fxr.frame_forward_heads_nccl(cfg, g, comm, m_cap, a["q"], a["k"], a["v"], a["mask"], None,
+                                     a["pos"], a["norm_q"], a["norm_k"], a["cache_k"],
+                                     a["cache_v"], a["out"], ws)
+        wsf = torch.empty(fxr.workspace_size(cfg), dtype=torch.uint8, device="cuda")
+        fxr.frame_forward(cfg, b["q"], b["k"], b["v"], b["mask"], None, b["pos"], b["norm_q"],
+                          b["norm_k"], b["cache_k"], b["cache_v"], b["out"], wsf)
+        torch.cuda.synchronize()
+        assert fxr.check_device_error() == 0
+        for key in ("out", "cache_k", "cache_v", "mask"):
+            bad = (a[key] != b[key]).reshape(a[key].shape[0], -1).any(dim=1).nonzero().flatten()
+            assert bad.numel() == 0, (key, bad.numel(), bad[:8].tolist(), M)
+    finally:
+        torch.cuda.synchronize()
+        fxr.nccl_comm_destroy(comm)
+
+
 def _two_gpu_worker(rank, world, port, result_path):
     import torch
     import torch.distributed as dist
@@ -210,6 +258,26 @@ def _two_gpu_worker(rank, world, port, result_path):
         torch.cuda.synchronize()
         ok = (err == 0 and torch.equal(got, t["out"]) and torch.equal(ck, t["cache_k"][:, c0:c1])
               and torch.equal(cv, t["cache_v"][:, c0:c1]))
+        # the same frame with the O exchange as one NCCL all-gather
+        uid = [fxr.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = fxr.nccl_comm_init(world, rank, uid[0])
+        try:
+            t2 = _frame_tensors(w, fr)
+            ck2 = t2["cache_k"][:, c0:c1].contiguous()
+            cv2 = t2["cache_v"][:, c0:c1].contiguous()
+            M = int((fr["mask"] != 0).sum())
+            wsn = torch.empty(fxr.heads_nccl_workspace_size(cfg, g, M), dtype=torch.uint8,
+                              device="cuda")
+            fxr.frame_forward_heads_nccl(cfg, g, comm, M, t2["q"], t2["k"], t2["v"], t2["mask"],
+                                         None, t2["pos"], t2["norm_q"], t2["norm_k"], ck2, cv2,
+                                         t2["out"], wsn)
+            torch.cuda.synchronize()
+            ok = ok and fxr.check_device_error() == 0 and torch.equal(t2["out"], t["out"]) and \
+                torch.equal(ck2, ck)
+        finally:
+            torch.cuda.synchronize()
+            fxr.nccl_comm_destroy(comm)
         oks = [None] * world
         dist.all_gather_object(oks, bool(ok))
         if rank == 0:
