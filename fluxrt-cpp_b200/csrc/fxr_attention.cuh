@@ -57,7 +57,8 @@ constexpr uint32_t kTileBytes = 2 * kHalfBytes; // 128 x 128 16-bit tile
 constexpr uint32_t kSmemQ = 0;
 constexpr uint32_t kSmemRing = kTileBytes;
 constexpr uint32_t kSmemX = kSmemRing + kSlots * kTileBytes;  // exchange [2 buf][4 wg][128 rows]
-constexpr uint32_t kSmemBar = kSmemX + 2 * 4 * 128 * 4;
+constexpr uint32_t kSmemRowIdx = kSmemX + 2 * 4 * 128 * 4;   // [softmax thread] output row of its item
+constexpr uint32_t kSmemBar = kSmemRowIdx + kSoftmaxThreads * 4;
 constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;       // barriers + alignment slack
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
@@ -86,6 +87,19 @@ static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 constexpr int kMaxOut = 8;   // destinations of a head-sharded frame: one per GPU of the group
 
+// Key-range split of a work unit across CTAs (when there are too few units to fill the GPU): each
+// part writes its partial O (unnormalised, fp32) with its row maxima and sums to a scratch slot; per
+// (unit, warp) portion an arrival counter elects the last-arriving part's warp, which combines all
+// parts of its 32 rows x 32 columns and stores them. No CTA waits for another.
+constexpr int kMaxSplits = 4;
+// Costs in 256-key steps (measured: ~2.4 us per step at c2): the fixed cost of a work item (first
+// Q tile, pipeline ramp, epilogue) and the extra cost of a split item (partial write, arrival
+// counter, combine through L2).
+constexpr float kItemOverheadSteps = 2.0f;
+constexpr float kSplitOverheadSteps = 4.0f;
+constexpr int kSplitSlotFloats = 128 * 128 + 2 * 4 * 128;   // O [128][128], m [4][128], l [4][128]
+constexpr int kSplitPortions = 16;                   // softmax warps: counters per unit
+
 struct Params {
     const int32_t* count;
     const int32_t* idx;
@@ -97,7 +111,30 @@ struct Params {
     int32_t src_rank;   // arrival slot this GPU increments at every destination
     void* out[kMaxOut];          // O row bases (this GPU's buffer and peers' mapped buffers)
     uint32_t* arrive[kMaxOut];   // arrival slots of each destination; null: no signalling
+    float* split_scratch;        // [split_slots][kSplitSlotFloats]
+    int32_t* split_cnt;          // [split_slots][kSplitPortions], zero at launch
+    int32_t split_slots;         // 0: never split
 };
+
+// Parts per unit: the shortest estimated kernel time (CTA rounds x steps per item + overheads);
+// the same on every role of every CTA (a function of M, the grid and the scratch only). It splits
+// only when the units leave SMs idle for long: a 2048^2 frame's 72 units of 66 steps per GPU of an
+// 8-way head split, not the 1024^2 frame's 288 units of 18 steps.
+__device__ __forceinline__ int32_t choose_splits(int32_t n_units, int32_t grid, int32_t n_steps,
+                                                 int32_t slots) {
+    int32_t best = 1;
+    float best_cost = (float)((n_units + grid - 1) / grid) * ((float)n_steps + kItemOverheadSteps);
+    for (int32_t sp = 2; sp <= kMaxSplits; ++sp) {
+        if (sp > n_steps || n_units * sp > slots) break;
+        const float cost = (float)((n_units * sp + grid - 1) / grid) *
+                           ((float)n_steps / (float)sp + kItemOverheadSteps + kSplitOverheadSteps);
+        if (cost < best_cost) {
+            best = sp;
+            best_cost = cost;
+        }
+    }
+    return best;
+}
 
 __device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
     // After an abort only: waits (bounded, ignoring the abort flag) for an asynchronous operation
@@ -145,10 +182,66 @@ __device__ __forceinline__ float2 ex2_poly2(float2 x) {
                        __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
 }
 
+// End of a split unit for the part that arrived last at a (unit, warp) portion: every part (this one
+// included) is read back from its slot and combined in part order — the result does not depend on
+// which CTA arrived last — then normalised and stored like the unsplit epilogue. Out of line, so
+// that its registers do not weigh on the softmax loop of the kernel.
 template <typename T>
+__device__ __noinline__ void split_combine_store(const Params& p, const float* slots, int32_t n_split,
+                                                 int r, int wg, int32_t orow, int32_t head) {
+    float m_all = -INFINITY;
+    for (int32_t q = 0; q < n_split; ++q)
+        m_all = fmaxf(m_all, slots[q * kSplitSlotFloats + kBM * kD + wg * kBM + r]);
+    float acc[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) acc[k] = 0.f;
+    float l_tot = 0.f;
+    for (int32_t q = 0; q < n_split; ++q) {
+        const float* sq = slots + q * kSplitSlotFloats;
+        const float a = ex2_approx(sq[kBM * kD + wg * kBM + r] - m_all);
+        l_tot += a * sq[kBM * kD + 4 * kBM + wg * kBM + r];
+        const float4* oq = reinterpret_cast<const float4*>(sq + r * kD + wg * 32);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float4 x = oq[k];
+            acc[4 * k] += a * x.x;
+            acc[4 * k + 1] += a * x.y;
+            acc[4 * k + 2] += a * x.z;
+            acc[4 * k + 3] += a * x.w;
+        }
+    }
+    if (orow < 0) return;                       // a padding row of the last tile
+    if (orow >= p.n_tokens) {
+        atomicOr(&g_error_word, kErrBounds);
+        return;
+    }
+    const float inv = 1.0f / l_tot;
+    const int64_t off = (int64_t)orow * p.ld_out + (int64_t)head * kD + wg * 32;
+    uint4 v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        v[k].x = StoreT<T>::pack2(acc[8 * k + 0] * inv, acc[8 * k + 1] * inv);
+        v[k].y = StoreT<T>::pack2(acc[8 * k + 2] * inv, acc[8 * k + 3] * inv);
+        v[k].z = StoreT<T>::pack2(acc[8 * k + 4] * inv, acc[8 * k + 5] * inv);
+        v[k].w = StoreT<T>::pack2(acc[8 * k + 6] * inv, acc[8 * k + 7] * inv);
+    }
+#pragma unroll
+    for (int t = 0; t < kMaxOut; ++t) {
+        if (t < p.n_out) {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.out[t]) + off);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) dst[k] = v[k];
+        }
+    }
+}
+
+// kSplit: the instantiation that may split key ranges (launched for few heads per launch, where
+// the units cannot fill the GPU); without it the split code is compiled out, since its mere presence
+// costs the softmax loop ~10 % (register allocation).
+template <typename T, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
 attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                 const __grid_constant__ CUtensorMap tmV, const Params p) {
+                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -201,6 +294,8 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     const int32_t n_qt = (M + kBM - 1) / kBM;
     const int32_t n_units = n_qt * p.n_heads;
     const int32_t n_steps = (p.n_tokens + kStepN - 1) / kStepN;
+    const int32_t n_split = kSplit ? choose_splits(n_units, (int32_t)gridDim.x, n_steps, p.split_slots) : 1;
+    const int32_t n_items = n_units * n_split;   // item w: unit w / n_split, key part w % n_split
 
     if (warp == kProducerWarp) {
         if (lane == 0) {
@@ -219,19 +314,21 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 ++it;
                 return true;
             };
-            for (int32_t u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+            for (int32_t w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+                const int32_t u = w / n_split, part = w - u * n_split;
                 const int32_t head = u / n_qt, row0 = (u % n_qt) * kBM;
+                const int32_t s0 = part * n_steps / n_split, s1 = (part + 1) * n_steps / n_split;
                 if (q_it > 0 && !mbar_wait(bar(kQEmpty), (q_it - 1) & 1, abort)) { ok = false; break; }
                 mbar_arrive_expect_tx(bar(kQFull), kTileBytes);
                 tma_load_2d(base + kSmemQ, &tmQ, bar(kQFull), head * kD, row0);
                 tma_load_2d(base + kSmemQ + kHalfBytes, &tmQ, bar(kQFull), head * kD + 64, row0);
                 ++q_it;
-                ok = load(&tmK, head, 0) && load(&tmK, head, kSubN);
-                for (int32_t j = 1; ok && j < n_steps; ++j)
+                ok = load(&tmK, head, s0 * kStepN) && load(&tmK, head, s0 * kStepN + kSubN);
+                for (int32_t j = s0 + 1; ok && j < s1; ++j)
                     ok = load(&tmK, head, j * kStepN) && load(&tmK, head, j * kStepN + kSubN) &&
                          load(&tmV, head, (j - 1) * kStepN) && load(&tmV, head, (j - 1) * kStepN + kSubN);
-                ok = ok && load(&tmV, head, (n_steps - 1) * kStepN) &&
-                     load(&tmV, head, (n_steps - 1) * kStepN + kSubN);
+                ok = ok && load(&tmV, head, (s1 - 1) * kStepN) &&
+                     load(&tmV, head, (s1 - 1) * kStepN + kSubN);
             }
             if (*abort) {
                 if (q_it > 0) mbar_wait_drain(bar(kQFull), (q_it - 1) & 1);
@@ -259,9 +356,9 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 ++it;
             };
             // O (+)= P V for one step (A = P from tensor memory, B = V sub-tiles, MN-major)
-            auto pv = [&](int32_t jj, uint32_t gg) -> bool {
+            auto pv = [&](int32_t jj, uint32_t gg, int32_t first) -> bool {
                 if (!mbar_wait(bar(kPFull), gg & 1, abort)) return false;
-                if (jj == 0 && units_done > 0 && !mbar_wait(bar(kOFree), (units_done - 1) & 1, abort))
+                if (jj == first && units_done > 0 && !mbar_wait(bar(kOFree), (units_done - 1) & 1, abort))
                     return false;
                 tc_fence_after();
                 for (int h = 0; h < 2; ++h) {
@@ -271,17 +368,19 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                     for (int k = 0; k < kSubN / 16; ++k) {
                         const uint64_t bdesc = smem_desc_sw128(sV + k * 2048u, kHalfBytes, 1024);
                         umma_ts(tmem + kColO, tmem + kColP + (h * 8 + k) * 8u, bdesc, idesc_pv,
-                                (jj > 0 || h > 0 || k > 0) ? 1u : 0u);
+                                (jj > first || h > 0 || k > 0) ? 1u : 0u);
                     }
                     release_tile();
                 }
                 umma_commit(bar(kPFree));
                 return true;
             };
-            for (int32_t u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+            for (int32_t w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+                const int32_t part = w % n_split;
+                const int32_t s0 = part * n_steps / n_split, s1 = (part + 1) * n_steps / n_split;
                 if (!mbar_wait(bar(kQFull), q_it & 1, abort)) { ok = false; break; }
                 ++q_it;
-                for (int32_t j = 0; j < n_steps; ++j, ++g) {
+                for (int32_t j = s0; j < s1; ++j, ++g) {
                     // S(j) = Q K(2j..2j+1)^T once every softmax thread has loaded S(j-1)
                     if (g > 0 && !mbar_wait(bar(kSFree), (g - 1) & 1, abort)) { ok = false; break; }
                     for (int h = 0; h < 2; ++h) {
@@ -298,10 +397,10 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                     }
                     if (!ok) break;
                     umma_commit(bar(kSFull));
-                    if (j == n_steps - 1) umma_commit(bar(kQEmpty));
-                    if (j > 0 && !pv(j - 1, g - 1)) { ok = false; break; }
+                    if (j == s1 - 1) umma_commit(bar(kQEmpty));
+                    if (j > s0 && !pv(j - 1, g - 1, s0)) { ok = false; break; }
                 }
-                if (!ok || !pv(n_steps - 1, g - 1)) { ok = false; break; }
+                if (!ok || !pv(s1 - 1, g - 1, s0)) { ok = false; break; }
                 ++units_done;
             }
             if (*abort && issued) {
@@ -340,11 +439,17 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             for (int k = 0; k < 4; ++k) o4[k] = xb[k * 128 + r];
             return true;
         };
-        for (int32_t u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+        for (int32_t w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+            const int32_t u = w / n_split, part = w - u * n_split;
             const int32_t head = u / n_qt, row0 = (u % n_qt) * kBM;
+            const int32_t s0 = part * n_steps / n_split, s1 = (part + 1) * n_steps / n_split;
             const bool live = row0 + r < M;
+            // the output row of this thread, loaded now (kept in shared memory: the step loop has
+            // no register to spare) so that the epilogue does not wait on a global load
+            int32_t* orow_slot = reinterpret_cast<int32_t*>(gbase + kSmemRowIdx) + threadIdx.x;
+            *orow_slot = live ? __ldg(p.idx + row0 + r) : -1;
             float m_run = -INFINITY, l_run = 0.f;
-            for (int32_t j = 0; j < n_steps; ++j, ++s_it) {
+            for (int32_t j = s0; j < s1; ++j, ++s_it) {
                 if (!wwait(bar(kSFull), s_it & 1)) { ok = false; break; }
                 tc_fence_after();
                 uint32_t s[64];
@@ -373,7 +478,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 const float mx = fmaxf(fmaxf(pm4[0], pm4[1]), fmaxf(pm4[2], pm4[3])) * c;
                 float alpha = 1.f;
                 bool rescale = false;
-                if (j == 0) {
+                if (j == s0) {
                     m_run = mx;
                 } else if (__any_sync(0xffffffffu, live && mx > m_run + kRescaleThreshold)) {
                     // warp-uniform decision over the rows that will be stored: the padding rows of
@@ -422,7 +527,10 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 mbar_arrive(bar(kPFull));
             }
             if (!ok) break;
-            // epilogue: O is final once the last PV finished
+            // epilogue: the row sums are exchanged while the last PV runs; O is final once it is done
+            float l4[4];
+            if (!exchange(l_run, l4)) { ok = false; break; }
+            float l_tot = (l4[0] + l4[1]) + (l4[2] + l4[3]);
             if (!wwait(bar(kPFree), (s_it - 1) & 1)) { ok = false; break; }
             tc_fence_after();
             uint32_t o[32];
@@ -430,12 +538,32 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             tc_fence_before();
             mbar_arrive(bar(kOFree));
             ++units_done;
-            float l4[4];
-            if (!exchange(l_run, l4)) { ok = false; break; }
-            const float l_tot = (l4[0] + l4[1]) + (l4[2] + l4[3]);
             const int32_t m = row0 + r;
+            if (n_split > 1) {
+                // partial of this part: O (32 columns of row r), row maximum and sum
+                float* slot = p.split_scratch + (size_t)(u * n_split + part) * kSplitSlotFloats;
+                float4* od = reinterpret_cast<float4*>(slot + r * kD + wg * 32);
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    od[k] = make_float4(__uint_as_float(o[4 * k]), __uint_as_float(o[4 * k + 1]),
+                                        __uint_as_float(o[4 * k + 2]), __uint_as_float(o[4 * k + 3]));
+                slot[kBM * kD + wg * kBM + r] = m_run;
+                slot[kBM * kD + 4 * kBM + wg * kBM + r] = l_tot;
+                __threadfence();
+                __syncwarp();
+                int32_t prev = 0;
+                if (lane == 0) prev = atomicAdd(p.split_cnt + u * kSplitPortions + warp, 1);
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                if (prev == n_split - 1) {   // the last part to arrive combines this portion
+                    if (lane == 0) p.split_cnt[u * kSplitPortions + warp] = 0;   // for the next launch
+                    __threadfence();
+                    split_combine_store<T>(p, p.split_scratch + (size_t)u * n_split * kSplitSlotFloats,
+                                           n_split, r, wg, m < M ? *orow_slot : -1, head);
+                }
+                continue;
+            }
             if (m < M) {
-                const int32_t i = p.idx[m];
+                const int32_t i = *orow_slot;
                 if (i >= 0 && i < p.n_tokens) {
                     const float inv = 1.0f / l_tot;
                     const int64_t off = (int64_t)i * p.ld_out + (int64_t)head * kD + wg * 32;

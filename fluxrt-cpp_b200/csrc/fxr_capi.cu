@@ -211,6 +211,38 @@ Views carve(const fxr_frame_desc* d, void* ws) {
     return v;
 }
 
+// Optional key-range split scratch after a frame's workspace: per slot 16 arrival counters and one
+// partial-result slot of the attention. A workspace of at least the base size works without it;
+// fxr_workspace_size includes room for kSplitSlotsPerSm slots per SM.
+constexpr int kSplitSlotsPerSm = 4;
+constexpr int kSplitMaxHeads = 8;   // launches with at most this many heads may split key ranges
+constexpr size_t kSplitSlotBytes = (size_t)fxr::attn::kSplitSlotFloats * sizeof(float);
+constexpr size_t kSplitCntBytes = (size_t)fxr::attn::kSplitPortions * sizeof(int32_t);
+
+struct SplitArea {
+    int32_t* cnt = nullptr;
+    float* scratch = nullptr;
+    int32_t slots = 0;
+};
+
+size_t split_bytes(int32_t slots) {
+    return align_up((size_t)slots * kSplitCntBytes, 256) + (size_t)slots * kSplitSlotBytes;
+}
+
+SplitArea split_area(size_t base, void* ws, size_t ws_bytes) {
+    SplitArea a;
+    if (!ws || ws_bytes <= base) return a;
+    const int32_t max_slots = kSplitSlotsPerSm * sm_count();
+    int32_t slots = (int32_t)std::min<size_t>(max_slots, (ws_bytes - base) / (kSplitSlotBytes + kSplitCntBytes));
+    while (slots > 0 && split_bytes(slots) > ws_bytes - base) --slots;
+    if (slots <= 0) return a;
+    char* b = static_cast<char*>(ws) + base;
+    a.cnt = reinterpret_cast<int32_t*>(b);
+    a.scratch = reinterpret_cast<float*>(b + align_up((size_t)slots * kSplitCntBytes, 256));
+    a.slots = slots;
+    return a;
+}
+
 int grid_rows(int64_t rows, int rows_per_cta) {
     const int64_t need = (rows + rows_per_cta - 1) / rows_per_cta;
     const int64_t cap = (int64_t)sm_count() * 8;
@@ -224,6 +256,7 @@ struct OutSet {
     int32_t src_rank = 0;
     void* out[fxr::attn::kMaxOut] = {};
     uint32_t* arrive[fxr::attn::kMaxOut] = {};
+    SplitArea split;   // key-range split scratch (none: never split)
 };
 
 int64_t attention_ctas(int64_t n_tokens, int64_t n_heads) {
@@ -240,9 +273,12 @@ int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < kMaxDevices && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(fxr::attn::attention_kernel<T>,
+        cudaError_t e = cudaFuncSetAttribute(fxr::attn::attention_kernel<T, false>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)fxr::attn::kSmemBytes);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(fxr::attn::attention_kernel<T, true>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fxr::attn::kSmemBytes);
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
         configured[dev] = true;
     }
@@ -262,14 +298,22 @@ int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
         p.out[t] = os.out[t];
         p.arrive[t] = os.arrive[t];
     }
+    p.split_scratch = os.split.scratch;
+    p.split_cnt = os.split.cnt;
+    p.split_slots = os.split.slots;
     p.ld_out = d->ld_out;
     p.n_tokens = d->n_tokens;
     p.n_heads = d->n_heads;
     const float scale = d->softmax_scale > 0.f ? d->softmax_scale : 1.0f / std::sqrt((float)d->head_dim);
     p.scale_log2 = scale * 1.4426950408889634f;
     const int grid = (int)attention_ctas(N, d->n_heads);
-    cudaError_t e = launch_pdl(fxr::attn::attention_kernel<T>, dim3(grid), dim3(fxr::attn::kThreads),
-                               fxr::attn::kSmemBytes, stream, tq, tk, tv, p);
+    // few heads per launch (a GPU's share of a head-split frame, small models): the query tiles x
+    // heads may leave SMs idle, so launch the instantiation that can split key ranges
+    const bool split = os.split.slots > 0 && d->n_heads <= kSplitMaxHeads;
+    cudaError_t e = split ? launch_pdl(fxr::attn::attention_kernel<T, true>, dim3(grid), dim3(fxr::attn::kThreads),
+                                       fxr::attn::kSmemBytes, stream, tq, tk, tv, p)
+                          : launch_pdl(fxr::attn::attention_kernel<T, false>, dim3(grid), dim3(fxr::attn::kThreads),
+                                       fxr::attn::kSmemBytes, stream, tq, tk, tv, p);
     if (e != cudaSuccess) return cuda_status(e, "attention_kernel launch");
     return FXR_OK;
 }
@@ -301,11 +345,11 @@ int32_t launch_gather(const fxr_frame_desc* d, const void* q, const void* k, con
     a.n_axes = d->rope_n_axes;
     a.eps = d->eps;
     fill_rope(d, &a.rope);
-    // bulk-copy pipeline: stages of 3 rows, ~160 KB of rows in flight per SM
+    // bulk-copy pipeline: stages of 3 rows, up to ~190 KB of rows in flight per SM
     const size_t row_bytes = (size_t)d->n_heads * d->head_dim * sizeof(T);
     fxr::BulkLayout lay{};
     lay.stage_bytes = (uint32_t)align_up(3 * row_bytes, 128);
-    const size_t budget = 160 * 1024;
+    const size_t budget = 190 * 1024;
     lay.stages = (uint32_t)std::max<size_t>(2, std::min<size_t>(fxr::kBulkMaxStages, budget / lay.stage_bytes));
     const size_t smem = (size_t)lay.stages * lay.stage_bytes + (size_t)lay.stages * fxr::kBulkInfoWords * 4 +
                         (size_t)lay.stages * 16;
@@ -362,7 +406,7 @@ int32_t fxr_check_device_error(void* stream, uint32_t* word_out) {
 
 size_t fxr_workspace_size(const fxr_frame_desc* desc) {
     if (!desc || dtype_bytes(desc->dtype) == 0 || desc->n_heads <= 0 || desc->head_dim <= 0) return 0;
-    return carve(desc, nullptr).total;
+    return carve(desc, nullptr).total + split_bytes(kSplitSlotsPerSm * sm_count());
 }
 
 // Device address of g_noalloc_scratch on the current device. The first call on a device resolves
@@ -418,14 +462,23 @@ int32_t fxr_workspace_views(const fxr_frame_desc* desc, void* workspace, int32_t
     return FXR_OK;
 }
 
-int32_t fxr_mask_compact(int32_t* mask, const uint8_t* valid, int32_t n_tokens, int32_t* idx,
-                         int32_t* count, void* stream) {
+static int32_t launch_compact(int32_t* mask, const uint8_t* valid, int32_t n_tokens, int32_t* idx,
+                              int32_t* count, const SplitArea& split, void* stream) {
     if (n_tokens < 0) return fail(FXR_ERR_INVALID, "n_tokens < 0");
     if (!count || (n_tokens > 0 && (!mask || !idx))) return fail(FXR_ERR_INVALID, "null pointer");
+    // the attention's split counters of this frame start at zero
+    uint4* zero = reinterpret_cast<uint4*>(split.cnt);
+    const int32_t zero_vec = (int32_t)((size_t)split.slots * kSplitCntBytes / 16);
     cudaError_t e = launch_pdl(fxr::compact_kernel, dim3(1), dim3(fxr::kCompactThreads), 0,
-                               static_cast<cudaStream_t>(stream), mask, valid, n_tokens, idx, count);
+                               static_cast<cudaStream_t>(stream), mask, valid, n_tokens, idx, count,
+                               zero, zero_vec);
     if (e != cudaSuccess) return cuda_status(e, "compact_kernel launch");
     return FXR_OK;
+}
+
+int32_t fxr_mask_compact(int32_t* mask, const uint8_t* valid, int32_t n_tokens, int32_t* idx,
+                         int32_t* count, void* stream) {
+    return launch_compact(mask, valid, n_tokens, idx, count, SplitArea{}, stream);
 }
 
 int32_t fxr_preprocess_mask(int32_t* mask, const uint8_t* valid, int32_t n_tokens, void* stream) {
@@ -687,13 +740,21 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void*
     if (workspace_bytes < w.total)
         return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, w.total);
     if (!aligned16(workspace)) return fail(FXR_ERR_INVALID, "workspace must be 16-byte aligned");
-    if ((st = fxr_mask_compact(mask, valid, desc->n_tokens, w.idx, w.count, stream)) != FXR_OK) return st;
+    const SplitArea split = split_area(w.total, workspace, workspace_bytes);
+    if ((st = launch_compact(mask, valid, desc->n_tokens, w.idx, w.count, split, stream)) != FXR_OK) return st;
     if ((st = fxr_gather_norm_rope(desc, q, k, v, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc,
                                    w.ld_qc, cache_k, cache_v, w.save, stream)) != FXR_OK)
         return st;
-    if ((st = fxr_attention_active(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, out,
-                                   stream)) != FXR_OK)
-        return st;
+    if (!cache_k || !cache_v || !out || !aligned16(cache_k) || !aligned16(cache_v) || !aligned16(out))
+        return fail(FXR_ERR_INVALID, "cache/out must be non-null and 16-byte aligned");
+    OutSet os;
+    os.out[0] = out;
+    os.split = split;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    st = desc->dtype == FXR_BF16
+             ? launch_attention<__nv_bfloat16>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s)
+             : launch_attention<__half>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s);
+    if (st != FXR_OK) return st;
     return fxr_restore_rows(desc, mask, w.idx, w.count, w.save, cache_k, cache_v, stream);
 }
 
@@ -762,8 +823,9 @@ int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g, c
         os.out[r] = static_cast<char*>(g->out[r]) + col;
         os.arrive[r] = signal ? g->arrive[r] : nullptr;
     }
+    os.split = split_area(w.total, workspace, workspace_bytes);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if ((st = fxr_mask_compact(mask, valid, sd.n_tokens, w.idx, w.count, stream)) != FXR_OK) return st;
+    if ((st = launch_compact(mask, valid, sd.n_tokens, w.idx, w.count, os.split, stream)) != FXR_OK) return st;
     if ((st = fxr_gather_norm_rope(&sd, qh, kh, vh, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc,
                                    w.ld_qc, cache_k, cache_v, w.save, stream)) != FXR_OK)
         return st;
@@ -837,7 +899,7 @@ static NcclViews carve_nccl(const fxr_frame_desc* d, const fxr_head_group* g, in
 
 size_t fxr_heads_nccl_workspace_size(const fxr_frame_desc* desc, const fxr_head_group* g, int32_t m_cap) {
     if (check_desc(desc, false) != FXR_OK || !group_ok(g) || m_cap < 0) return 0;
-    return carve_nccl(desc, g, m_cap, nullptr).total;
+    return carve_nccl(desc, g, m_cap, nullptr).total + split_bytes(kSplitSlotsPerSm * sm_count());
 }
 
 int32_t fxr_allgather_heads(const fxr_frame_desc* desc, const fxr_head_group* g, void* nccl_comm,
@@ -906,7 +968,9 @@ int32_t fxr_frame_forward_heads_nccl(const fxr_frame_desc* desc, const fxr_head_
     sd.n_heads = g->n_heads;
     sd.ld_cache = (int64_t)g->n_heads * desc->head_dim;
     const size_t col = (size_t)g->head0 * desc->head_dim * dtype_bytes(desc->dtype);
-    if ((st = fxr_mask_compact(mask, valid, sd.n_tokens, w.frame.idx, w.frame.count, stream)) != FXR_OK) return st;
+    const SplitArea split = split_area(w.total, workspace, workspace_bytes);
+    if ((st = launch_compact(mask, valid, sd.n_tokens, w.frame.idx, w.frame.count, split, stream)) != FXR_OK)
+        return st;
     if (g->n_heads > 0) {
         if ((st = fxr_gather_norm_rope(&sd, static_cast<const char*>(q) + col, static_cast<const char*>(k) + col,
                                        static_cast<const char*>(v) + col, mask, w.frame.idx, w.frame.count, pos,
@@ -922,6 +986,7 @@ int32_t fxr_frame_forward_heads_nccl(const fxr_frame_desc* desc, const fxr_head_
             return fail(FXR_ERR_INVALID, "cache must be non-null and 16-byte aligned");
         OutSet os;
         os.out[0] = w.o_local;
+        os.split = split;
         st = od.dtype == FXR_BF16
                  ? launch_attention<__nv_bfloat16>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, w.iota, os, s)
                  : launch_attention<__half>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, w.iota, os, s);

@@ -30,12 +30,15 @@ constexpr int kCompactChunk = kCompactWarps * kCompactGroups * 32;
 
 __global__ void __launch_bounds__(kCompactThreads, 1)
 compact_kernel(int32_t* __restrict__ mask, const uint8_t* __restrict__ valid, int32_t n,
-               int32_t* __restrict__ idx, int32_t* __restrict__ count) {
+               int32_t* __restrict__ idx, int32_t* __restrict__ count, uint4* __restrict__ zero,
+               int32_t zero_vec) {
     __shared__ int32_t warp_tot[kCompactWarps];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t lt = (1u << lane) - 1u;
     pdl_launch_dependents();
     pdl_wait();  // the previous frame's kernels may still read mask / idx / count
+    // the attention's key-split arrival counters of this frame (zero_vec 16-byte words)
+    for (int32_t e = threadIdx.x; e < zero_vec; e += kCompactThreads) zero[e] = make_uint4(0, 0, 0, 0);
     int32_t base = 0;
     for (int32_t c0 = 0; c0 < n; c0 += kCompactChunk) {
         const int32_t n_chunk = min(n - c0, kCompactChunk);
@@ -194,7 +197,7 @@ __device__ __forceinline__ void norm_rope_store_x2(const uint4& x, const float2*
 // mode 1 first copy their old cache rows to the save buffer.
 // ---------------------------------------------------------------------------------------------
 constexpr int kBulkGroupWarps = 4;
-constexpr int kBulkGroups = 4;
+constexpr int kBulkGroups = 6;
 constexpr int kBulkProducerWarp = kBulkGroupWarps * kBulkGroups;
 constexpr int kBulkThreads = (kBulkProducerWarp + 1) * 32;
 constexpr int kBulkMaxStages = 32;
@@ -356,9 +359,9 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
                         rope_sincos((float)inf[2 + ax] * a.rope.omega[j], &sn[t], &cs[t]);
                     }
                 }
-                // kUnitBatch independent head vectors per half-warp at a time (6 x 4 = 24 heads
-                // of a row): their loads, shuffles and stores interleave
-                constexpr int kUnitBatch = 6;
+                // kUnitBatch independent head vectors per half-warp at a time (their loads,
+                // shuffles and stores interleave); 24 heads = 2 batches of 3 x 4 half-warps
+                constexpr int kUnitBatch = 3;
                 const uint8_t* src = stage + (isq ? 0 : row_bytes) + (size_t)(8 * sub) * sizeof(T);
                 T* dst = (isq ? QC + (int64_t)r * a.ld_qc : CK + (int64_t)i * a.ld_cache) + 8 * sub;
                 // warp-uniform loop bound: both half-warps join every shuffle

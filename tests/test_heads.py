@@ -3,8 +3,10 @@
 CPU: the head split, argument checks, and — as world-size-2 gloo ranks — that per-rank head shards
 of the oracle, all-gathered by head, reproduce the full-frame oracle exactly (heads are independent
 in every step of the path). GPU: G ranks emulated on one GPU (every rank's frame is issued before
-any rank's wait, so no wait depends on later work) against the single-GPU frame, bit-exact; and,
-where the box has two GPUs, two real ranks exchanging O over NVLink peer mappings."""
+any rank's wait, so no wait depends on later work) against the single-GPU frame (caches bit-exact,
+outputs within the attention bar, every rank's output identical); and, where the box has two GPUs,
+two real ranks exchanging O over NVLink peer mappings or an NCCL all-gather (bit-exact between the
+two exchanges)."""
 import os
 import socket
 
@@ -111,6 +113,18 @@ def test_head_shards_reassemble_the_oracle_frame_gloo(tmp_path):
 
 
 # ---------------------------------------------------------------------------------------------
+def _out_close(a, b, dtype):
+    """Outputs of a head-split frame against the single-GPU frame. A rank's attention runs fewer
+    (query tile, head) units than the whole frame and may split each unit's key range across CTAs
+    where the single-GPU frame does not, which reorders the softmax sums: equal within the bar of
+    the attention output, not bit for bit."""
+    import torch
+    tol = (2e-3, 2e-4) if dtype == "f16" else (4e-3, 2e-4)
+    err = (a.float() - b.float()).abs()
+    return bool(torch.isfinite(a.float()).all()) and err.max().item() <= tol[0] and \
+        err.mean().item() <= tol[1]
+
+
 def _frame_tensors(w, fr):
     import torch
     td = {"bf16": torch.bfloat16, "f16": torch.float16}[w.dtype]
@@ -170,7 +184,8 @@ def test_heads_emulated_on_one_gpu_match_the_frame(cuda, world, dtype):
         assert fxr.check_device_error() == 0
         for r, g in enumerate(groups):
             assert g.epoch == f + 1
-            assert torch.equal(outs[r], ref["out"]), (f, r)
+            assert _out_close(outs[r], ref["out"], dtype), (f, r)
+            assert torch.equal(outs[r], outs[0]), (f, r)        # every rank holds the same output
             c0, c1 = g.head0 * 128, (g.head0 + g.n_heads) * 128
             assert torch.equal(caches[r][0], ref["cache_k"][:, c0:c1]), (f, r)
             assert torch.equal(caches[r][1], ref["cache_v"][:, c0:c1]), (f, r)
@@ -256,8 +271,11 @@ def _two_gpu_worker(rank, world, port, result_path):
         fxr.frame_forward(cfg, t["q"], t["k"], t["v"], t["mask"], None, t["pos"], t["norm_q"],
                           t["norm_k"], t["cache_k"], t["cache_v"], t["out"], ws)
         torch.cuda.synchronize()
-        ok = (err == 0 and torch.equal(got, t["out"]) and torch.equal(ck, t["cache_k"][:, c0:c1])
-              and torch.equal(cv, t["cache_v"][:, c0:c1]))
+        ok = (err == 0 and _out_close(got, t["out"], "bf16") and
+              torch.equal(ck, t["cache_k"][:, c0:c1]) and torch.equal(cv, t["cache_v"][:, c0:c1]))
+        outs = [None] * world
+        dist.all_gather_object(outs, got.cpu())
+        ok = ok and all(torch.equal(o, outs[0]) for o in outs)   # both ranks hold the same frame
         # the same frame with the O exchange as one NCCL all-gather
         uid = [fxr.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
@@ -273,7 +291,7 @@ def _two_gpu_worker(rank, world, port, result_path):
                                          None, t2["pos"], t2["norm_q"], t2["norm_k"], ck2, cv2,
                                          t2["out"], wsn)
             torch.cuda.synchronize()
-            ok = ok and fxr.check_device_error() == 0 and torch.equal(t2["out"], t["out"]) and \
+            ok = ok and fxr.check_device_error() == 0 and torch.equal(t2["out"], got) and \
                 torch.equal(ck2, ck)
         finally:
             torch.cuda.synchronize()
