@@ -43,6 +43,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--active", type=float, default=None, help="override the active fraction")
+    ap.add_argument("--heads", type=int, default=None, help="override the number of heads")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
@@ -63,6 +64,9 @@ def workload(args):
     w = {"c1": W.C1, "c2": W.C2, "c3": W.C3, "c4": W.C4, "c5": W.C5}[args.config]
     if args.active is not None:
         w = W.with_active(w, args.active)
+    if args.heads is not None:     # one GPU's share of a head-split frame, timed alone
+        w = W.Workload(f"{w.name}_h{args.heads}", w.grid_h, w.grid_w, w.n_text, args.heads, w.head_dim,
+                       w.dtype, w.active, w.pattern, w.rope_axes, w.rope_theta)
     return w
 
 

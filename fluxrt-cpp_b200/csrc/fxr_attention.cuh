@@ -85,8 +85,6 @@ constexpr uint32_t kSlotAbort = kSlotTmem + 4;
 static_assert(kSlotAbort + 4 <= 256, "barrier area overflow");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
-constexpr int kMaxOut = 8;   // destinations of a head-sharded frame: one per GPU of the group
-
 // Key-range split of a work unit across CTAs (when there are too few units to fill the GPU): each
 // part writes its partial O (unnormalised, fp32) with its row maxima and sums to a scratch slot; per
 // (unit, warp) portion an arrival counter elects the last-arriving part's warp, which combines all
@@ -107,10 +105,7 @@ struct Params {
     int32_t n_tokens;
     int32_t n_heads;
     float scale_log2;   // softmax scale * log2(e)
-    int32_t n_out;      // O destinations (1: this GPU only)
-    int32_t src_rank;   // arrival slot this GPU increments at every destination
-    void* out[kMaxOut];          // O row bases (this GPU's buffer and peers' mapped buffers)
-    uint32_t* arrive[kMaxOut];   // arrival slots of each destination; null: no signalling
+    void* out;                   // O row base
     float* split_scratch;        // [split_slots][kSplitSlotFloats]
     int32_t* split_cnt;          // [split_slots][kSplitPortions], zero at launch
     int32_t split_slots;         // 0: never split
@@ -184,10 +179,9 @@ __device__ __forceinline__ float2 ex2_poly2(float2 x) {
 
 // End of a split unit for the part that arrived last at a (unit, warp) portion: every part (this one
 // included) is read back from its slot and combined in part order — the result does not depend on
-// which CTA arrived last — then normalised and stored like the unsplit epilogue. Out of line, so
-// that its registers do not weigh on the softmax loop of the kernel.
+// which CTA arrived last — then normalised and stored like the unsplit epilogue.
 template <typename T>
-__device__ __noinline__ void split_combine_store(const Params& p, const float* slots, int32_t n_split,
+__device__ __forceinline__ void split_combine_store(const Params& p, const float* slots, int32_t n_split,
                                                  int r, int wg, int32_t orow, int32_t head) {
     float m_all = -INFINITY;
     for (int32_t q = 0; q < n_split; ++q)
@@ -225,14 +219,9 @@ __device__ __noinline__ void split_combine_store(const Params& p, const float* s
         v[k].z = StoreT<T>::pack2(acc[8 * k + 4] * inv, acc[8 * k + 5] * inv);
         v[k].w = StoreT<T>::pack2(acc[8 * k + 6] * inv, acc[8 * k + 7] * inv);
     }
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + off);
 #pragma unroll
-    for (int t = 0; t < kMaxOut; ++t) {
-        if (t < p.n_out) {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.out[t]) + off);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) dst[k] = v[k];
-        }
-    }
+    for (int k = 0; k < 4; ++k) dst[k] = v[k];
 }
 
 // kSplit: the instantiation that may split key ranges (launched for few heads per launch, where
@@ -575,16 +564,9 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                         v[k].z = StoreT<T>::pack2(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv);
                         v[k].w = StoreT<T>::pack2(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv);
                     }
-                    // the fused all-gather + scatter: the same 64 bytes go to every destination
-                    // (peer buffers are written over NVLink by these plain stores)
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + off);
 #pragma unroll
-                    for (int t = 0; t < kMaxOut; ++t) {
-                        if (t < p.n_out) {
-                            uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.out[t]) + off);
-#pragma unroll
-                            for (int k = 0; k < 4; ++k) dst[k] = v[k];
-                        }
-                    }
+                    for (int k = 0; k < 4; ++k) dst[k] = v[k];
                 } else {
                     atomicOr(&g_error_word, kErrBounds);
                 }
@@ -593,20 +575,11 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     }
 
     __syncwarp();  // role warps ran their loops on one lane; reconverge before the CTA barrier
-    const bool signal = p.arrive[0] != nullptr;
-    if (signal) __threadfence_system();   // this thread's O stores, visible to every GPU first
     tc_fence_before();
     __syncthreads();
     if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
-    }
-    // One arrival per CTA at every destination, also after an abort, so that the destinations'
-    // bounded waits end (the abort itself is reported through the error word).
-    if (signal && threadIdx.x == 0) {
-#pragma unroll
-        for (int t = 0; t < kMaxOut; ++t)
-            if (t < p.n_out) red_release_sys_add(p.arrive[t] + p.src_rank, 1u);
     }
 }
 

@@ -252,10 +252,7 @@ int grid_rows(int64_t rows, int rows_per_cta) {
 // Where the attention epilogue stores O: one buffer (a single-GPU frame), or every rank's buffer
 // of a head group plus the arrival slots it increments there.
 struct OutSet {
-    int32_t n = 1;
-    int32_t src_rank = 0;
-    void* out[fxr::attn::kMaxOut] = {};
-    uint32_t* arrive[fxr::attn::kMaxOut] = {};
+    void* out = nullptr;
     SplitArea split;   // key-range split scratch (none: never split)
 };
 
@@ -292,12 +289,7 @@ int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
     fxr::attn::Params p{};
     p.count = count;
     p.idx = idx;
-    p.n_out = os.n;
-    p.src_rank = os.src_rank;
-    for (int t = 0; t < fxr::attn::kMaxOut; ++t) {
-        p.out[t] = os.out[t];
-        p.arrive[t] = os.arrive[t];
-    }
+    p.out = os.out;
     p.split_scratch = os.split.scratch;
     p.split_cnt = os.split.cnt;
     p.split_slots = os.split.slots;
@@ -540,7 +532,7 @@ int32_t fxr_attention_active(const fxr_frame_desc* desc, const void* qc, int64_t
         return fail(FXR_ERR_INVALID, "qc/cache/out must be 16-byte aligned with ld_qc >= C, %% 8");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     OutSet os;
-    os.out[0] = out;
+    os.out = out;
     if (desc->dtype == FXR_BF16)
         return launch_attention<__nv_bfloat16>(desc, qc, ld_qc, count, cache_k, cache_v, idx, os, s);
     return launch_attention<__half>(desc, qc, ld_qc, count, cache_k, cache_v, idx, os, s);
@@ -748,7 +740,7 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void*
     if (!cache_k || !cache_v || !out || !aligned16(cache_k) || !aligned16(cache_v) || !aligned16(out))
         return fail(FXR_ERR_INVALID, "cache/out must be non-null and 16-byte aligned");
     OutSet os;
-    os.out[0] = out;
+    os.out = out;
     os.split = split;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     st = desc->dtype == FXR_BF16
@@ -757,6 +749,10 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void*
     if (st != FXR_OK) return st;
     return fxr_restore_rows(desc, mask, w.idx, w.count, w.save, cache_k, cache_v, stream);
 }
+
+// Exchange CTAs of a head-split frame (arrivals each GPU with heads sends per frame); every GPU of
+// the group is assumed to have this GPU's SM count.
+static int32_t push_ctas() { return sm_count(); }
 
 int32_t fxr_head_group_init(fxr_head_group* g, int32_t world, int32_t rank, int32_t n_heads,
                             int32_t n_tokens) {
@@ -775,10 +771,34 @@ int32_t fxr_head_group_init(fxr_head_group* g, int32_t world, int32_t rank, int3
             g->head0 = h;
             g->n_heads = hn;
         }
-        g->ctas[r] = (int32_t)attention_ctas(n_tokens, hn);
+        // a single GPU stores its rows directly; with peers every GPU that has heads runs the
+        // exchange kernel, whose CTAs each send one arrival
+        g->ctas[r] = (world > 1 && hn > 0 && n_tokens > 0) ? push_ctas() : 0;
         h += hn;
     }
     return FXR_OK;
+}
+
+// Workspace of one GPU's share of a head-split frame with peers: the share's frame workspace, then
+// an identity row list (the attention's compact output) and the compact O rows of its heads.
+struct HeadsViews {
+    Views frame;
+    int32_t* iota;
+    void* o_local;
+    size_t total;
+};
+
+static HeadsViews carve_heads(const fxr_frame_desc* sd, void* ws) {
+    HeadsViews v{};
+    v.frame = carve(sd, ws);
+    char* b = static_cast<char*>(ws);
+    size_t off = v.frame.total;
+    v.iota = reinterpret_cast<int32_t*>(b ? b + off : nullptr);
+    off = align_up(off + (size_t)std::max(sd->n_tokens, 1) * sizeof(int32_t), 256);
+    v.o_local = b ? b + off : nullptr;
+    off = align_up(off + (size_t)std::max(sd->n_tokens, 1) * sd->n_heads * sd->head_dim * dtype_bytes(sd->dtype), 256);
+    v.total = off;
+    return v;
 }
 
 int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g, const void* q,
@@ -794,56 +814,84 @@ int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g, c
         return fail(FXR_ERR_INVALID, "head group heads [%d, %d) outside the frame's %d heads", g->head0,
                     g->head0 + g->n_heads, desc->n_heads);
     if (desc->n_tokens == 0 || g->n_heads == 0) return FXR_OK;
-    if ((int64_t)g->ctas[g->rank] != attention_ctas(desc->n_tokens, g->n_heads))
-        return fail(FXR_ERR_INVALID, "head group was initialised for another frame size");
-    const bool signal = g->world > 1 || g->arrive[0] != nullptr;
+    const bool peers = g->world > 1;
+    if (g->ctas[g->rank] != (peers ? push_ctas() : 0))
+        return fail(FXR_ERR_INVALID, "head group was initialised for another frame or device");
     for (int32_t r = 0; r < g->world; ++r) {
         if (!g->out[r]) return fail(FXR_ERR_INVALID, "head group out[%d] is null", r);
-        if (signal && !g->arrive[r]) return fail(FXR_ERR_INVALID, "head group arrive[%d] is null", r);
+        if (peers && !g->arrive[r]) return fail(FXR_ERR_INVALID, "head group arrive[%d] is null", r);
         if (!aligned16(g->out[r])) return fail(FXR_ERR_INVALID, "head group out[%d] not 16-byte aligned", r);
     }
     if (!workspace) return fail(FXR_ERR_INVALID, "null workspace");
-    // this rank's slice of the frame: its heads, read from and written to the full-width rows
+    if (!q || !k || !v) return fail(FXR_ERR_INVALID, "null q/k/v");
+    if (!cache_k || !cache_v || !aligned16(cache_k) || !aligned16(cache_v))
+        return fail(FXR_ERR_INVALID, "cache must be non-null and 16-byte aligned");
+    // this GPU's share of the frame: its heads, read from the full-width rows
     fxr_frame_desc sd = *desc;
     sd.n_heads = g->n_heads;
     sd.ld_cache = (int64_t)g->n_heads * desc->head_dim;
-    const Views w = carve(&sd, workspace);
-    if (workspace_bytes < w.total)
-        return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, w.total);
+    const HeadsViews w = carve_heads(&sd, workspace);
+    const size_t need = peers ? w.total : w.frame.total;
+    if (workspace_bytes < need)
+        return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, need);
     if (!aligned16(workspace)) return fail(FXR_ERR_INVALID, "workspace must be 16-byte aligned");
-    const size_t col = (size_t)g->head0 * desc->head_dim * dtype_bytes(desc->dtype);
-    const char* qh = static_cast<const char*>(q) + col;
-    const char* kh = static_cast<const char*>(k) + col;
-    const char* vh = static_cast<const char*>(v) + col;
-    if (!q || !k || !v) return fail(FXR_ERR_INVALID, "null q/k/v");
-    OutSet os;
-    os.n = g->world;
-    os.src_rank = g->rank;
-    for (int32_t r = 0; r < g->world; ++r) {
-        os.out[r] = static_cast<char*>(g->out[r]) + col;
-        os.arrive[r] = signal ? g->arrive[r] : nullptr;
-    }
-    os.split = split_area(w.total, workspace, workspace_bytes);
+    const int32_t eb = (int32_t)dtype_bytes(desc->dtype);
+    const size_t col = (size_t)g->head0 * desc->head_dim * eb;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if ((st = launch_compact(mask, valid, sd.n_tokens, w.idx, w.count, os.split, stream)) != FXR_OK) return st;
-    if ((st = fxr_gather_norm_rope(&sd, qh, kh, vh, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc,
-                                   w.ld_qc, cache_k, cache_v, w.save, stream)) != FXR_OK)
+    OutSet os;
+    os.split = split_area(need, workspace, workspace_bytes);
+    if ((st = launch_compact(mask, valid, sd.n_tokens, w.frame.idx, w.frame.count, os.split, stream)) != FXR_OK)
         return st;
-    if (!cache_k || !cache_v || !aligned16(cache_k) || !aligned16(cache_v))
-        return fail(FXR_ERR_INVALID, "cache must be non-null and 16-byte aligned");
+    if ((st = fxr_gather_norm_rope(&sd, static_cast<const char*>(q) + col, static_cast<const char*>(k) + col,
+                                   static_cast<const char*>(v) + col, mask, w.frame.idx, w.frame.count, pos,
+                                   norm_q, norm_k, w.frame.qc, w.frame.ld_qc, cache_k, cache_v, w.frame.save,
+                                   stream)) != FXR_OK)
+        return st;
+    fxr_frame_desc od = sd;
+    const int32_t* att_idx = w.frame.idx;
+    if (peers) {
+        // compact output: row m of this GPU's heads at o_local[m]; the exchange scatters it
+        fxr::iota_rows_kernel<<<std::max(1, std::min(grid_rows(desc->n_tokens, 256), sm_count())), 256, 0, s>>>(
+            w.iota, desc->n_tokens, desc->n_tokens);
+        FXR_CHECK_LAUNCH("iota_rows_kernel launch");
+        od.ld_out = sd.ld_cache;
+        os.out = w.o_local;
+        att_idx = w.iota;
+    } else {
+        os.out = static_cast<char*>(g->out[0]) + col;
+    }
     st = sd.dtype == FXR_BF16
-             ? launch_attention<__nv_bfloat16>(&sd, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s)
-             : launch_attention<__half>(&sd, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s);
+             ? launch_attention<__nv_bfloat16>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, att_idx, os, s)
+             : launch_attention<__half>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, att_idx, os, s);
     if (st != FXR_OK) return st;
-    if (signal) g->epoch += 1;
-    return fxr_restore_rows(&sd, mask, w.idx, w.count, w.save, cache_k, cache_v, stream);
+    if ((st = fxr_restore_rows(&sd, mask, w.frame.idx, w.frame.count, w.frame.save, cache_k, cache_v, stream)) != FXR_OK)
+        return st;
+    if (!peers) return FXR_OK;
+    fxr::PushArgs a{};
+    a.o = static_cast<const uint4*>(w.o_local);
+    a.idx = w.frame.idx;
+    a.count = w.frame.count;
+    a.ld_out_vecs = desc->ld_out * eb / 16;
+    a.row_vecs = (int32_t)(sd.ld_cache * eb / 16);
+    a.n_tokens = desc->n_tokens;
+    a.world = g->world;
+    a.src_rank = g->rank;
+    for (int32_t r = 0; r < g->world; ++r) {
+        a.out[r] = reinterpret_cast<uint4*>(static_cast<char*>(g->out[r]) + col);
+        a.arrive[r] = g->arrive[r];
+    }
+    cudaError_t e = launch_pdl(fxr::heads_push_kernel, dim3(push_ctas()), dim3(fxr::kPushThreads), 0, s, a);
+    if (e != cudaSuccess) return cuda_status(e, "heads_push_kernel launch");
+    g->epoch += 1;
+    return FXR_OK;
 }
 
 int32_t fxr_head_group_wait(const fxr_head_group* g, void* stream) {
     if (!g || g->world < 1 || g->world > FXR_MAX_RANKS || g->rank < 0 || g->rank >= g->world)
         return fail(FXR_ERR_INVALID, "head group not initialised");
+    if (g->world == 1) return FXR_OK;   // a single GPU stored its rows itself
     uint32_t* slots = g->arrive[g->rank];
-    if (!slots) return g->world == 1 ? FXR_OK : fail(FXR_ERR_INVALID, "head group arrive[rank] is null");
+    if (!slots) return fail(FXR_ERR_INVALID, "head group arrive[rank] is null");
     fxr::ArrivalCounts c{};
     for (int32_t r = 0; r < g->world; ++r) c.ctas[r] = (uint32_t)g->ctas[r];
     fxr::arrival_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(slots, c, g->world);
@@ -985,7 +1033,7 @@ int32_t fxr_frame_forward_heads_nccl(const fxr_frame_desc* desc, const fxr_head_
         if (!cache_k || !cache_v || !aligned16(cache_k) || !aligned16(cache_v))
             return fail(FXR_ERR_INVALID, "cache must be non-null and 16-byte aligned");
         OutSet os;
-        os.out[0] = w.o_local;
+        os.out = w.o_local;
         os.split = split;
         st = od.dtype == FXR_BF16
                  ? launch_attention<__nv_bfloat16>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, w.iota, os, s)

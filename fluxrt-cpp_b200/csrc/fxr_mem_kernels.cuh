@@ -420,8 +420,63 @@ restore_rows_kernel(const int32_t* __restrict__ mask, const int32_t* __restrict_
 }
 
 // ---------------------------------------------------------------------------------------------
+// Exchange of a head-split frame: every executed row's slice of this GPU's heads (compact O, written
+// by the attention) goes to the full-frame output of every GPU of the group — the all-gather and the
+// scatter in one pass, over NVLink through peer mappings. A warp per row; each lane moves 16-byte
+// pieces of the slice (hn x 256 contiguous bytes at the destination), the slice loaded once and
+// stored to every destination. Each CTA then adds one arrival (release, system scope) to its slot
+// at every destination.
+// ---------------------------------------------------------------------------------------------
+constexpr int kPushThreads = 256;
+constexpr int kPushMaxVecs = 8;    // 16-byte pieces per lane of a row slice: up to 8 heads x 256 B / 32
+
+struct PushArgs {
+    const uint4* o;            // compact O [rows][row_vecs], this GPU's heads
+    const int32_t* idx;
+    const int32_t* count;
+    int64_t ld_out_vecs;       // destination row stride in 16-byte units
+    int32_t row_vecs;          // 16-byte pieces per row slice (hn * head_dim * size / 16)
+    int32_t n_tokens, world, src_rank;
+    uint4* out[8];             // destinations, offset to this GPU's first head column
+    uint32_t* arrive[8];
+};
+
+__global__ void __launch_bounds__(kPushThreads) heads_push_kernel(const __grid_constant__ PushArgs a) {
+    const int lane = threadIdx.x & 31;
+    pdl_wait();                // the attention's compact O
+    const int32_t M = *a.count;
+    for (int32_t m = blockIdx.x * (kPushThreads / 32) + (threadIdx.x >> 5); m < M;
+         m += gridDim.x * (kPushThreads / 32)) {
+        const int32_t i = a.idx[m];
+        if (i < 0 || i >= a.n_tokens) {
+            if (lane == 0) atomicOr(&g_error_word, kErrBounds);
+            continue;
+        }
+        for (int32_t c0 = 0; c0 < a.row_vecs; c0 += 32 * kPushMaxVecs) {
+            uint4 v[kPushMaxVecs];
+            const uint4* src = a.o + (int64_t)m * a.row_vecs + c0;
+            const int32_t nv = min(a.row_vecs - c0, 32 * kPushMaxVecs);
+#pragma unroll
+            for (int k = 0; k < kPushMaxVecs; ++k)
+                if (lane + 32 * k < nv) v[k] = src[lane + 32 * k];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                if (t >= a.world) break;
+                uint4* dst = a.out[t] + (int64_t)i * a.ld_out_vecs + c0;
+#pragma unroll
+                for (int k = 0; k < kPushMaxVecs; ++k)
+                    if (lane + 32 * k < nv) dst[lane + 32 * k] = v[k];
+            }
+        }
+    }
+    __threadfence_system();    // this thread's stores, visible to every GPU before the arrival
+    __syncthreads();
+    if (threadIdx.x < a.world) red_release_sys_add(a.arrive[threadIdx.x] + a.src_rank, 1u);
+}
+
+// ---------------------------------------------------------------------------------------------
 // Arrival wait of a head-sharded frame. slots[0..8): arrivals from each source GPU (one per
-// attention CTA of that GPU per frame); slots[8]: frames this GPU has waited for, kept on the
+// exchange CTA of that GPU per frame); slots[8]: frames this GPU has waited for, kept on the
 // device so that a CUDA graph of the frame can be replayed. Thread s waits (bounded) until slot s
 // reaches (frames + 1) * ctas[s]; the acquire at system scope makes the O rows that GPU s stored
 // here before its increments visible to the kernels after this one.

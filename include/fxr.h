@@ -210,19 +210,20 @@ int32_t fxr_workspace_views(const fxr_frame_desc* desc, void* workspace, int32_t
 /* ---- one frame split by attention heads over the GPUs of one node ------------------------------
  * The reference runs a frame on one GPU. Here a high-resolution frame can be split by heads: rank r
  * (one process per GPU) owns heads [head0, head0 + n_heads), gathers, normalises and rotates its
- * heads of every executed token, keeps its heads' K/V cache locally (no cache traffic), and its
- * attention epilogue stores each finished O row slice into the full-frame output of EVERY rank
- * through peer mappings (an all-gather fused with the scatter, over NVLink, tile by tile). Each
- * attention CTA then adds one arrival to slot `rank` of every rank's arrival counters;
- * fxr_head_group_wait makes a rank's stream wait (bounded) until all ranks' arrivals of the frame
- * are in, after which its output holds every head. */
+ * heads of every executed token and keeps its heads' K/V cache locally (no cache traffic). Its
+ * attention writes the executed rows of its heads compactly; an exchange kernel then stores each
+ * row's slice (n_heads x head_dim contiguous elements) into the full-frame output of EVERY rank
+ * through peer mappings — the all-gather and the scatter in one pass over NVLink, with coalesced
+ * 16-byte stores — and each of its CTAs adds one arrival to slot `rank` of every rank's arrival
+ * counters. fxr_head_group_wait makes a rank's stream wait (bounded) until all ranks' arrivals of
+ * the frame are in, after which its output holds every head. */
 #define FXR_MAX_RANKS 8
 
 typedef struct fxr_head_group {
     int32_t world;                      /* ranks sharing the frame, 1..FXR_MAX_RANKS */
     int32_t rank;                       /* this rank */
     int32_t head0, n_heads;             /* this rank's heads (set by fxr_head_group_init) */
-    int32_t ctas[FXR_MAX_RANKS];        /* attention CTAs (arrivals sent) per frame, per rank */
+    int32_t ctas[FXR_MAX_RANKS];        /* exchange CTAs (arrivals sent) per frame, per rank */
     uint32_t epoch;                     /* frames issued by this rank (host count, informational) */
     int32_t reserved0;
     void* out[FXR_MAX_RANKS];           /* each rank's full-frame O [n_tokens, ld_out], mapped here */
@@ -236,17 +237,18 @@ typedef struct fxr_head_group {
 #define FXR_HEAD_GROUP_SLOTS 16
 
 /* Fills world, rank, the contiguous balanced head split (ranks < n_heads % world get one more
- * head), the per-rank CTA counts for frames of n_tokens tokens (all GPUs are assumed to have this
- * GPU's SM count), epoch = 0, and clears out[] / arrive[] (the caller sets them). */
+ * head), the per-rank arrival counts (all GPUs are assumed to have this GPU's SM count; none for a
+ * single GPU, which stores its rows itself), epoch = 0, and clears out[] / arrive[] (the caller sets
+ * them). */
 int32_t fxr_head_group_init(fxr_head_group* g, int32_t world, int32_t rank, int32_t n_heads,
                             int32_t n_tokens);
 
 /* One frame of this rank's heads. desc describes the FULL frame (n_heads = all heads, ld_qkv and
  * ld_out over all heads); q/k/v are the full-frame inputs; cache_k/cache_v hold this rank's heads
  * only, [n_tokens, g->n_heads * head_dim] packed. Workspace: fxr_workspace_size(desc) suffices.
- * Issues compaction, gather/norm/RoPE, attention with the peer stores and arrivals, and the
- * mask==1 cache restore; it does not wait for the other ranks (fxr_head_group_wait does), so a
- * single GPU may emulate several ranks by issuing every rank's frame before any rank's wait.
+ * Issues compaction, gather/norm/RoPE, attention, the mask==1 cache restore and (with peers) the
+ * exchange with its arrivals; it does not wait for the other ranks (fxr_head_group_wait does), so
+ * a single GPU may emulate several ranks by issuing every rank's frame before any rank's wait.
  * Callers must not let a rank start frame f+1 while another rank still reads frame f's output. */
 int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g,
                                 const void* q, const void* k, const void* v,

@@ -31,8 +31,8 @@ def test_head_split_tiles_the_heads(world, heads):
         assert all(not p for p in g.out) and all(not p for p in g.arrive)
     assert h == heads
     for r, g in enumerate(gs):
-        tiles = (4608 + 127) // 128 * g.n_heads
-        assert gs[0].ctas[r] == (min(tiles, gs[0].ctas[r]) if tiles else 0)
+        # arrivals per frame: one per exchange CTA of every GPU that has heads; none on one GPU
+        assert (gs[0].ctas[r] > 0) == (world > 1 and g.n_heads > 0)
 
 
 def test_head_group_rejects_bad_arguments():
