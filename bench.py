@@ -44,6 +44,9 @@ def parse():
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--active", type=float, default=None, help="override the active fraction")
     ap.add_argument("--heads", type=int, default=None, help="override the number of heads")
+    ap.add_argument("--streams", type=int, default=None,
+                    help="independent edit streams in total (one batched set of launches per GPU "
+                         "per step; c4 default 8, spread over the GPUs)")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
@@ -56,6 +59,8 @@ def parse():
     a = ap.parse_args()
     if a.split is None:
         a.split = "heads" if a.config == "c5" else "replicas"
+    if a.streams is None and a.config == "c4":
+        a.streams = 8
     return a
 
 
@@ -815,6 +820,113 @@ def run_heads(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------------------------
+# independent edit streams, batched (config 4: 8 streams of 768^2 spread over the GPUs)
+# ---------------------------------------------------------------------------------------------
+def run_streams(args):
+    """A step is one frame of every stream: each GPU runs its streams' frames as one batched set
+    of launches (fxr_frame_forward_batch). value = attention FLOP of all streams / max-over-ranks
+    time; frames_per_s = streams / step time. Strong scaling: the total of streams is fixed."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import fxr
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    fxr.load()
+    w = workload(args)
+    cfg = frame_cfg(w)
+    total = args.streams
+    mine = [s_ for s_ in range(total) if s_ % world == rank]
+    # two rotating sets of every stream's inputs: 2 x streams x ~100 MB > L2
+    n_sets = 2
+    sets = [[make_device_frame(w, args.seed + 7919 * s_ + 104729 * k, device) for s_ in mine]
+            for k in range(n_sets)]
+    pos = sets[0][0]["pos"]
+    nq, nk = sets[0][0]["norm_q"], sets[0][0]["norm_k"]
+    ws = [torch.empty(max(1, fxr.batch_workspace_size(cfg, len(mine))), dtype=torch.uint8, device=device)
+          for _ in range(n_sets)]
+
+    def step(i):
+        k = i % n_sets
+        if mine:
+            fxr.frame_forward_batch(cfg, sets[k], pos, nq, nk, ws[k])
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    if fxr.check_device_error() != 0:
+        raise RuntimeError("device error during warm-up")
+    graphs = []
+    if not args.no_graph:
+        for k in range(n_sets):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step(k)
+            graphs.append(g)
+    run = (lambda i: graphs[i % n_sets].replay()) if graphs else step
+    stream = torch.cuda.current_stream()
+    clocks = Clocks(local)
+    clocks.start()
+    t_end = time.time() + 1.0
+    i = 0
+    while time.time() < t_end:
+        run(i)
+        i += 1
+        if i % 16 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        run(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    flops = sum(attn_flops(w, fr["M"]) for k in range(n_sets) for fr in sets[k]) / n_sets * args.steps
+    if world > 1:
+        t = torch.tensor([t_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_ms = float(t.item())
+        f = torch.tensor([flops], dtype=torch.float64, device=device)
+        dist.all_reduce(f, op=dist.ReduceOp.SUM)
+        flops = float(f.item())
+    if fxr.check_device_error() != 0:
+        raise RuntimeError("device error during the timed region")
+    ms_per_step = t_ms / args.steps
+    out_line = {
+        "metric": METRIC, "value": round(flops / (t_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5), "frames_per_s": round(total / (ms_per_step * 1e-3), 1),
+        "us_per_frame_per_gpu": round(ms_per_step * 1e3 / max(1, len(mine)), 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": w.dtype,
+        "impl": "ours", "data": "synthetic: N(0,1) Q/K/V/cache, N(1,0.1) norm weights, Bernoulli masks (seeded, one per stream)",
+        "config": {"workload": w.name, "streams": total, "streams_per_gpu": len(mine),
+                   "n_tokens": w.n_tokens, "active": w.active, "heads": w.n_heads,
+                   "parallelism": f"streams{total}-over-{world}",
+                   "l2": f"{n_sets} rotating sets of every stream's inputs", "graph": bool(graphs)},
+        "e2e": None, "gpu_launches": 4 * args.steps, "clocks": clk,
+    }
+    if rank == 0:
+        print(json.dumps(out_line), flush=True)
+    for g in graphs:
+        del g
+    graphs.clear()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def _heads_split(n_heads, world):
     return [n_heads // world + (1 if r < n_heads % world else 0) for r in range(world)]
 
@@ -825,6 +937,8 @@ def main():
         run_reference(args)
     elif args.split in ("heads", "heads_nccl"):
         run_heads(args)
+    elif args.streams is not None and args.streams > 1:
+        run_streams(args)
     else:
         run_ours(args)
 

@@ -57,8 +57,8 @@ constexpr uint32_t kTileBytes = 2 * kHalfBytes; // 128 x 128 16-bit tile
 constexpr uint32_t kSmemQ = 0;
 constexpr uint32_t kSmemRing = kTileBytes;
 constexpr uint32_t kSmemX = kSmemRing + kSlots * kTileBytes;  // exchange [2 buf][4 wg][128 rows]
-constexpr uint32_t kSmemRowIdx = kSmemX + 2 * 4 * 128 * 4;   // [softmax thread] output row of its item
-constexpr uint32_t kSmemBar = kSmemRowIdx + kSoftmaxThreads * 4;
+constexpr uint32_t kSmemRowIdx = kSmemX + 2 * 4 * 128 * 4;   // output row, stream of a softmax thread's item
+constexpr uint32_t kSmemBar = kSmemRowIdx + 2 * kSoftmaxThreads * 4;   // [2][softmax thread]
 constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;       // barriers + alignment slack
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
@@ -82,7 +82,8 @@ enum Bar : uint32_t {
 };
 constexpr uint32_t kSlotTmem = kNumBars * 8;
 constexpr uint32_t kSlotAbort = kSlotTmem + 4;
-static_assert(kSlotAbort + 4 <= 256, "barrier area overflow");
+constexpr uint32_t kSlotSched = kSlotAbort + 4;   // [parts per unit, work items] of the launch
+static_assert(kSlotSched + 8 <= 256, "barrier area overflow");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // Key-range split of a work unit across CTAs (when there are too few units to fill the GPU): each
@@ -98,14 +99,26 @@ constexpr float kSplitOverheadSteps = 4.0f;
 constexpr int kSplitSlotFloats = 128 * 128 + 2 * 4 * 128;   // O [128][128], m [4][128], l [4][128]
 constexpr int kSplitPortions = 16;                   // softmax warps: counters per unit
 
+struct Stream {                  // one edit stream of the launch
+    const int32_t* count;        // executed rows (compaction output, device)
+    const int32_t* idx;          // their token indices
+    void* out;                   // O row base
+};
+
+// Tensor maps of every stream: compact Q' and the K / V caches.
+struct Maps {
+    CUtensorMap q[kMaxBatch];
+    CUtensorMap k[kMaxBatch];
+    CUtensorMap v[kMaxBatch];
+};
+
 struct Params {
-    const int32_t* count;
-    const int32_t* idx;
+    Stream s[kMaxBatch];
+    int32_t n_streams;
     int64_t ld_out;
     int32_t n_tokens;
     int32_t n_heads;
     float scale_log2;   // softmax scale * log2(e)
-    void* out;                   // O row base
     float* split_scratch;        // [split_slots][kSplitSlotFloats]
     int32_t* split_cnt;          // [split_slots][kSplitPortions], zero at launch
     int32_t split_slots;         // 0: never split
@@ -180,8 +193,42 @@ __device__ __forceinline__ float2 ex2_poly2(float2 x) {
 // End of a split unit for the part that arrived last at a (unit, warp) portion: every part (this one
 // included) is read back from its slot and combined in part order — the result does not depend on
 // which CTA arrived last — then normalised and stored like the unsplit epilogue.
+// Work unit u of the launch -> stream b, head and first compact row; units are numbered stream
+// after stream, (query tile, head) within a stream as tile + head * tiles. m_b: the stream's rows.
+// (Loops over the streams use static indices only: a runtime index into the kernel parameters
+// makes the compiler copy them to local memory, which costs the softmax warps ~130 bytes of spills.)
+__device__ __forceinline__ void decode_unit(const Params& p, int32_t u, int32_t& b, int32_t& head,
+                                            int32_t& row0, int32_t& m_b) {
+    b = -1;
+#pragma unroll
+    for (int k = 0; k < kMaxBatch; ++k) {
+        if (b < 0 && k < p.n_streams) {
+            const int32_t mk = *p.s[k].count;
+            const int32_t units = (mk + kBM - 1) / kBM * p.n_heads;
+            if (u < units || k + 1 == p.n_streams) {
+                b = k;
+                m_b = mk;
+            } else {
+                u -= units;
+            }
+        }
+    }
+    const int32_t n_qt = (m_b + kBM - 1) / kBM;
+    head = n_qt > 0 ? u / n_qt : 0;
+    row0 = (u - head * n_qt) * kBM;
+}
+
+// Output row base of stream b (static-index selection, see above).
+__device__ __forceinline__ void* stream_out(const Params& p, int32_t b) {
+    void* o = p.s[0].out;
+#pragma unroll
+    for (int k = 1; k < kMaxBatch; ++k)
+        if (k == b) o = p.s[k].out;
+    return o;
+}
+
 template <typename T>
-__device__ __forceinline__ void split_combine_store(const Params& p, const float* slots, int32_t n_split,
+__device__ __forceinline__ void split_combine_store(const Params& p, T* out, const float* slots, int32_t n_split,
                                                  int r, int wg, int32_t orow, int32_t head) {
     float m_all = -INFINITY;
     for (int32_t q = 0; q < n_split; ++q)
@@ -219,7 +266,7 @@ __device__ __forceinline__ void split_combine_store(const Params& p, const float
         v[k].z = StoreT<T>::pack2(acc[8 * k + 4] * inv, acc[8 * k + 5] * inv);
         v[k].w = StoreT<T>::pack2(acc[8 * k + 6] * inv, acc[8 * k + 7] * inv);
     }
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + off);
+    uint4* dst = reinterpret_cast<uint4*>(out + off);
 #pragma unroll
     for (int k = 0; k < 4; ++k) dst[k] = v[k];
 }
@@ -229,8 +276,7 @@ __device__ __forceinline__ void split_combine_store(const Params& p, const float
 // costs the softmax loop ~10 % (register allocation).
 template <typename T, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
-attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ Params p) {
+attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -261,9 +307,11 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         fence_mbar_init();
     }
     if (warp == kProducerWarp && lane == 0) {
-        prefetch_tmap(&tmQ);
-        prefetch_tmap(&tmK);
-        prefetch_tmap(&tmV);
+        // the first stream's descriptors (prefetching every stream's in a loop costs the softmax
+        // warps ~130 bytes of register spills; the others are fetched on first use)
+        prefetch_tmap(&maps.q[0]);
+        prefetch_tmap(&maps.k[0]);
+        prefetch_tmap(&maps.v[0]);
     }
     if (warp == kMmaWarp) {
         tmem_alloc(smem_u32((const void*)tmem_slot), kTmemCols);
@@ -279,12 +327,23 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     // queries, indices and count it wrote are read below.
     pdl_launch_dependents();
     pdl_wait();
-    const int32_t M = *p.count;
-    const int32_t n_qt = (M + kBM - 1) / kBM;
-    const int32_t n_units = n_qt * p.n_heads;
+    int32_t n_units = 0;
+#pragma unroll
+    for (int b = 0; b < kMaxBatch; ++b)
+        if (b < p.n_streams) n_units += (*p.s[b].count + kBM - 1) / kBM * p.n_heads;
     const int32_t n_steps = (p.n_tokens + kStepN - 1) / kStepN;
     const int32_t n_split = kSplit ? choose_splits(n_units, (int32_t)gridDim.x, n_steps, p.split_slots) : 1;
     const int32_t n_items = n_units * n_split;   // item w: unit w / n_split, key part w % n_split
+    // the softmax warps re-read the schedule from shared memory per item: in the split-capable
+    // build, keeping it in registers across the step loop tips the allocation into spills
+    volatile int32_t* sched = reinterpret_cast<volatile int32_t*>(gbase + kSmemBar + kSlotSched);
+    if (kSplit) {
+        if (threadIdx.x == 0) {
+            sched[0] = n_split;
+            sched[1] = n_items;
+        }
+        __syncthreads();
+    }
 
     if (warp == kProducerWarp) {
         if (lane == 0) {
@@ -305,19 +364,30 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             };
             for (int32_t w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
                 const int32_t u = w / n_split, part = w - u * n_split;
-                const int32_t head = u / n_qt, row0 = (u % n_qt) * kBM;
+                int32_t b, head, row0, m_b;
+                decode_unit(p, u, b, head, row0, m_b);
+                const CUtensorMap* tmQ = &maps.q[0];
+                const CUtensorMap* tmK = &maps.k[0];
+                const CUtensorMap* tmV = &maps.v[0];
+#pragma unroll
+                for (int k = 1; k < kMaxBatch; ++k)
+                    if (k == b) {
+                        tmQ = &maps.q[k];
+                        tmK = &maps.k[k];
+                        tmV = &maps.v[k];
+                    }
                 const int32_t s0 = part * n_steps / n_split, s1 = (part + 1) * n_steps / n_split;
                 if (q_it > 0 && !mbar_wait(bar(kQEmpty), (q_it - 1) & 1, abort)) { ok = false; break; }
                 mbar_arrive_expect_tx(bar(kQFull), kTileBytes);
-                tma_load_2d(base + kSmemQ, &tmQ, bar(kQFull), head * kD, row0);
-                tma_load_2d(base + kSmemQ + kHalfBytes, &tmQ, bar(kQFull), head * kD + 64, row0);
+                tma_load_2d(base + kSmemQ, tmQ, bar(kQFull), head * kD, row0);
+                tma_load_2d(base + kSmemQ + kHalfBytes, tmQ, bar(kQFull), head * kD + 64, row0);
                 ++q_it;
-                ok = load(&tmK, head, s0 * kStepN) && load(&tmK, head, s0 * kStepN + kSubN);
+                ok = load(tmK, head, s0 * kStepN) && load(tmK, head, s0 * kStepN + kSubN);
                 for (int32_t j = s0 + 1; ok && j < s1; ++j)
-                    ok = load(&tmK, head, j * kStepN) && load(&tmK, head, j * kStepN + kSubN) &&
-                         load(&tmV, head, (j - 1) * kStepN) && load(&tmV, head, (j - 1) * kStepN + kSubN);
-                ok = ok && load(&tmV, head, (s1 - 1) * kStepN) &&
-                     load(&tmV, head, (s1 - 1) * kStepN + kSubN);
+                    ok = load(tmK, head, j * kStepN) && load(tmK, head, j * kStepN + kSubN) &&
+                         load(tmV, head, (j - 1) * kStepN) && load(tmV, head, (j - 1) * kStepN + kSubN);
+                ok = ok && load(tmV, head, (s1 - 1) * kStepN) &&
+                     load(tmV, head, (s1 - 1) * kStepN + kSubN);
             }
             if (*abort) {
                 if (q_it > 0) mbar_wait_drain(bar(kQFull), (q_it - 1) & 1);
@@ -428,15 +498,17 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             for (int k = 0; k < 4; ++k) o4[k] = xb[k * 128 + r];
             return true;
         };
-        for (int32_t w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
-            const int32_t u = w / n_split, part = w - u * n_split;
-            const int32_t head = u / n_qt, row0 = (u % n_qt) * kBM;
-            const int32_t s0 = part * n_steps / n_split, s1 = (part + 1) * n_steps / n_split;
-            const bool live = row0 + r < M;
-            // the output row of this thread, loaded now (kept in shared memory: the step loop has
-            // no register to spare) so that the epilogue does not wait on a global load
+        for (int32_t w = blockIdx.x; ok && w < (kSplit ? sched[1] : n_items); w += gridDim.x) {
+            const int32_t ns = kSplit ? sched[0] : 1;
+            int32_t b, head, row0, m_b;
+            decode_unit(p, w / ns, b, head, row0, m_b);
+            const int32_t s0 = (w % ns) * n_steps / ns, s1 = (w % ns + 1) * n_steps / ns;
+            const bool live = row0 + r < m_b;
+            // the output row and stream of this thread, loaded now (kept in shared memory: the step
+            // loop has no register to spare) so that the epilogue does not wait on a global load
             int32_t* orow_slot = reinterpret_cast<int32_t*>(gbase + kSmemRowIdx) + threadIdx.x;
-            *orow_slot = live ? __ldg(p.idx + row0 + r) : -1;
+            orow_slot[0] = live ? __ldg(p.s[b].idx + row0 + r) : -1;
+            orow_slot[kSoftmaxThreads] = b;
             float m_run = -INFINITY, l_run = 0.f;
             for (int32_t j = s0; j < s1; ++j, ++s_it) {
                 if (!wwait(bar(kSFull), s_it & 1)) { ok = false; break; }
@@ -527,10 +599,12 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             tc_fence_before();
             mbar_arrive(bar(kOFree));
             ++units_done;
-            const int32_t m = row0 + r;
+            const int32_t n_split = kSplit ? sched[0] : 1;
             if (n_split > 1) {
-                // partial of this part: O (32 columns of row r), row maximum and sum
-                float* slot = p.split_scratch + (size_t)(u * n_split + part) * kSplitSlotFloats;
+                // partial of this part: O (32 columns of row r), row maximum and sum (unit and part
+                // recomputed from the item, not kept live across the step loop)
+                const int32_t u = w / n_split;
+                float* slot = p.split_scratch + (size_t)w * kSplitSlotFloats;
                 float4* od = reinterpret_cast<float4*>(slot + r * kD + wg * 32);
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
@@ -546,12 +620,13 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 if (prev == n_split - 1) {   // the last part to arrive combines this portion
                     if (lane == 0) p.split_cnt[u * kSplitPortions + warp] = 0;   // for the next launch
                     __threadfence();
-                    split_combine_store<T>(p, p.split_scratch + (size_t)u * n_split * kSplitSlotFloats,
-                                           n_split, r, wg, m < M ? *orow_slot : -1, head);
+                    split_combine_store<T>(p, static_cast<T*>(stream_out(p, orow_slot[kSoftmaxThreads])),
+                                           p.split_scratch + (size_t)u * n_split * kSplitSlotFloats,
+                                           n_split, r, wg, live ? *orow_slot : -1, head);
                 }
                 continue;
             }
-            if (m < M) {
+            if (live) {
                 const int32_t i = *orow_slot;
                 if (i >= 0 && i < p.n_tokens) {
                     const float inv = 1.0f / l_tot;
@@ -564,7 +639,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                         v[k].z = StoreT<T>::pack2(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv);
                         v[k].w = StoreT<T>::pack2(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv);
                     }
-                    uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + off);
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(stream_out(p, orow_slot[kSoftmaxThreads])) + off);
 #pragma unroll
                     for (int k = 0; k < 4; ++k) dst[k] = v[k];
                 } else {

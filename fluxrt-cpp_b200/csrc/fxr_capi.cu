@@ -262,10 +262,21 @@ int64_t attention_ctas(int64_t n_tokens, int64_t n_heads) {
     return std::max<int64_t>(1, std::min<int64_t>(max_tiles, sm_count()));
 }
 
+// One edit stream's operands of an attention launch.
+struct AttnStreamArgs {
+    const void* qc;
+    int64_t ld_qc;
+    const int32_t* count;
+    const void* ck;
+    const void* cv;
+    const int32_t* idx;
+    void* out;
+};
+
 template <typename T>
-int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
-                         const int32_t* count, const void* ck, const void* cv, const int32_t* idx,
-                         const OutSet& os, cudaStream_t stream) {
+int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, const AttnStreamArgs* st,
+                                 const SplitArea& split, cudaStream_t stream) {
+    if (n_streams < 1 || n_streams > fxr::kMaxBatch) return fail(FXR_ERR_INVALID, "1..%d streams per launch", fxr::kMaxBatch);
     static bool configured[kMaxDevices] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -281,54 +292,59 @@ int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
     }
     const int64_t C = (int64_t)d->n_heads * d->head_dim;
     const int64_t N = d->n_tokens;
-    CUtensorMap tq, tk, tv;
-    int32_t st;
-    if ((st = make_tmap(&tq, qc, d->dtype, C, N, ld_qc)) != FXR_OK) return st;
-    if ((st = make_tmap(&tk, ck, d->dtype, C, N, d->ld_cache)) != FXR_OK) return st;
-    if ((st = make_tmap(&tv, cv, d->dtype, C, N, d->ld_cache)) != FXR_OK) return st;
+    fxr::attn::Maps maps;
+    std::memset(&maps, 0, sizeof(maps));
     fxr::attn::Params p{};
-    p.count = count;
-    p.idx = idx;
-    p.out = os.out;
-    p.split_scratch = os.split.scratch;
-    p.split_cnt = os.split.cnt;
-    p.split_slots = os.split.slots;
+    int32_t rc;
+    for (int32_t b = 0; b < n_streams; ++b) {
+        if ((rc = make_tmap(&maps.q[b], st[b].qc, d->dtype, C, N, st[b].ld_qc)) != FXR_OK) return rc;
+        if ((rc = make_tmap(&maps.k[b], st[b].ck, d->dtype, C, N, d->ld_cache)) != FXR_OK) return rc;
+        if ((rc = make_tmap(&maps.v[b], st[b].cv, d->dtype, C, N, d->ld_cache)) != FXR_OK) return rc;
+        p.s[b].count = st[b].count;
+        p.s[b].idx = st[b].idx;
+        p.s[b].out = st[b].out;
+    }
+    p.n_streams = n_streams;
+    p.split_scratch = split.scratch;
+    p.split_cnt = split.cnt;
+    p.split_slots = split.slots;
     p.ld_out = d->ld_out;
     p.n_tokens = d->n_tokens;
     p.n_heads = d->n_heads;
     const float scale = d->softmax_scale > 0.f ? d->softmax_scale : 1.0f / std::sqrt((float)d->head_dim);
     p.scale_log2 = scale * 1.4426950408889634f;
-    const int grid = (int)attention_ctas(N, d->n_heads);
+    const int grid = (int)std::min<int64_t>(attention_ctas(N, d->n_heads) * n_streams, sm_count());
     // few heads per launch (a GPU's share of a head-split frame, small models): the query tiles x
     // heads may leave SMs idle, so launch the instantiation that can split key ranges
-    const bool split = os.split.slots > 0 && d->n_heads <= kSplitMaxHeads;
-    cudaError_t e = split ? launch_pdl(fxr::attn::attention_kernel<T, true>, dim3(grid), dim3(fxr::attn::kThreads),
-                                       fxr::attn::kSmemBytes, stream, tq, tk, tv, p)
-                          : launch_pdl(fxr::attn::attention_kernel<T, false>, dim3(grid), dim3(fxr::attn::kThreads),
-                                       fxr::attn::kSmemBytes, stream, tq, tk, tv, p);
+    const bool split_ok = split.slots > 0 && d->n_heads <= kSplitMaxHeads;
+    cudaError_t e = split_ok ? launch_pdl(fxr::attn::attention_kernel<T, true>, dim3(grid), dim3(fxr::attn::kThreads),
+                                          fxr::attn::kSmemBytes, stream, maps, p)
+                             : launch_pdl(fxr::attn::attention_kernel<T, false>, dim3(grid), dim3(fxr::attn::kThreads),
+                                          fxr::attn::kSmemBytes, stream, maps, p);
     if (e != cudaSuccess) return cuda_status(e, "attention_kernel launch");
     return FXR_OK;
 }
 
 template <typename T>
-int32_t launch_gather(const fxr_frame_desc* d, const void* q, const void* k, const void* v,
-                      const int32_t* mask, const int32_t* idx, const int32_t* count,
-                      const int32_t* pos, const float* nq, const float* nk, void* qc, int64_t ld_qc,
-                      void* ck, void* cv, void* save, cudaStream_t stream) {
+int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc, const int32_t* count,
+                         const void* ck, const void* cv, const int32_t* idx, const OutSet& os,
+                         cudaStream_t stream) {
+    const AttnStreamArgs st{qc, ld_qc, count, ck, cv, idx, os.out};
+    return launch_attention_streams<T>(d, 1, &st, os.split, stream);
+}
+
+// Gather of n_streams frames of the same geometry (one launch; rows stream after stream).
+template <typename T>
+int32_t launch_gather_streams(const fxr_frame_desc* d, int32_t n_streams, const fxr::GatherStream* gs,
+                              const int32_t* pos, const float* nq, const float* nk, int64_t ld_qc,
+                              cudaStream_t stream) {
+    if (n_streams < 1 || n_streams > fxr::kMaxBatch) return fail(FXR_ERR_INVALID, "1..%d streams per launch", fxr::kMaxBatch);
     fxr::GatherArgs a{};
-    a.q = q;
-    a.k = k;
-    a.v = v;
-    a.mask = mask;
-    a.idx = idx;
-    a.count = count;
+    for (int32_t b = 0; b < n_streams; ++b) a.s[b] = gs[b];
+    a.n_streams = n_streams;
     a.pos = pos;
     a.norm_q = nq;
     a.norm_k = nk;
-    a.qc = qc;
-    a.cache_k = ck;
-    a.cache_v = cv;
-    a.save = save;
     a.ld_qkv = d->ld_qkv;
     a.ld_qc = ld_qc;
     a.ld_cache = d->ld_cache;
@@ -361,6 +377,15 @@ int32_t launch_gather(const fxr_frame_desc* d, const void* q, const void* k, con
                                stream, a, lay);
     if (e != cudaSuccess) return cuda_status(e, "gather_bulk_kernel launch");
     return FXR_OK;
+}
+
+template <typename T>
+int32_t launch_gather(const fxr_frame_desc* d, const void* q, const void* k, const void* v,
+                      const int32_t* mask, const int32_t* idx, const int32_t* count,
+                      const int32_t* pos, const float* nq, const float* nk, void* qc, int64_t ld_qc,
+                      void* ck, void* cv, void* save, cudaStream_t stream) {
+    const fxr::GatherStream gs{q, k, v, mask, idx, count, qc, ck, cv, save};
+    return launch_gather_streams<T>(d, 1, &gs, pos, nq, nk, ld_qc, stream);
 }
 
 }  // namespace
@@ -454,18 +479,26 @@ int32_t fxr_workspace_views(const fxr_frame_desc* desc, void* workspace, int32_t
     return FXR_OK;
 }
 
+// Compaction of n_streams frames (CTA b: stream b); the attention's split counters of the launch
+// start at zero.
+static int32_t launch_compact_streams(fxr::CompactArgs a, int32_t n_streams, int32_t n_tokens,
+                                      const SplitArea& split, void* stream) {
+    a.n = n_tokens;
+    a.zero = reinterpret_cast<uint4*>(split.cnt);
+    a.zero_vec = (int32_t)((size_t)split.slots * kSplitCntBytes / 16);
+    cudaError_t e = launch_pdl(fxr::compact_kernel, dim3(n_streams), dim3(fxr::kCompactThreads), 0,
+                               static_cast<cudaStream_t>(stream), a);
+    if (e != cudaSuccess) return cuda_status(e, "compact_kernel launch");
+    return FXR_OK;
+}
+
 static int32_t launch_compact(int32_t* mask, const uint8_t* valid, int32_t n_tokens, int32_t* idx,
                               int32_t* count, const SplitArea& split, void* stream) {
     if (n_tokens < 0) return fail(FXR_ERR_INVALID, "n_tokens < 0");
     if (!count || (n_tokens > 0 && (!mask || !idx))) return fail(FXR_ERR_INVALID, "null pointer");
-    // the attention's split counters of this frame start at zero
-    uint4* zero = reinterpret_cast<uint4*>(split.cnt);
-    const int32_t zero_vec = (int32_t)((size_t)split.slots * kSplitCntBytes / 16);
-    cudaError_t e = launch_pdl(fxr::compact_kernel, dim3(1), dim3(fxr::kCompactThreads), 0,
-                               static_cast<cudaStream_t>(stream), mask, valid, n_tokens, idx, count,
-                               zero, zero_vec);
-    if (e != cudaSuccess) return cuda_status(e, "compact_kernel launch");
-    return FXR_OK;
+    fxr::CompactArgs a{};
+    a.s[0] = fxr::CompactStream{mask, valid, idx, count};
+    return launch_compact_streams(a, 1, n_tokens, split, stream);
 }
 
 int32_t fxr_mask_compact(int32_t* mask, const uint8_t* valid, int32_t n_tokens, int32_t* idx,
@@ -538,6 +571,20 @@ int32_t fxr_attention_active(const fxr_frame_desc* desc, const void* qc, int64_t
     return launch_attention<__half>(desc, qc, ld_qc, count, cache_k, cache_v, idx, os, s);
 }
 
+static int32_t launch_restore_streams(const fxr_frame_desc* desc, fxr::RestoreArgs a, int32_t n_streams,
+                                     void* stream) {
+    const int64_t row_bytes = (int64_t)desc->n_heads * desc->head_dim * (int64_t)dtype_bytes(desc->dtype);
+    a.ld_cache_bytes = desc->ld_cache * (int64_t)dtype_bytes(desc->dtype);
+    a.row_vec = (int32_t)(row_bytes / 16);
+    a.n_tokens = desc->n_tokens;
+    // one CTA per SM at most: usually no row has mask 1 and the kernel only scans M mask values
+    const int grid = std::max(1, std::min(grid_rows(desc->n_tokens, 8), sm_count() / n_streams));
+    cudaError_t e = launch_pdl(fxr::restore_rows_kernel, dim3(grid, n_streams), dim3(256), 0,
+                               static_cast<cudaStream_t>(stream), a);
+    if (e != cudaSuccess) return cuda_status(e, "restore_rows_kernel launch");
+    return FXR_OK;
+}
+
 int32_t fxr_restore_rows(const fxr_frame_desc* desc, const int32_t* mask, const int32_t* idx,
                          const int32_t* count, const void* save, void* cache_k, void* cache_v,
                          void* stream) {
@@ -548,16 +595,10 @@ int32_t fxr_restore_rows(const fxr_frame_desc* desc, const int32_t* mask, const 
         return fail(FXR_ERR_INVALID, "null pointer argument");
     if (!aligned16(save) || !aligned16(cache_k) || !aligned16(cache_v))
         return fail(FXR_ERR_INVALID, "save/cache must be 16-byte aligned");
-    const int64_t row_bytes = (int64_t)desc->n_heads * desc->head_dim * (int64_t)dtype_bytes(desc->dtype);
-    // one CTA per SM at most: usually no row has mask 1 and the kernel only scans M mask values
-    const int grid = std::min(grid_rows(desc->n_tokens, 8), sm_count());
-    cudaError_t e = launch_pdl(fxr::restore_rows_kernel, dim3(grid), dim3(256), 0,
-                               static_cast<cudaStream_t>(stream), mask, idx, count,
-                               static_cast<const uint4*>(save), static_cast<char*>(cache_k),
-                               static_cast<char*>(cache_v), desc->ld_cache * (int64_t)dtype_bytes(desc->dtype),
-                               (int32_t)(row_bytes / 16), desc->n_tokens);
-    if (e != cudaSuccess) return cuda_status(e, "restore_rows_kernel launch");
-    return FXR_OK;
+    fxr::RestoreArgs a{};
+    a.s[0] = fxr::RestoreStream{mask, idx, count, static_cast<const uint4*>(save), static_cast<char*>(cache_k),
+                                static_cast<char*>(cache_v)};
+    return launch_restore_streams(desc, a, 1, stream);
 }
 
 static int32_t rows_copy(bool scatter, const void* src, int64_t ld_src, const int32_t* idx,
@@ -748,6 +789,72 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void*
              : launch_attention<__half>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s);
     if (st != FXR_OK) return st;
     return fxr_restore_rows(desc, mask, w.idx, w.count, w.save, cache_k, cache_v, stream);
+}
+
+size_t fxr_batch_workspace_size(const fxr_frame_desc* desc, int32_t n_streams) {
+    if (!desc || dtype_bytes(desc->dtype) == 0 || desc->n_heads <= 0 || desc->head_dim <= 0 || n_streams < 0)
+        return 0;
+    return (size_t)std::min(n_streams, (int32_t)FXR_MAX_BATCH) * carve(desc, nullptr).total;
+}
+
+}  // extern "C"
+
+template <typename T>
+static int32_t batch_group(const fxr_frame_desc* desc, int32_t nb, const fxr_stream_frame* f,
+                           const int32_t* pos, const float* nq, const float* nk, char* ws, size_t base,
+                           cudaStream_t s) {
+    fxr::CompactArgs ca{};
+    fxr::GatherStream gs[fxr::kMaxBatch];
+    AttnStreamArgs as[fxr::kMaxBatch];
+    fxr::RestoreArgs ra{};
+    int64_t ld_qc = 0;
+    for (int32_t b = 0; b < nb; ++b) {
+        const Views w = carve(desc, ws + (size_t)b * base);
+        const fxr_stream_frame& x = f[b];
+        if (!x.q || !x.k || !x.v || !x.mask || !x.cache_k || !x.cache_v || !x.out)
+            return fail(FXR_ERR_INVALID, "stream %d: null pointer", b);
+        if (!aligned16(x.q) || !aligned16(x.k) || !aligned16(x.v) || !aligned16(x.cache_k) ||
+            !aligned16(x.cache_v) || !aligned16(x.out))
+            return fail(FXR_ERR_INVALID, "stream %d: buffers must be 16-byte aligned", b);
+        ca.s[b] = fxr::CompactStream{x.mask, x.valid, w.idx, w.count};
+        gs[b] = fxr::GatherStream{x.q, x.k, x.v, x.mask, w.idx, w.count, w.qc, x.cache_k, x.cache_v, w.save};
+        as[b] = AttnStreamArgs{w.qc, w.ld_qc, w.count, x.cache_k, x.cache_v, w.idx, x.out};
+        ra.s[b] = fxr::RestoreStream{x.mask, w.idx, w.count, static_cast<const uint4*>(w.save),
+                                     static_cast<char*>(x.cache_k), static_cast<char*>(x.cache_v)};
+        ld_qc = w.ld_qc;
+    }
+    int32_t st;
+    if ((st = launch_compact_streams(ca, nb, desc->n_tokens, SplitArea{}, s)) != FXR_OK) return st;
+    if ((st = launch_gather_streams<T>(desc, nb, gs, pos, nq, nk, ld_qc, s)) != FXR_OK) return st;
+    if ((st = launch_attention_streams<T>(desc, nb, as, SplitArea{}, s)) != FXR_OK) return st;
+    return launch_restore_streams(desc, ra, nb, s);
+}
+
+extern "C" {
+
+int32_t fxr_frame_forward_batch(const fxr_frame_desc* desc, int32_t n_streams, const fxr_stream_frame* frames,
+                                const int32_t* pos, const float* norm_q, const float* norm_k, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+    int32_t st = check_desc(desc, true);
+    if (st != FXR_OK) return st;
+    if (n_streams < 0) return fail(FXR_ERR_INVALID, "n_streams < 0");
+    if (n_streams == 0 || desc->n_tokens == 0) return FXR_OK;
+    if (!frames || !workspace || !norm_q || !norm_k || (desc->rope_n_axes > 0 && !pos))
+        return fail(FXR_ERR_INVALID, "null pointer argument");
+    const size_t base = carve(desc, nullptr).total;
+    const size_t need = fxr_batch_workspace_size(desc, n_streams);
+    if (workspace_bytes < need) return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, need);
+    if (!aligned16(workspace)) return fail(FXR_ERR_INVALID, "workspace must be 16-byte aligned");
+    static_assert(FXR_MAX_BATCH == fxr::kMaxBatch, "batch limits");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (int32_t c0 = 0; c0 < n_streams; c0 += FXR_MAX_BATCH) {
+        const int32_t nb = std::min(n_streams - c0, (int32_t)FXR_MAX_BATCH);
+        st = desc->dtype == FXR_BF16
+                 ? batch_group<__nv_bfloat16>(desc, nb, frames + c0, pos, norm_q, norm_k, static_cast<char*>(workspace), base, s)
+                 : batch_group<__half>(desc, nb, frames + c0, pos, norm_q, norm_k, static_cast<char*>(workspace), base, s);
+        if (st != FXR_OK) return st;
+    }
+    return FXR_OK;
 }
 
 // Exchange CTAs of a head-split frame (arrivals each GPU with heads sends per frame); every GPU of

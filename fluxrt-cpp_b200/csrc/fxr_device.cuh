@@ -33,6 +33,9 @@ __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Independent edit streams (frames of one geometry) processed by one launch, at most.
+constexpr int kMaxBatch = 8;
+
 // Release-ordered add at system scope (visible to other GPUs after the writes it orders).
 __device__ __forceinline__ void red_release_sys_add(uint32_t* addr, uint32_t v) {
     asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");

@@ -28,17 +28,34 @@ constexpr int kCompactWarps = kCompactThreads / 32;
 constexpr int kCompactGroups = 32;                              // per warp and chunk, at most
 constexpr int kCompactChunk = kCompactWarps * kCompactGroups * 32;
 
-__global__ void __launch_bounds__(kCompactThreads, 1)
-compact_kernel(int32_t* __restrict__ mask, const uint8_t* __restrict__ valid, int32_t n,
-               int32_t* __restrict__ idx, int32_t* __restrict__ count, uint4* __restrict__ zero,
-               int32_t zero_vec) {
+struct CompactStream {
+    int32_t* mask;
+    const uint8_t* valid;
+    int32_t* idx;
+    int32_t* count;
+};
+
+struct CompactArgs {
+    CompactStream s[kMaxBatch];   // CTA b compacts stream b
+    int32_t n;
+    uint4* zero;                  // the attention's key-split arrival counters, zeroed by CTA 0
+    int32_t zero_vec;
+};
+
+__global__ void __launch_bounds__(kCompactThreads, 1) compact_kernel(const __grid_constant__ CompactArgs a) {
+    int32_t* __restrict__ mask = a.s[blockIdx.x].mask;
+    const uint8_t* __restrict__ valid = a.s[blockIdx.x].valid;
+    int32_t* __restrict__ idx = a.s[blockIdx.x].idx;
+    int32_t* __restrict__ count = a.s[blockIdx.x].count;
+    const int32_t n = a.n;
     __shared__ int32_t warp_tot[kCompactWarps];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t lt = (1u << lane) - 1u;
     pdl_launch_dependents();
     pdl_wait();  // the previous frame's kernels may still read mask / idx / count
     // the attention's key-split arrival counters of this frame (zero_vec 16-byte words)
-    for (int32_t e = threadIdx.x; e < zero_vec; e += kCompactThreads) zero[e] = make_uint4(0, 0, 0, 0);
+    if (blockIdx.x == 0)
+        for (int32_t e = threadIdx.x; e < a.zero_vec; e += kCompactThreads) a.zero[e] = make_uint4(0, 0, 0, 0);
     int32_t base = 0;
     for (int32_t c0 = 0; c0 < n; c0 += kCompactChunk) {
         const int32_t n_chunk = min(n - c0, kCompactChunk);
@@ -112,20 +129,25 @@ struct RopeTable {
     int8_t axis[kPairs];     // axis of pair j, -1 for none (identity)
 };
 
-struct GatherArgs {
+struct GatherStream {           // one stream's buffers
     const void* q;
     const void* k;
     const void* v;
     const int32_t* mask;
     const int32_t* idx;
     const int32_t* count;
-    const int32_t* pos;
-    const float* norm_q;
-    const float* norm_k;
     void* qc;
     void* cache_k;
     void* cache_v;
     void* save;
+};
+
+struct GatherArgs {
+    GatherStream s[kMaxBatch];
+    int32_t n_streams;
+    const int32_t* pos;
+    const float* norm_q;
+    const float* norm_k;
     int64_t ld_qkv, ld_qc, ld_cache;
     int32_t n_tokens, n_heads, n_axes;
     float eps;
@@ -201,7 +223,7 @@ constexpr int kBulkGroups = 6;
 constexpr int kBulkProducerWarp = kBulkGroupWarps * kBulkGroups;
 constexpr int kBulkThreads = (kBulkProducerWarp + 1) * 32;
 constexpr int kBulkMaxStages = 32;
-constexpr int kBulkInfoWords = 8;   // per stage: token, mode, position ids[4], pad
+constexpr int kBulkInfoWords = 8;   // per stage: token, mode, position ids[4], stream, compact row
 
 struct BulkLayout {
     uint32_t stage_bytes;   // 3 rows (Q, K, V) of C elements, 128-byte aligned
@@ -233,7 +255,10 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
     pdl_launch_dependents();
     pdl_wait();  // count / idx / mask come from the compaction
 
-    const int32_t M = *a.count;
+    // executed rows of all streams, stream after stream: row r of the launch is row r - pre[b] of
+    // stream b (pre = exclusive prefix of the streams' counts)
+    int32_t M = 0;
+    for (int b = 0; b < a.n_streams; ++b) M += *a.s[b].count;
     const int64_t C = (int64_t)a.n_heads * kHeadDim;
     const uint32_t row_bytes = (uint32_t)(C * (int64_t)sizeof(T));
     const int32_t rows_here =
@@ -245,15 +270,17 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
         int32_t issued = 0;
         for (int32_t kb = 0; ok && kb < rows_here; kb += 32) {
             const int32_t kl = kb + lane;
-            int32_t i = -1;
+            int32_t i = -1, sb = 0, m = 0;
             if (kl < rows_here) {
-                i = __ldg(a.idx + (int32_t)blockIdx.x + kl * (int32_t)gridDim.x);
+                m = (int32_t)blockIdx.x + kl * (int32_t)gridDim.x;
+                while (sb + 1 < a.n_streams && m >= *a.s[sb].count) m -= *a.s[sb++].count;
+                i = __ldg(a.s[sb].idx + m);
                 if (i < 0 || i >= a.n_tokens) i = -1;
             }
             // bookkeeping loads of the 32 rows, in flight while the row copies are issued
             int32_t mode = 0, p[4] = {0, 0, 0, 0};
             if (i >= 0) {
-                mode = __ldg(a.mask + i);
+                mode = __ldg(a.s[sb].mask + i);
 #pragma unroll
                 for (int ax = 0; ax < 4; ++ax)
                     if (ax < a.n_axes) p[ax] = __ldg(a.pos + (int64_t)i * a.n_axes + ax);
@@ -267,14 +294,17 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
                     break;
                 }
                 const int32_t ti = __shfl_sync(0xffffffffu, i, j);
+                const int32_t tb = __shfl_sync(0xffffffffu, sb, j);
+                const int32_t tmr = __shfl_sync(0xffffffffu, m, j);
                 if (lane == 0) {
                     if (ti >= 0) {
                         const uint32_t dst = smem_u32(ring + st * lay.stage_bytes);
                         const int64_t off = (int64_t)ti * a.ld_qkv;
+                        const GatherStream& gs = a.s[tb];
                         mbar_arrive_expect_tx(full(st), 3u * row_bytes);
-                        bulk_load(dst, static_cast<const T*>(a.q) + off, row_bytes, full(st));
-                        bulk_load(dst + row_bytes, static_cast<const T*>(a.k) + off, row_bytes, full(st));
-                        bulk_load(dst + 2 * row_bytes, static_cast<const T*>(a.v) + off, row_bytes, full(st));
+                        bulk_load(dst, static_cast<const T*>(gs.q) + off, row_bytes, full(st));
+                        bulk_load(dst + row_bytes, static_cast<const T*>(gs.k) + off, row_bytes, full(st));
+                        bulk_load(dst + 2 * row_bytes, static_cast<const T*>(gs.v) + off, row_bytes, full(st));
                     } else {
                         atomicOr(&g_error_word, kErrBounds);
                         mbar_arrive(full(st));
@@ -290,6 +320,8 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
                     inf[1] = tm;
 #pragma unroll
                     for (int ax = 0; ax < 4; ++ax) inf[2 + ax] = tp[ax];
+                    inf[6] = tb;
+                    inf[7] = tmr;
                     mbar_arrive(full(st));
                 }
                 __syncwarp();
@@ -314,10 +346,6 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
 #pragma unroll
             for (int t = 0; t < 4; ++t) w2[t] = make_float2(__ldg(wsrc + 2 * t), __ldg(wsrc + 2 * t + 1));
         }
-        T* __restrict__ QC = static_cast<T*>(a.qc);
-        T* __restrict__ CK = static_cast<T*>(a.cache_k);
-        T* __restrict__ CV = static_cast<T*>(a.cache_v);
-        T* __restrict__ SV = static_cast<T*>(a.save);
         const bool bulk_lane = gw == 0 && lane == 0;
         const int gtid = gw * 32 + lane;
         for (int32_t k = grp; k < rows_here; k += kBulkGroups) {
@@ -325,7 +353,12 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
             if (!__all_sync(0xffffffffu, mbar_wait_suspend(full(st), use & 1, abort))) break;
             const int32_t* inf = info + st * kBulkInfoWords;
             const int32_t i = inf[0], mode = inf[1];
-            const int32_t r = (int32_t)blockIdx.x + k * (int32_t)gridDim.x;
+            const GatherStream& gs = a.s[inf[6]];
+            const int32_t r = inf[7];                       // compact row within its stream
+            T* __restrict__ QC = static_cast<T*>(gs.qc);
+            T* __restrict__ CK = static_cast<T*>(gs.cache_k);
+            T* __restrict__ CV = static_cast<T*>(gs.cache_v);
+            T* __restrict__ SV = static_cast<T*>(gs.save);
             const uint8_t* stage = ring + st * lay.stage_bytes;
             if (i >= 0) {
                 if (mode == 1 && SV != nullptr) {
@@ -393,11 +426,31 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
 // ---------------------------------------------------------------------------------------------
 // Restore of mask==1 cache rows (execute without cache update) from the save buffer.
 // ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
-restore_rows_kernel(const int32_t* __restrict__ mask, const int32_t* __restrict__ idx,
-                    const int32_t* __restrict__ count, const uint4* __restrict__ save,
-                    char* __restrict__ cache_k, char* __restrict__ cache_v, int64_t ld_cache_bytes,
-                    int32_t row_vec, int32_t n_tokens) {
+struct RestoreStream {
+    const int32_t* mask;
+    const int32_t* idx;
+    const int32_t* count;
+    const uint4* save;
+    char* cache_k;
+    char* cache_v;
+};
+
+struct RestoreArgs {
+    RestoreStream s[kMaxBatch];   // grid row blockIdx.y restores stream blockIdx.y
+    int64_t ld_cache_bytes;
+    int32_t row_vec, n_tokens;
+};
+
+__global__ void __launch_bounds__(256) restore_rows_kernel(const __grid_constant__ RestoreArgs a) {
+    const RestoreStream& rs = a.s[blockIdx.y];
+    const int32_t* __restrict__ mask = rs.mask;
+    const int32_t* __restrict__ idx = rs.idx;
+    const int32_t* __restrict__ count = rs.count;
+    const uint4* __restrict__ save = rs.save;
+    char* __restrict__ cache_k = rs.cache_k;
+    char* __restrict__ cache_v = rs.cache_v;
+    const int64_t ld_cache_bytes = a.ld_cache_bytes;
+    const int32_t row_vec = a.row_vec, n_tokens = a.n_tokens;
     const int lane = threadIdx.x & 31;
     // The last kernel of a frame: it lets its successor start only once the attention is over, since
     // that successor may be code outside this library (a collective, a copy) that reads the frame's

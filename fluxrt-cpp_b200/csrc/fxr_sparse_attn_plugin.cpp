@@ -186,9 +186,11 @@ public:
         return true;
     }
 
-    size_t workspace_bytes_for(int32_t N, int32_t dtype) const {
+    // The frames of all B streams run as one batched set of launches (fxr_frame_forward_batch);
+    // the engine's read-only masks are copied behind that workspace.
+    size_t workspace_bytes_for(int32_t B, int32_t N, int32_t dtype) const {
         fxr_frame_desc d = desc(N, dtype);
-        return fxr_workspace_size(&d) + align256((size_t)N * sizeof(int32_t));
+        return fxr_batch_workspace_size(&d, B) + (size_t)B * align256((size_t)N * sizeof(int32_t));
     }
 
     void release() {
@@ -239,29 +241,35 @@ public:
         if (B != B_ || N != N_ || dtype != dtype_) return plugin_fail("enqueue shapes differ from configure");
         if (!inputs || !outputs || !workspace) return plugin_fail("null tensor or workspace pointer");
         const fxr_frame_desc d = desc(N, dtype);
-        const size_t frame_ws = fxr_workspace_size(&d);
-        if (workspace_bytes < workspace_bytes_for(N, dtype)) return plugin_fail("workspace too small");
+        const size_t frames_ws = fxr_batch_workspace_size(&d, B);
+        if (workspace_bytes < workspace_bytes_for(B, N, dtype)) return plugin_fail("workspace too small");
         // The engine's input tensors are read-only; the preprocess rewrites the mask in place, so
-        // each stream's mask is first copied into the workspace.
-        int32_t* mask_copy = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + frame_ws);
+        // every stream's mask is first copied into the workspace (one copy for all streams).
+        char* mask_area = static_cast<char*>(workspace) + frames_ws;
+        const size_t mask_stride = align256((size_t)N * sizeof(int32_t));
+        for (int32_t b = 0; b < B; ++b)
+            if (cudaMemcpyAsync(mask_area + b * mask_stride, static_cast<const int32_t*>(inputs[3]) + (size_t)b * N,
+                                (size_t)N * sizeof(int32_t), cudaMemcpyDeviceToDevice, stream) != cudaSuccess)
+                return plugin_fail("mask copy failed");
         const size_t elem = 2, C = (size_t)num_heads * head_dim;
+        std::vector<fxr_stream_frame> fr((size_t)B);
         for (int32_t b = 0; b < B; ++b) {
             const size_t off = (size_t)b * N * C * elem;
-            const int32_t* mask_b = static_cast<const int32_t*>(inputs[3]) + (size_t)b * N;
-            if (cudaMemcpyAsync(mask_copy, mask_b, (size_t)N * sizeof(int32_t), cudaMemcpyDeviceToDevice,
-                                stream) != cudaSuccess)
-                return plugin_fail("mask copy failed");
-            int32_t st = fxr_frame_forward(&d, static_cast<const char*>(inputs[0]) + off,
-                                           static_cast<const char*>(inputs[1]) + off,
-                                           static_cast<const char*>(inputs[2]) + off, mask_copy,
-                                           static_cast<const uint8_t*>(valid_[b]), static_cast<const int32_t*>(inputs[4]),
-                                           static_cast<const float*>(inputs[5]),
-                                           static_cast<const float*>(inputs[6]), ck_[b], cv_[b],
-                                           static_cast<char*>(outputs[0]) + off, workspace, frame_ws, stream);
-            if (st == FXR_OK) st = fxr_mark_updated(mask_copy, static_cast<uint8_t*>(valid_[b]), n_txt, N, stream);
-            if (st != FXR_OK) return -1;  // fxr_last_error_string() already describes it
+            fr[b].q = static_cast<const char*>(inputs[0]) + off;
+            fr[b].k = static_cast<const char*>(inputs[1]) + off;
+            fr[b].v = static_cast<const char*>(inputs[2]) + off;
+            fr[b].mask = reinterpret_cast<int32_t*>(mask_area + b * mask_stride);
+            fr[b].valid = static_cast<const uint8_t*>(valid_[b]);
+            fr[b].cache_k = ck_[b];
+            fr[b].cache_v = cv_[b];
+            fr[b].out = static_cast<char*>(outputs[0]) + off;
         }
-        return 0;
+        int32_t st = fxr_frame_forward_batch(&d, B, fr.data(), static_cast<const int32_t*>(inputs[4]),
+                                             static_cast<const float*>(inputs[5]),
+                                             static_cast<const float*>(inputs[6]), workspace, frames_ws, stream);
+        for (int32_t b = 0; st == FXR_OK && b < B; ++b)
+            st = fxr_mark_updated(fr[b].mask, static_cast<uint8_t*>(valid_[b]), n_txt, N, stream);
+        return st == FXR_OK ? 0 : -1;  // fxr_last_error_string() describes a failure
     }
 
     int32_t cache(int32_t b, void** k, void** v, uint8_t** valid) {
@@ -373,7 +381,7 @@ size_t fxr_plugin_workspace_size(const fxr_plugin* p, const fxr_tensor_desc* in,
     std::string err;
     int32_t B, N, dt;
     if (!p->core.check_shapes(in, nb_in, &B, &N, &dt, &err)) return 0;
-    return p->core.workspace_bytes_for(N, dt);
+    return p->core.workspace_bytes_for(B, N, dt);
 }
 
 int32_t fxr_plugin_enqueue(fxr_plugin* p, const fxr_tensor_desc* in, const fxr_tensor_desc* out,

@@ -37,7 +37,10 @@ EXPORTED = [
     "fxr_head_group_wait", "fxr_ipc_alloc", "fxr_ipc_open", "fxr_ipc_close", "fxr_ipc_free",
     "fxr_nccl_unique_id", "fxr_nccl_comm_init", "fxr_nccl_comm_destroy",
     "fxr_heads_nccl_workspace_size", "fxr_allgather_heads", "fxr_frame_forward_heads_nccl",
+    "fxr_batch_workspace_size", "fxr_frame_forward_batch",
 ]
+
+FXR_MAX_BATCH = 8
 
 FXR_MAX_RANKS = 8
 
@@ -61,6 +64,11 @@ class TensorDesc(ctypes.Structure):
     """Mirror of fxr_tensor_desc (include/fxr_plugin.h)."""
     _fields_ = [("nb_dims", ctypes.c_int32), ("dtype", ctypes.c_int32),
                 ("dims", ctypes.c_int64 * 8)]
+
+
+class StreamFrame(ctypes.Structure):
+    """Mirror of fxr_stream_frame (include/fxr.h)."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ("q", "k", "v", "mask", "valid", "cache_k", "cache_v", "out")]
 
 
 class HeadGroup(ctypes.Structure):
@@ -135,6 +143,10 @@ def load(path: str | None = None) -> ctypes.CDLL:
     L.fxr_frame_forward.argtypes = [ctypes.POINTER(FrameDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]
     L.fxr_frame_forward_noalloc.argtypes = [ctypes.POINTER(FrameDesc)] + [_vp] * 12
+    L.fxr_batch_workspace_size.argtypes = [ctypes.POINTER(FrameDesc), _i32]
+    L.fxr_batch_workspace_size.restype = ctypes.c_size_t
+    L.fxr_frame_forward_batch.argtypes = [ctypes.POINTER(FrameDesc), _i32, ctypes.POINTER(StreamFrame),
+                                          _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]
     _hg = ctypes.POINTER(HeadGroup)
     L.fxr_head_group_init.argtypes = [_hg, _i32, _i32, _i32, _i32]
     L.fxr_frame_forward_heads.argtypes = [ctypes.POINTER(FrameDesc), _hg] + [_vp] * 11 + \
@@ -571,3 +583,22 @@ def frame_forward_heads_nccl(cfg: FrameConfig, g: HeadGroup, comm: int, m_cap: i
         _ptr(valid), _ptr(pos), _ptr(norm_q), _ptr(norm_k), _ptr(cache_k), _ptr(cache_v),
         _ptr(out), _ptr(workspace), workspace.numel() * workspace.element_size(),
         _stream(stream)))
+
+
+# ---- independent edit streams in one set of launches --------------------------------------------
+def batch_workspace_size(cfg: FrameConfig, n_streams: int) -> int:
+    d = cfg.desc()
+    return load().fxr_batch_workspace_size(ctypes.byref(d), n_streams)
+
+
+def frame_forward_batch(cfg: FrameConfig, streams, pos, norm_q, norm_k, workspace, stream=None):
+    """streams: list of dicts with q, k, v, mask, valid (or None), cache_k, cache_v, out tensors."""
+    d = cfg.desc()
+    arr = (StreamFrame * max(len(streams), 1))()
+    for b, f in enumerate(streams):
+        arr[b] = StreamFrame(*[_ptr(f.get(k)) for k in ("q", "k", "v", "mask", "valid", "cache_k",
+                                                         "cache_v", "out")])
+    _check(load().fxr_frame_forward_batch(ctypes.byref(d), len(streams), arr, _ptr(pos), _ptr(norm_q),
+                                          _ptr(norm_k), _ptr(workspace),
+                                          workspace.numel() * workspace.element_size(),
+                                          _stream(stream)))

@@ -203,6 +203,35 @@ int32_t fxr_frame_forward_noalloc(const fxr_frame_desc* desc,
                                   const float* norm_q, const float* norm_k,
                                   void* cache_k, void* cache_v, void* out, void* stream);
 
+/* ---- independent edit streams in one set of launches -------------------------------------------
+ * n_streams frames of the same geometry (the plugin's batch dimension; config 4 runs 8 streams of
+ * 768x768): one compaction launch (a CTA per stream), one gather launch over every stream's
+ * executed rows, one attention launch over every stream's (query tile, head) units — which fills
+ * the GPU where one small frame leaves SMs idle — and one restore launch; more than FXR_MAX_BATCH
+ * streams run as consecutive groups. Streams share the geometry, pos and the norm weights; each
+ * has its own inputs, mask, validity, K/V cache and output. Results equal per-stream
+ * fxr_frame_forward calls bit for bit. */
+#define FXR_MAX_BATCH 8
+
+typedef struct fxr_stream_frame {
+    const void* q;
+    const void* k;
+    const void* v;
+    int32_t* mask;            /* preprocessed in place */
+    const uint8_t* valid;     /* NULL = every row valid */
+    void* cache_k;
+    void* cache_v;
+    void* out;
+} fxr_stream_frame;
+
+/* Workspace of fxr_frame_forward_batch: min(n_streams, FXR_MAX_BATCH) frame workspaces. */
+size_t fxr_batch_workspace_size(const fxr_frame_desc* desc, int32_t n_streams);
+
+int32_t fxr_frame_forward_batch(const fxr_frame_desc* desc, int32_t n_streams,
+                                const fxr_stream_frame* frames, const int32_t* pos,
+                                const float* norm_q, const float* norm_k,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
 /* Device pointers into the workspace (for callers that want idx / count / compact Q). */
 int32_t fxr_workspace_views(const fxr_frame_desc* desc, void* workspace, int32_t** idx,
                             int32_t** count, void** qc, int64_t* ld_qc, void** save);

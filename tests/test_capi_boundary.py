@@ -86,3 +86,15 @@ def test_product_path_has_no_cpu_fallback():
             if f.endswith((".py", ".cu", ".cuh", ".cpp", ".h")):
                 text = open(os.path.join(dirpath, f)).read()
                 assert "oracle" not in text.lower(), f
+
+
+def test_batch_workspace_and_arguments(lib):
+    cfg = fxr.FrameConfig(n_tokens=2816, n_text=512)
+    one = fxr.batch_workspace_size(cfg, 1)
+    assert one > 0 and fxr.batch_workspace_size(cfg, 8) == 8 * one
+    assert fxr.batch_workspace_size(cfg, 20) == 8 * one          # groups of 8 reuse it
+    assert fxr.batch_workspace_size(cfg, -1) == 0
+    d = cfg.desc()
+    assert lib.fxr_frame_forward_batch(ctypes.byref(d), 0, None, None, None, None, None, 0, None) == fxr.FXR_OK
+    st = lib.fxr_frame_forward_batch(ctypes.byref(d), 2, None, None, None, None, None, 0, None)
+    assert st == fxr.FXR_ERR_INVALID

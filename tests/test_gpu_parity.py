@@ -415,3 +415,30 @@ def test_frame_output_independent_of_stale_workspace(cuda, fill):
         outs.append(t)
     for k in ("out", "cache_k", "cache_v"):
         assert torch.equal(outs[0][k], outs[1][k]), k
+
+
+@pytest.mark.parametrize("n_streams,wl,heads", [(3, W.C4, 24), (9, W.C1, 12), (1, W.C2, 12)])
+def test_frame_forward_batch_matches_per_stream_frames(cuda, n_streams, wl, heads):
+    """Streams in one set of launches equal per-stream frames bit for bit (each (query tile, head)
+    unit is computed the same way whichever launch holds it); 9 streams run as groups of 8 + 1.
+    More than 8 heads per launch, so that neither path splits key ranges."""
+    w = small(wl, heads)
+    cfg = cfg_of(w)
+    pos = dev(W.positions(w), "i32")
+    frs = [_with_exec_only(W.make_frame(w, seed=300 + b), seed=400 + b) for b in range(n_streams)]
+    nq, nk = dev(frs[0]["norm_q"]), dev(frs[0]["norm_k"])
+    rng = np.random.default_rng(5)
+    valids = [torch.from_numpy((rng.random(w.n_tokens) < 0.9).astype(np.uint8)).cuda()
+              for _ in range(n_streams)]
+    a = [_frame_tensors(w, fr) for fr in frs]
+    b = [_frame_tensors(w, fr) for fr in frs]
+    ws = torch.empty(fxr.batch_workspace_size(cfg, n_streams), dtype=torch.uint8, device="cuda")
+    fxr.frame_forward_batch(cfg, [dict(t, valid=valids[i]) for i, t in enumerate(a)], pos, nq, nk, ws)
+    wsf = torch.empty(fxr.workspace_size(cfg), dtype=torch.uint8, device="cuda")
+    for i, t in enumerate(b):
+        fxr.frame_forward(cfg, t["q"], t["k"], t["v"], t["mask"], valids[i], pos, nq, nk,
+                          t["cache_k"], t["cache_v"], t["out"], wsf)
+    sync_ok()
+    for i in range(n_streams):
+        for k in ("out", "cache_k", "cache_v", "mask"):
+            assert torch.equal(a[i][k], b[i][k]), (i, k)

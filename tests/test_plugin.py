@@ -90,11 +90,11 @@ def test_supports_format_combination(lib):
     assert not p.supports(3, io + [fxr.tensor_desc((1, 1536, 512), BF16)])
 
 
-def test_workspace_is_frame_workspace_plus_mask_copy(lib):
+def test_workspace_is_batch_workspace_plus_mask_copies(lib):
     p = fxr.SparseAttnPlugin(num_heads=24, n_txt=512)
     ws = p.workspace_size(descs(4, 4608, 24))
-    frame = fxr.workspace_size(fxr.FrameConfig(n_tokens=4608, n_text=512))
-    assert ws == frame + (4608 * 4 + 255) // 256 * 256
+    frames = fxr.batch_workspace_size(fxr.FrameConfig(n_tokens=4608, n_text=512), 4)
+    assert ws == frames + 4 * ((4608 * 4 + 255) // 256 * 256)
     assert p.workspace_size(descs(4, 4608, 23)) == 0
 
 
