@@ -15,6 +15,7 @@
 #include "fxr_attention.cuh"
 #include "fxr_compat_kernels.cuh"
 #include "fxr_device.cuh"
+#include "fxr_gemm.cuh"
 #include "fxr_mem_kernels.cuh"
 
 // Built-in frame scratch of fxr_frame_forward_noalloc (see that function). 96 MiB holds the
@@ -118,12 +119,12 @@ EncodeTiledFn encode_fn() {
 // 2-D map over a row-major [rows, cols] 16-bit matrix with row stride ld (elements); box 64 x 128
 // (one 128-byte swizzle span wide), 128-byte swizzle, zero fill out of bounds.
 int32_t make_tmap(CUtensorMap* map, const void* ptr, int32_t dtype, int64_t cols, int64_t rows,
-                  int64_t ld) {
+                  int64_t ld, uint32_t box_rows = 128) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return fail(FXR_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t box[2] = {64, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUtensorMapDataType t =
         dtype == FXR_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -789,6 +790,63 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void*
              : launch_attention<__half>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s);
     if (st != FXR_OK) return st;
     return fxr_restore_rows(desc, mask, w.idx, w.count, w.save, cache_k, cache_v, stream);
+}
+
+int32_t fxr_qkv_project(const fxr_frame_desc* desc, const void* hidden, int64_t ld_hidden, int32_t k_dim,
+                        const void* w_qkv, const float* bias, const int32_t* idx, const int32_t* count,
+                        void* q, void* k, void* v, void* stream) {
+    int32_t st = check_desc(desc, true);
+    if (st != FXR_OK) return st;
+    const int64_t C = (int64_t)desc->n_heads * desc->head_dim;
+    if (k_dim <= 0 || k_dim % fxr::gemm::kBK != 0)
+        return fail(FXR_ERR_UNSUPPORTED, "k_dim %d must be a positive multiple of %d", k_dim, fxr::gemm::kBK);
+    if (C % fxr::gemm::kBN != 0)
+        return fail(FXR_ERR_UNSUPPORTED, "n_heads * head_dim = %lld must be a multiple of %d", (long long)C,
+                    fxr::gemm::kBN);
+    if (ld_hidden < k_dim || ld_hidden % 8) return fail(FXR_ERR_INVALID, "ld_hidden must be >= k_dim and a multiple of 8");
+    if (desc->n_tokens == 0) return FXR_OK;
+    if (!hidden || !w_qkv || !idx || !count || !q || !k || !v) return fail(FXR_ERR_INVALID, "null pointer argument");
+    if (!aligned16(hidden) || !aligned16(w_qkv) || !aligned16(q) || !aligned16(k) || !aligned16(v))
+        return fail(FXR_ERR_INVALID, "buffers must be 16-byte aligned");
+    static bool configured[kMaxDevices][2] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int ti = desc->dtype == FXR_BF16 ? 0 : 1;
+    if (dev >= 0 && dev < kMaxDevices && !configured[dev][ti]) {
+        cudaError_t e = ti == 0 ? cudaFuncSetAttribute(fxr::gemm::qkv_gather_gemm_kernel<__nv_bfloat16>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       (int)fxr::gemm::kSmemBytes)
+                                : cudaFuncSetAttribute(fxr::gemm::qkv_gather_gemm_kernel<__half>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       (int)fxr::gemm::kSmemBytes);
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(qkv gemm)");
+        configured[dev][ti] = true;
+    }
+    CUtensorMap tw;
+    if ((st = make_tmap(&tw, w_qkv, desc->dtype, k_dim, 3 * C, k_dim, fxr::gemm::kBN)) != FXR_OK) return st;
+    fxr::gemm::Args a{};
+    a.x = hidden;
+    a.idx = idx;
+    a.count = count;
+    a.bias = bias;
+    a.y[0] = q;
+    a.y[1] = k;
+    a.y[2] = v;
+    a.ld_x = ld_hidden;
+    a.ld_y = desc->ld_qkv;
+    a.k_dim = k_dim;
+    a.n_out = (int32_t)(3 * C);
+    a.c_part = (int32_t)C;
+    a.n_tokens = desc->n_tokens;
+    const int64_t max_tiles = (desc->n_tokens + fxr::gemm::kBM - 1) / fxr::gemm::kBM * (3 * C / fxr::gemm::kBN);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_tiles, sm_count()));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = ti == 0 ? launch_pdl(fxr::gemm::qkv_gather_gemm_kernel<__nv_bfloat16>, dim3(grid),
+                                         dim3(fxr::gemm::kThreads), fxr::gemm::kSmemBytes, s, tw, a)
+                            : launch_pdl(fxr::gemm::qkv_gather_gemm_kernel<__half>, dim3(grid),
+                                         dim3(fxr::gemm::kThreads), fxr::gemm::kSmemBytes, s, tw, a);
+    if (e != cudaSuccess) return cuda_status(e, "qkv_gather_gemm_kernel launch");
+    return FXR_OK;
 }
 
 size_t fxr_batch_workspace_size(const fxr_frame_desc* desc, int32_t n_streams) {

@@ -37,7 +37,7 @@ EXPORTED = [
     "fxr_head_group_wait", "fxr_ipc_alloc", "fxr_ipc_open", "fxr_ipc_close", "fxr_ipc_free",
     "fxr_nccl_unique_id", "fxr_nccl_comm_init", "fxr_nccl_comm_destroy",
     "fxr_heads_nccl_workspace_size", "fxr_allgather_heads", "fxr_frame_forward_heads_nccl",
-    "fxr_batch_workspace_size", "fxr_frame_forward_batch",
+    "fxr_batch_workspace_size", "fxr_frame_forward_batch", "fxr_qkv_project",
 ]
 
 FXR_MAX_BATCH = 8
@@ -143,6 +143,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
     L.fxr_frame_forward.argtypes = [ctypes.POINTER(FrameDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]
     L.fxr_frame_forward_noalloc.argtypes = [ctypes.POINTER(FrameDesc)] + [_vp] * 12
+    L.fxr_qkv_project.argtypes = [ctypes.POINTER(FrameDesc), _vp, _i64, _i32, _vp, _vp, _vp, _vp,
+                                  _vp, _vp, _vp, _vp]
     L.fxr_batch_workspace_size.argtypes = [ctypes.POINTER(FrameDesc), _i32]
     L.fxr_batch_workspace_size.restype = ctypes.c_size_t
     L.fxr_frame_forward_batch.argtypes = [ctypes.POINTER(FrameDesc), _i32, ctypes.POINTER(StreamFrame),
@@ -602,3 +604,11 @@ def frame_forward_batch(cfg: FrameConfig, streams, pos, norm_q, norm_k, workspac
                                           _ptr(norm_k), _ptr(workspace),
                                           workspace.numel() * workspace.element_size(),
                                           _stream(stream)))
+
+
+def qkv_project(cfg: FrameConfig, hidden, w_qkv, bias, idx, count, q, k, v, stream=None):
+    """q/k/v[idx[m]] = hidden[idx[m]] @ w_qkv.T (+ bias) for the executed rows (tcgen05 GEMM)."""
+    d = cfg.desc()
+    _check(load().fxr_qkv_project(ctypes.byref(d), _ptr(hidden), hidden.stride(0), hidden.shape[1],
+                                  _ptr(w_qkv), _ptr(bias), _ptr(idx), _ptr(count), _ptr(q), _ptr(k),
+                                  _ptr(v), _stream(stream)))

@@ -203,6 +203,20 @@ int32_t fxr_frame_forward_noalloc(const fxr_frame_desc* desc,
                                   const float* norm_q, const float* norm_k,
                                   void* cache_k, void* cache_v, void* out, void* stream);
 
+/* ---- QKV projection of the executed tokens ------------------------------------------------------
+ * The reference projects every token's hidden state with fp32 cublasSgemm calls
+ * (flux2_double_block_plugin.cpp:392-398) before sparsity applies. This projects only the executed
+ * rows, after the compaction, so the gather happens before the GEMM:
+ *   [q | k | v][idx[m], :] = hidden[idx[m], :] . w_qkv^T (+ bias)   for m < *count
+ * hidden: [n_tokens, ld_hidden] (k_dim columns, multiple of 64); w_qkv: [3C, k_dim] row-major
+ * (C = n_heads * head_dim, multiple of 256), same element type as desc->dtype; bias: [3C] fp32 or
+ * NULL; q/k/v: [n_tokens, ld_qkv] — rows of skipped tokens are left untouched. tcgen05 GEMM with
+ * the A rows gathered by cp.async and W streamed by TMA, fp32 accumulation in tensor memory. */
+int32_t fxr_qkv_project(const fxr_frame_desc* desc, const void* hidden, int64_t ld_hidden,
+                        int32_t k_dim, const void* w_qkv, const float* bias,
+                        const int32_t* idx, const int32_t* count,
+                        void* q, void* k, void* v, void* stream);
+
 /* ---- independent edit streams in one set of launches -------------------------------------------
  * n_streams frames of the same geometry (the plugin's batch dimension; config 4 runs 8 streams of
  * 768x768): one compaction launch (a CTA per stream), one gather launch over every stream's
