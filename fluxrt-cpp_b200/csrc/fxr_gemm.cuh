@@ -4,16 +4,16 @@
 // (fluxrt-cpp src/inference/plugins/flux2_double_block_plugin.cpp:392-398) before any sparsity is
 // applied. Here the projection runs on the executed rows only:
 //   Y[idx[m], :] = X[idx[m], :] . W^T (+ bias)   for m < *count,  Y = [Q | K | V] split by columns
-// A persistent CTA per SM walks 128 x 256 output tiles (m fastest, so the CTAs working at one time
+// A persistent CTA per SM walks 256 x 256 output tiles (m fastest, so the CTAs working at one time
 // share a 256-column slice of W through L2):
-//   * 4 warps gather the tile's 128 rows of X with cp.async (16 bytes per copy, written in the
-//     128-byte swizzle the tensor core reads; rows past the count are zero-filled) — the row gather
-//     is the A-operand load;
+//   * 8 warps gather the tile's 256 rows of X with cp.async (16 bytes per copy, each warp
+//     instruction reading four whole 128-byte row segments, written in the 128-byte swizzle the
+//     tensor core reads; rows past the count are zero-filled) — the row gather is the A load;
 //   * 1 warp streams W's 256 x 64 slices with TMA (128-byte swizzle);
-//   * 1 warp issues tcgen05.mma (M 128, N 256, K 16; bf16/fp16 in, fp32 in tensor memory) into one
-//     of two 256-column accumulators;
-//   * 4 warps drain the other accumulator: tensor memory -> registers, + bias, -> bf16/fp16, and
-//     store each row's 256 outputs (512 contiguous bytes) to its token row.
+//   * 1 warp issues tcgen05.mma (M 128, N 256, K 16; bf16/fp16 in, fp32 in tensor memory) for both
+//     128-row halves of the tile, which share each W slice, into two 256-column accumulators;
+//   * 8 warps drain them: tensor memory -> registers, + bias, -> bf16/fp16, and store each row's
+//     256 outputs (512 contiguous bytes) to its token row.
 // Every wait is bounded (2 s); after a timeout the kernel sets the device error word and returns.
 #pragma once
 
@@ -27,17 +27,19 @@
 namespace fxr {
 namespace gemm {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kStages = 4;
-constexpr uint32_t kABytes = kBM * kBK * 2;          // 16 KB
+// A tile is 256 rows (two 128-row MMA halves sharing each W slice, which halves the W traffic per
+// FLOP against 128-row tiles) x 256 columns; the two halves' accumulators fill tensor memory.
+constexpr int kBM = 256, kHalf = 128, kBN = 256, kBK = 64;
+constexpr int kStages = 3;
+constexpr uint32_t kABytes = kBM * kBK * 2;          // 32 KB
 constexpr uint32_t kBBytes = kBN * kBK * 2;          // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr int kAWarps = 4, kBWarp = 4, kMmaWarp = 5, kEpiWarp0 = 6, kEpiWarps = 4;
-constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;   // 320
-constexpr uint32_t kTmemCols = 2 * kBN;                  // two accumulators
+constexpr int kAWarps = 8, kBWarp = 8, kMmaWarp = 9, kEpiWarp0 = 10, kEpiWarps = 8;
+constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;   // 576
+constexpr uint32_t kTmemCols = 2 * kBN;                  // the two halves' accumulators
 constexpr uint32_t kSmemBar = kStages * kStageBytes;
-enum : uint32_t { kFull = 0, kEmpty = kStages, kAccFull = 2 * kStages, kAccEmpty = 2 * kStages + 2,
-                  kDrain = 2 * kStages + 4, kNumBars = 2 * kStages + 5 };
+enum : uint32_t { kFull = 0, kEmpty = kStages, kAccFull = 2 * kStages, kAccEmpty = 2 * kStages + 1,
+                  kDrain = 2 * kStages + 2, kNumBars = 2 * kStages + 3 };
 constexpr uint32_t kSlotTmem = kNumBars * 8, kSlotAbort = kSlotTmem + 4;
 constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;     // + alignment slack
 
@@ -83,13 +85,11 @@ qkv_gather_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_con
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(bar(kFull + s), kAWarps * 32 + 1);   // 128 gather threads + the W load
+            mbar_init(bar(kFull + s), kAWarps * 32 + 1);   // 256 gather threads + the W load
             mbar_init(bar(kEmpty + s), 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(bar(kAccFull + b), 1);
-            mbar_init(bar(kAccEmpty + b), kEpiWarps * 32);
-        }
+        mbar_init(bar(kAccFull), 1);
+        mbar_init(bar(kAccEmpty), kEpiWarps * 32);
         mbar_init(bar(kDrain), 1);
         *abort = 0;
         fence_mbar_init();
@@ -114,10 +114,12 @@ qkv_gather_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_con
     if (warp < kAWarps) {
         // ---------------- row gather of X (A operand) ----------------
         // Stage `it` is signalled once its copies have landed and this thread has fenced them for
-        // the tensor core; up to kLag stages stay in flight behind it.
+        // the tensor core, right after the copies of stage it + 1 are issued. Issuing a stage first
+        // waits for the tensor core to free its buffer, so signalling any later than one stage
+        // behind would leave the tensor core idle while this thread waits on that buffer.
         // Lane l of warp w moves 16-byte chunk (l % 8) of rows w*32 + 4j + l/8, j = 0..7: each copy
         // instruction of a warp reads four whole 128-byte row segments.
-        constexpr int kLag = kStages - 1;
+        constexpr int kLag = 1;
         const int c = (int)(lane & 7), sub = (int)(lane >> 3);
         uint32_t it = 0, signalled = 0;
         bool ok = true;
@@ -180,28 +182,29 @@ qkv_gather_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_con
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
-            constexpr uint32_t idesc = make_idesc_f16(StoreT<T>::kUmmaFormat, 0, kBM, kBN);
+            constexpr uint32_t idesc = make_idesc_f16(StoreT<T>::kUmmaFormat, 0, kHalf, kBN);
             uint32_t it = 0, t_it = 0;
             bool ok = true, issued = false;
             for (int32_t u = blockIdx.x; ok && u < n_tiles; u += gridDim.x, ++t_it) {
-                const uint32_t acc = t_it & 1, acc_use = t_it >> 1;
-                if (acc_use > 0 && !mbar_wait(bar(kAccEmpty + acc), (acc_use - 1) & 1, abort)) { ok = false; break; }
+                // the accumulators are free once the epilogue has drained the previous tile
+                if (t_it > 0 && !mbar_wait(bar(kAccEmpty), (t_it - 1) & 1, abort)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t d = tmem + acc * kBN;
                 for (int32_t kb = 0; kb < n_kb; ++kb, ++it) {
                     const uint32_t st = it % kStages;
                     if (!mbar_wait(bar(kFull + st), (it / kStages) & 1, abort)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t sa = base + st * kStageBytes, sb = sa + kABytes;
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; ++k)
-                        umma_ss(d, smem_desc_sw128(sa + k * 32u, 16, 1024), smem_desc_sw128(sb + k * 32u, 16, 1024),
-                                idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    for (int h = 0; h < 2; ++h)          // the two 128-row halves share the W slice
+#pragma unroll
+                        for (int k = 0; k < kBK / 16; ++k)
+                            umma_ss(tmem + h * kBN, smem_desc_sw128(sa + h * (kHalf * 128u) + k * 32u, 16, 1024),
+                                    smem_desc_sw128(sb + k * 32u, 16, 1024), idesc, (kb > 0 || k > 0) ? 1u : 0u);
                     issued = true;
                     umma_commit(bar(kEmpty + st));
                 }
                 if (!ok) break;
-                umma_commit(bar(kAccFull + acc));
+                umma_commit(bar(kAccFull));
             }
             if (*abort && issued) {   // the issued MMAs still read shared memory: wait for them
                 umma_commit(bar(kDrain));
@@ -209,19 +212,21 @@ qkv_gather_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_con
             }
         }
     } else {
-        // ---------------- epilogue: 4 warps, one TMEM lane (tile row) per thread ----------------
+        // ---------- epilogue: 8 warps; warp (sub-partition s, half h) drains TMEM lanes of rows
+        // h*128 + 32s .. +32 from accumulator h, one tile row per thread ----------
         auto wwait = [&](uint32_t b_, uint32_t par_) -> bool {
             return __all_sync(0xffffffffu, mbar_wait(b_, par_, abort));
         };
         const int sub = warp & 3;                          // TMEM sub-partition of this warp
-        const int r = sub * 32 + (int)lane;                // tile row
+        const int half = (warp - kEpiWarp0) / 4;
+        const int r = half * kHalf + sub * 32 + (int)lane; // tile row
         const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
+        const uint32_t acc = (uint32_t)half;
         uint32_t t_it = 0;
         for (int32_t u = blockIdx.x; u < n_tiles; u += gridDim.x, ++t_it) {
-            const uint32_t acc = t_it & 1, acc_use = t_it >> 1;
             const int32_t m = (u % n_mt) * kBM + r, n0 = (u / n_mt) * kBN;
             const int32_t i = m < M ? __ldg(a.idx + m) : -1;
-            if (!wwait(bar(kAccFull + acc), acc_use & 1)) break;
+            if (!wwait(bar(kAccFull), t_it & 1)) break;
             tc_fence_after();
             const int32_t part = n0 / a.c_part, col0 = n0 - part * a.c_part;
             T* yrow = (i >= 0 && i < a.n_tokens)
@@ -248,7 +253,7 @@ qkv_gather_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_con
                 }
             }
             tc_fence_before();
-            mbar_arrive(bar(kAccEmpty + acc));
+            mbar_arrive(bar(kAccEmpty));
         }
     }
 
