@@ -792,9 +792,161 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void*
     return fxr_restore_rows(desc, mask, w.idx, w.count, w.save, cache_k, cache_v, stream);
 }
 
+size_t fxr_rows_gemm_scratch_size(void) {
+    return fxr::gemm::kSyncBytes + (size_t)std::min(sm_count(), fxr::gemm::kMaxCtas) * fxr::gemm::kPartialBytes;
+}
+
+int32_t fxr_ln_modulate_rows(int32_t dtype, const void* x, int64_t ld_x, int32_t dim, const int32_t* idx,
+                             const int32_t* count, int32_t row0, int32_t row_end, int32_t n_tokens,
+                             const float* scale, const float* shift, float eps, void* y, int64_t ld_y,
+                             void* stream) {
+    if (dtype != FXR_BF16 && dtype != FXR_F16) return fail(FXR_ERR_UNSUPPORTED, "dtype must be bf16 or fp16");
+    if (dim <= 0 || dim % 256 != 0 || dim > fxr::kLnMaxChunks * 256)
+        return fail(FXR_ERR_UNSUPPORTED, "dim %d must be a multiple of 256 up to %d", dim, fxr::kLnMaxChunks * 256);
+    if (n_tokens < 0 || row0 < 0 || row_end > n_tokens) return fail(FXR_ERR_INVALID, "bad row range");
+    if (ld_x < dim || ld_y < dim || ld_x % 8 || ld_y % 8)
+        return fail(FXR_ERR_INVALID, "ld_x / ld_y must be >= dim and multiples of 8");
+    if (!(eps >= 0.f)) return fail(FXR_ERR_INVALID, "eps must be >= 0");
+    if (n_tokens == 0 || (row_end >= 0 && row_end <= row0)) return FXR_OK;
+    if (!x || !idx || !y || (row_end < 0 && !count)) return fail(FXR_ERR_INVALID, "null pointer argument");
+    if (!aligned16(x) || !aligned16(y) || !aligned16(scale) || !aligned16(shift))
+        return fail(FXR_ERR_INVALID, "x / y / scale / shift must be 16-byte aligned");
+    const int32_t max_rows = (row_end >= 0 ? row_end : n_tokens) - row0;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((max_rows + 7) / 8, (int64_t)sm_count() * 8));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e =
+        dtype == FXR_BF16
+            ? launch_pdl(fxr::ln_modulate_rows_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s,
+                         static_cast<const __nv_bfloat16*>(x), ld_x, idx, count, row0, row_end, n_tokens, dim,
+                         scale, shift, eps, static_cast<__nv_bfloat16*>(y), ld_y)
+            : launch_pdl(fxr::ln_modulate_rows_kernel<__half>, dim3(grid), dim3(256), 0, s,
+                         static_cast<const __half*>(x), ld_x, idx, count, row0, row_end, n_tokens, dim, scale,
+                         shift, eps, static_cast<__half*>(y), ld_y);
+    if (e != cudaSuccess) return cuda_status(e, "ln_modulate_rows_kernel launch");
+    return FXR_OK;
+}
+
+int32_t fxr_rows_gemm(const fxr_rows_gemm_desc* d, const int32_t* idx, const int32_t* count, void* scratch,
+                      size_t scratch_bytes, void* stream) {
+    namespace G = fxr::gemm;
+    if (!d) return fail(FXR_ERR_INVALID, "null desc");
+    if (d->dtype != FXR_BF16 && d->dtype != FXR_F16) return fail(FXR_ERR_UNSUPPORTED, "dtype must be bf16 or fp16");
+    if (d->n_operands < 1 || d->n_operands > 2) return fail(FXR_ERR_INVALID, "n_operands must be 1 or 2");
+    if (d->n_outputs < 1 || d->n_outputs > 4) return fail(FXR_ERR_INVALID, "n_outputs must be 1 to 4");
+    if (d->n_tokens < 0 || d->row0 < 0 || d->row_end > d->n_tokens) return fail(FXR_ERR_INVALID, "bad row range");
+    int64_t n_out = 0;
+    for (int p = 0; p < d->n_outputs; ++p) {
+        const fxr_rows_output& o = d->y[p];
+        if (o.cols <= 0 || o.cols % G::kBN) return fail(FXR_ERR_UNSUPPORTED, "output %d: cols must be a positive multiple of %d", p, G::kBN);
+        if (o.ld < o.cols || o.ld % 8) return fail(FXR_ERR_INVALID, "output %d: ld must be >= cols and a multiple of 8", p);
+        if (o.act != FXR_ACT_NONE && o.act != FXR_ACT_GELU_TANH) return fail(FXR_ERR_INVALID, "output %d: unknown act", p);
+        if (!o.rows || !aligned16(o.rows)) return fail(FXR_ERR_INVALID, "output %d: null or unaligned rows", p);
+        n_out += o.cols;
+    }
+    for (int q = 0; q < d->n_operands; ++q) {
+        const fxr_rows_operand& o = d->a[q];
+        if (o.k <= 0 || o.k % G::kBK) return fail(FXR_ERR_UNSUPPORTED, "operand %d: k must be a positive multiple of %d", q, G::kBK);
+        if (o.ld < o.k || o.ld % 8) return fail(FXR_ERR_INVALID, "operand %d: ld must be >= k and a multiple of 8", q);
+        if (!o.rows || !o.w || !aligned16(o.rows) || !aligned16(o.w))
+            return fail(FXR_ERR_INVALID, "operand %d: null or unaligned rows / w", q);
+    }
+    if (!aligned16(d->bias0) || !aligned16(d->bias1) || !aligned16(d->gate))
+        return fail(FXR_ERR_INVALID, "bias0 / bias1 / gate must be 16-byte aligned");
+    if (d->residual) {
+        if (d->n_outputs != 1) return fail(FXR_ERR_INVALID, "a residual needs a single output part");
+        if (d->ld_residual < n_out || d->ld_residual % 8 || !aligned16(d->residual))
+            return fail(FXR_ERR_INVALID, "residual: ld must be >= n_out and a multiple of 8, 16-byte aligned");
+    }
+    if (!idx || (d->row_end < 0 && !count)) return fail(FXR_ERR_INVALID, "null idx / count");
+    if (scratch && (scratch_bytes < fxr_rows_gemm_scratch_size() || !aligned16(scratch)))
+        return fail(FXR_ERR_WORKSPACE, "scratch %zu < required %zu (or unaligned)", scratch_bytes,
+                    fxr_rows_gemm_scratch_size());
+    if (d->n_tokens == 0 || (d->row_end >= 0 && d->row_end <= d->row0)) return FXR_OK;
+
+    // instantiations: dtype x (residual or not); the residual path costs registers the others keep
+    const int ti = (d->dtype == FXR_BF16 ? 0 : 2) + (d->residual ? 1 : 0);
+    using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const G::Args);
+    const KernelFn kernels[4] = {G::rows_gemm_kernel<__nv_bfloat16, false>, G::rows_gemm_kernel<__nv_bfloat16, true>,
+                                 G::rows_gemm_kernel<__half, false>, G::rows_gemm_kernel<__half, true>};
+    static bool configured[kMaxDevices][4] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < kMaxDevices && !configured[dev][ti]) {
+        cudaError_t e = cudaFuncSetAttribute(kernels[ti], cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::kSmemBytes);
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(rows gemm)");
+        configured[dev][ti] = true;
+    }
+    int32_t st;
+    CUtensorMap tw0, tw1;
+    if ((st = make_tmap(&tw0, d->a[0].w, d->dtype, d->a[0].k, n_out, d->a[0].k, G::kBN)) != FXR_OK) return st;
+    if (d->n_operands == 2) {
+        if ((st = make_tmap(&tw1, d->a[1].w, d->dtype, d->a[1].k, n_out, d->a[1].k, G::kBN)) != FXR_OK) return st;
+    } else {
+        tw1 = tw0;
+    }
+    G::Args a{};
+    a.op0.rows = d->a[0].rows;
+    a.op0.ld = d->a[0].ld;
+    a.op0.kb_end = d->a[0].k / G::kBK;
+    a.op0.gathered = d->a[0].gathered ? 1 : 0;
+    int32_t k_total = d->a[0].k;
+    if (d->n_operands == 2) {
+        a.op1.rows = d->a[1].rows;
+        a.op1.ld = d->a[1].ld;
+        a.op1.kb_end = a.op0.kb_end + d->a[1].k / G::kBK;
+        a.op1.gathered = d->a[1].gathered ? 1 : 0;
+        k_total += d->a[1].k;
+    } else {
+        a.op1 = a.op0;
+        a.op1.rows = nullptr;
+    }
+    a.idx = idx;
+    a.count = count;
+    a.row0 = d->row0;
+    a.row_end = d->row_end;
+    a.n_tokens = d->n_tokens;
+    a.n_kb = k_total / G::kBK;
+    a.n_out = (int32_t)n_out;
+    G::Part* parts[4] = {&a.p0, &a.p1, &a.p2, &a.p3};
+    int32_t col_end = 0;
+    for (int p = 0; p < 4; ++p) {
+        G::Part& P = *parts[p];
+        if (p < d->n_outputs) {
+            const fxr_rows_output& o = d->y[p];
+            col_end += o.cols;
+            P.rows = o.rows;
+            P.ld = o.ld;
+            P.scattered = o.scattered ? 1 : 0;
+            P.gelu = o.act == FXR_ACT_GELU_TANH ? 1 : 0;
+        } else {
+            P = *parts[d->n_outputs - 1];
+        }
+        P.col_end = col_end;
+    }
+    a.bias0 = d->bias0;
+    a.bias1 = d->bias1;
+    a.res = d->residual;
+    a.ld_res = d->ld_residual;
+    a.gate = d->gate;
+    a.sync = static_cast<uint32_t*>(scratch);
+    a.partials = scratch ? reinterpret_cast<float*>(static_cast<char*>(scratch) + G::kSyncBytes) : nullptr;
+    int grid;
+    if (scratch) {
+        grid = std::min(sm_count(), G::kMaxCtas);
+    } else {
+        const int64_t max_rows = (d->row_end >= 0 ? d->row_end : d->n_tokens) - d->row0;
+        const int64_t max_tiles = (max_rows + G::kBM - 1) / G::kBM * (n_out / G::kBN);
+        grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_tiles, sm_count()));
+    }
+    cudaError_t e = launch_pdl(kernels[ti], dim3(grid), dim3(G::kThreads), G::kSmemBytes,
+                               static_cast<cudaStream_t>(stream), tw0, tw1, a);
+    if (e != cudaSuccess) return cuda_status(e, "rows_gemm_kernel launch");
+    return FXR_OK;
+}
+
 int32_t fxr_qkv_project(const fxr_frame_desc* desc, const void* hidden, int64_t ld_hidden, int32_t k_dim,
                         const void* w_qkv, const float* bias, const int32_t* idx, const int32_t* count,
-                        void* q, void* k, void* v, void* stream) {
+                        void* q, void* k, void* v, void* scratch, size_t scratch_bytes, void* stream) {
     int32_t st = check_desc(desc, true);
     if (st != FXR_OK) return st;
     const int64_t C = (int64_t)desc->n_heads * desc->head_dim;
@@ -806,47 +958,18 @@ int32_t fxr_qkv_project(const fxr_frame_desc* desc, const void* hidden, int64_t 
     if (ld_hidden < k_dim || ld_hidden % 8) return fail(FXR_ERR_INVALID, "ld_hidden must be >= k_dim and a multiple of 8");
     if (desc->n_tokens == 0) return FXR_OK;
     if (!hidden || !w_qkv || !idx || !count || !q || !k || !v) return fail(FXR_ERR_INVALID, "null pointer argument");
-    if (!aligned16(hidden) || !aligned16(w_qkv) || !aligned16(q) || !aligned16(k) || !aligned16(v))
-        return fail(FXR_ERR_INVALID, "buffers must be 16-byte aligned");
-    static bool configured[kMaxDevices][2] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const int ti = desc->dtype == FXR_BF16 ? 0 : 1;
-    if (dev >= 0 && dev < kMaxDevices && !configured[dev][ti]) {
-        cudaError_t e = ti == 0 ? cudaFuncSetAttribute(fxr::gemm::qkv_gather_gemm_kernel<__nv_bfloat16>,
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                       (int)fxr::gemm::kSmemBytes)
-                                : cudaFuncSetAttribute(fxr::gemm::qkv_gather_gemm_kernel<__half>,
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                       (int)fxr::gemm::kSmemBytes);
-        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(qkv gemm)");
-        configured[dev][ti] = true;
-    }
-    CUtensorMap tw;
-    if ((st = make_tmap(&tw, w_qkv, desc->dtype, k_dim, 3 * C, k_dim, fxr::gemm::kBN)) != FXR_OK) return st;
-    fxr::gemm::Args a{};
-    a.x = hidden;
-    a.idx = idx;
-    a.count = count;
-    a.bias = bias;
-    a.y[0] = q;
-    a.y[1] = k;
-    a.y[2] = v;
-    a.ld_x = ld_hidden;
-    a.ld_y = desc->ld_qkv;
-    a.k_dim = k_dim;
-    a.n_out = (int32_t)(3 * C);
-    a.c_part = (int32_t)C;
-    a.n_tokens = desc->n_tokens;
-    const int64_t max_tiles = (desc->n_tokens + fxr::gemm::kBM - 1) / fxr::gemm::kBM * (3 * C / fxr::gemm::kBN);
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_tiles, sm_count()));
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t e = ti == 0 ? launch_pdl(fxr::gemm::qkv_gather_gemm_kernel<__nv_bfloat16>, dim3(grid),
-                                         dim3(fxr::gemm::kThreads), fxr::gemm::kSmemBytes, s, tw, a)
-                            : launch_pdl(fxr::gemm::qkv_gather_gemm_kernel<__half>, dim3(grid),
-                                         dim3(fxr::gemm::kThreads), fxr::gemm::kSmemBytes, s, tw, a);
-    if (e != cudaSuccess) return cuda_status(e, "qkv_gather_gemm_kernel launch");
-    return FXR_OK;
+    fxr_rows_gemm_desc g{};
+    g.dtype = desc->dtype;
+    g.n_tokens = desc->n_tokens;
+    g.row0 = 0;
+    g.row_end = -1;
+    g.n_operands = 1;
+    g.a[0] = fxr_rows_operand{hidden, ld_hidden, k_dim, 1, w_qkv};
+    g.n_outputs = 3;
+    void* parts[3] = {q, k, v};
+    for (int p = 0; p < 3; ++p) g.y[p] = fxr_rows_output{parts[p], desc->ld_qkv, (int32_t)C, 1, FXR_ACT_NONE, 0};
+    g.bias0 = bias;
+    return fxr_rows_gemm(&g, idx, count, scratch, scratch_bytes, stream);
 }
 
 size_t fxr_batch_workspace_size(const fxr_frame_desc* desc, int32_t n_streams) {

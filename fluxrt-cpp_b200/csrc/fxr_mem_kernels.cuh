@@ -8,6 +8,7 @@
 //   kv_sync_kernel           reference full-frame K/V merge + update
 //   out_cache_sync_kernel    reference output-cache merge + valid update
 //   rms_norm_kernel          standalone row RMSNorm
+//   ln_modulate_rows_kernel  executed-row gather + LayerNorm (no affine) + (1 + scale) x + shift
 // Rows move as 16-byte vectors; grids are multiples of the SM count and loop over rows, reading the
 // executed-row count M from device memory (no host synchronisation between the steps).
 #pragma once
@@ -707,6 +708,105 @@ rms_norm_kernel(const T* __restrict__ x, T* __restrict__ y, const float* __restr
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         const float rs = rsqrtf(ss / (float)dim + eps);
         for (int32_t e = lane; e < dim; e += 32) store_f(yr + e, load_f(xr + e) * rs * w[e]);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Executed-row LayerNorm + modulation, the input of the block's projections: for compact rows m in
+// [row0, row_end) (row_end < 0: *count),
+//   y[m, :] = (1 + scale) * (x[idx[m], :] - mean) * rsqrt(var + eps) + shift
+// with mean and the biased variance over the row's dim values (fp32). Restates
+// layer_norm_modulated_kernel without gamma/beta and apply_modulation_kernel
+// (gather_scatter_kernels.cu:77-99,106-169; called at flux2_double_block_plugin.cpp:373-383) on the
+// executed rows only, in one pass over HBM. A warp per row, the row held in registers: lane l reads
+// 16-byte chunks l, l + 32, ... so each warp instruction covers 512 contiguous bytes; dim is a
+// multiple of 256 up to 4096.
+// ---------------------------------------------------------------------------------------------
+constexpr int kLnMaxChunks = 16;   // 16-byte chunks per lane: dim <= 16 * 32 * 8
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+ln_modulate_rows_kernel(const T* __restrict__ x, int64_t ld_x, const int32_t* __restrict__ idx,
+                        const int32_t* __restrict__ count, int32_t row0, int32_t row_end_arg,
+                        int32_t n_tokens, int32_t dim, const float* __restrict__ scale,
+                        const float* __restrict__ shift, float eps, T* __restrict__ y, int64_t ld_y) {
+    pdl_launch_dependents();
+    pdl_wait();   // idx / count come from the compaction
+    const int lane = threadIdx.x & 31;
+    const int32_t row_end = min(row_end_arg >= 0 ? row_end_arg : *count, n_tokens);
+    const int nch = dim / 256;
+    const float inv_dim = 1.0f / (float)dim;
+    for (int32_t m = row0 + (int32_t)blockIdx.x * 8 + (int32_t)(threadIdx.x >> 5); m < row_end;
+         m += (int32_t)gridDim.x * 8) {
+        const int32_t i = __ldg(idx + m);
+        if (i < 0 || i >= n_tokens) {
+            if (lane == 0) atomicOr(&g_error_word, kErrBounds);
+            continue;
+        }
+        const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)i * ld_x);
+        uint4 v[kLnMaxChunks];
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < kLnMaxChunks; ++j) {
+            if (j < nch) {
+                v[j] = __ldg(xr + j * 32 + lane);
+                const uint32_t w4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = StoreT<T>::unpack2(w4[e]);
+                    s += f.x + f.y;
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float mean = s * inv_dim;
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < kLnMaxChunks; ++j) {
+            if (j < nch) {
+                const uint32_t w4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = StoreT<T>::unpack2(w4[e]);
+                    const float d0 = f.x - mean, d1 = f.y - mean;
+                    ss = fmaf(d0, d0, fmaf(d1, d1, ss));
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float rstd = rsqrtf(ss * inv_dim + eps);
+        uint4* yr = reinterpret_cast<uint4*>(y + (int64_t)m * ld_y);
+#pragma unroll
+        for (int j = 0; j < kLnMaxChunks; ++j) {
+            if (j < nch) {
+                const int col = (j * 32 + lane) * 8;
+                float sc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, sh[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                if (scale) {
+                    const float4 s0 = __ldg(reinterpret_cast<const float4*>(scale + col));
+                    const float4 s1 = __ldg(reinterpret_cast<const float4*>(scale + col) + 1);
+                    sc[0] = s0.x; sc[1] = s0.y; sc[2] = s0.z; sc[3] = s0.w;
+                    sc[4] = s1.x; sc[5] = s1.y; sc[6] = s1.z; sc[7] = s1.w;
+                }
+                if (shift) {
+                    const float4 s0 = __ldg(reinterpret_cast<const float4*>(shift + col));
+                    const float4 s1 = __ldg(reinterpret_cast<const float4*>(shift + col) + 1);
+                    sh[0] = s0.x; sh[1] = s0.y; sh[2] = s0.z; sh[3] = s0.w;
+                    sh[4] = s1.x; sh[5] = s1.y; sh[6] = s1.z; sh[7] = s1.w;
+                }
+                const uint32_t w4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+                uint32_t o4[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = StoreT<T>::unpack2(w4[e]);
+                    const float a0 = (f.x - mean) * rstd, a1 = (f.y - mean) * rstd;
+                    o4[e] = StoreT<T>::pack2(fmaf(1.0f + sc[2 * e], a0, sh[2 * e]),
+                                             fmaf(1.0f + sc[2 * e + 1], a1, sh[2 * e + 1]));
+                }
+                yr[j * 32 + lane] = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+            }
+        }
     }
 }
 

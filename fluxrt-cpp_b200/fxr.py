@@ -38,7 +38,10 @@ EXPORTED = [
     "fxr_nccl_unique_id", "fxr_nccl_comm_init", "fxr_nccl_comm_destroy",
     "fxr_heads_nccl_workspace_size", "fxr_allgather_heads", "fxr_frame_forward_heads_nccl",
     "fxr_batch_workspace_size", "fxr_frame_forward_batch", "fxr_qkv_project",
+    "fxr_ln_modulate_rows", "fxr_rows_gemm_scratch_size", "fxr_rows_gemm",
 ]
+
+FXR_ACT_NONE, FXR_ACT_GELU_TANH = 0, 1
 
 FXR_MAX_BATCH = 8
 
@@ -52,6 +55,27 @@ class FxrError(RuntimeError):
     def __init__(self, status: int, msg: str):
         super().__init__(f"fxr status {status}: {msg}")
         self.status = status
+
+
+class RowsOperand(ctypes.Structure):
+    """Mirror of fxr_rows_operand (include/fxr.h)."""
+    _fields_ = [("rows", ctypes.c_void_p), ("ld", ctypes.c_int64), ("k", ctypes.c_int32),
+                ("gathered", ctypes.c_int32), ("w", ctypes.c_void_p)]
+
+
+class RowsOutput(ctypes.Structure):
+    """Mirror of fxr_rows_output (include/fxr.h)."""
+    _fields_ = [("rows", ctypes.c_void_p), ("ld", ctypes.c_int64), ("cols", ctypes.c_int32),
+                ("scattered", ctypes.c_int32), ("act", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+class RowsGemmDesc(ctypes.Structure):
+    """Mirror of fxr_rows_gemm_desc (include/fxr.h)."""
+    _fields_ = [("dtype", ctypes.c_int32), ("n_tokens", ctypes.c_int32), ("row0", ctypes.c_int32),
+                ("row_end", ctypes.c_int32), ("n_operands", ctypes.c_int32),
+                ("n_outputs", ctypes.c_int32), ("a", RowsOperand * 2), ("y", RowsOutput * 4),
+                ("bias0", ctypes.c_void_p), ("bias1", ctypes.c_void_p), ("residual", ctypes.c_void_p),
+                ("ld_residual", ctypes.c_int64), ("gate", ctypes.c_void_p)]
 
 
 class PluginField(ctypes.Structure):
@@ -144,7 +168,12 @@ def load(path: str | None = None) -> ctypes.CDLL:
                                     _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]
     L.fxr_frame_forward_noalloc.argtypes = [ctypes.POINTER(FrameDesc)] + [_vp] * 12
     L.fxr_qkv_project.argtypes = [ctypes.POINTER(FrameDesc), _vp, _i64, _i32, _vp, _vp, _vp, _vp,
-                                  _vp, _vp, _vp, _vp]
+                                  _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]
+    L.fxr_ln_modulate_rows.argtypes = [_i32, _vp, _i64, _i32, _vp, _vp, _i32, _i32, _i32, _vp, _vp,
+                                       ctypes.c_float, _vp, _i64, _vp]
+    L.fxr_rows_gemm_scratch_size.argtypes = []
+    L.fxr_rows_gemm_scratch_size.restype = ctypes.c_size_t
+    L.fxr_rows_gemm.argtypes = [ctypes.POINTER(RowsGemmDesc), _vp, _vp, _vp, ctypes.c_size_t, _vp]
     L.fxr_batch_workspace_size.argtypes = [ctypes.POINTER(FrameDesc), _i32]
     L.fxr_batch_workspace_size.restype = ctypes.c_size_t
     L.fxr_frame_forward_batch.argtypes = [ctypes.POINTER(FrameDesc), _i32, ctypes.POINTER(StreamFrame),
@@ -606,9 +635,51 @@ def frame_forward_batch(cfg: FrameConfig, streams, pos, norm_q, norm_k, workspac
                                           _stream(stream)))
 
 
-def qkv_project(cfg: FrameConfig, hidden, w_qkv, bias, idx, count, q, k, v, stream=None):
-    """q/k/v[idx[m]] = hidden[idx[m]] @ w_qkv.T (+ bias) for the executed rows (tcgen05 GEMM)."""
+def qkv_project(cfg: FrameConfig, hidden, w_qkv, bias, idx, count, q, k, v, scratch=None,
+                stream=None):
+    """q/k/v[idx[m]] = hidden[idx[m]] @ w_qkv.T (+ bias) for the executed rows (tcgen05 GEMM).
+    scratch: a zeroed uint8 tensor of rows_gemm_scratch_size() bytes (stream-K), or None."""
     d = cfg.desc()
     _check(load().fxr_qkv_project(ctypes.byref(d), _ptr(hidden), hidden.stride(0), hidden.shape[1],
                                   _ptr(w_qkv), _ptr(bias), _ptr(idx), _ptr(count), _ptr(q), _ptr(k),
-                                  _ptr(v), _stream(stream)))
+                                  _ptr(v), _ptr(scratch), scratch.numel() if scratch is not None else 0,
+                                  _stream(stream)))
+
+
+def rows_gemm_scratch_size() -> int:
+    return int(load().fxr_rows_gemm_scratch_size())
+
+
+def rows_gemm_scratch(device="cuda"):
+    """A zeroed stream-K scratch area for rows_gemm (one per stream, reused as is)."""
+    import torch
+    return torch.zeros(rows_gemm_scratch_size(), dtype=torch.uint8, device=device)
+
+
+def ln_modulate_rows(x, idx, count, y, scale=None, shift=None, eps=1e-6, row0=0, row_end=-1,
+                     stream=None):
+    """y[m] = (1 + scale) * LayerNorm(x[idx[m]]) + shift for compact rows m in [row0, row_end)."""
+    _check(load().fxr_ln_modulate_rows(dtype_code(x.dtype), _ptr(x), x.stride(0), x.shape[1],
+                                       _ptr(idx), _ptr(count), row0, row_end, x.shape[0],
+                                       _ptr(scale), _ptr(shift), eps, _ptr(y), y.stride(0),
+                                       _stream(stream)))
+
+
+def rows_gemm(operands, outputs, idx, count, n_tokens, bias0=None, bias1=None, residual=None,
+              gate=None, row0=0, row_end=-1, scratch=None, stream=None):
+    """Executed-row GEMM (fxr_rows_gemm). operands: [(rows, w, gathered)] (1 or 2; rows [*, k],
+    w [n_out, k]); outputs: [(rows, cols, scattered, act)] (1 to 4)."""
+    d = RowsGemmDesc()
+    d.dtype = dtype_code(operands[0][0].dtype)
+    d.n_tokens = n_tokens
+    d.row0, d.row_end = row0, row_end
+    d.n_operands, d.n_outputs = len(operands), len(outputs)
+    for i, (rows, w, gathered) in enumerate(operands):
+        d.a[i] = RowsOperand(_ptr(rows), rows.stride(0), w.shape[1], 1 if gathered else 0, _ptr(w))
+    for i, (rows, cols, scattered, act) in enumerate(outputs):
+        d.y[i] = RowsOutput(_ptr(rows), rows.stride(0), cols, 1 if scattered else 0, act, 0)
+    d.bias0, d.bias1, d.gate = _ptr(bias0), _ptr(bias1), _ptr(gate)
+    d.residual = _ptr(residual)
+    d.ld_residual = residual.stride(0) if residual is not None else 0
+    _check(load().fxr_rows_gemm(ctypes.byref(d), _ptr(idx), _ptr(count), _ptr(scratch),
+                                scratch.numel() if scratch is not None else 0, _stream(stream)))

@@ -203,19 +203,89 @@ int32_t fxr_frame_forward_noalloc(const fxr_frame_desc* desc,
                                   const float* norm_q, const float* norm_k,
                                   void* cache_k, void* cache_v, void* out, void* stream);
 
-/* ---- QKV projection of the executed tokens ------------------------------------------------------
- * The reference projects every token's hidden state with fp32 cublasSgemm calls
- * (flux2_double_block_plugin.cpp:392-398) before sparsity applies. This projects only the executed
- * rows, after the compaction, so the gather happens before the GEMM:
+/* ---- the block's projections on the executed rows -----------------------------------------------
+ * The reference runs the double-stream block's dense math on every token in fp32: LayerNorm +
+ * modulation (gather_scatter_kernels.cu:77-169, called at flux2_double_block_plugin.cpp:373-383),
+ * the Q/K/V projections (:386-408), the out-projection (:429-432), the MLP with tanh GELU
+ * (:434-448, flux2_kernels.cu:14-29) and the residual (:450-458). These functions run each step
+ * on the executed rows only (compact rows m < *count of fxr_mask_compact's idx list), so the gather
+ * happens before the projections and skipped tokens cost nothing.
+ *
+ * Executed-row LayerNorm + modulation, compact output:
+ *   y[m, :] = (1 + scale) * (x[idx[m], :] - mean) / sqrt(var + eps) + shift,  m in [row0, row_end)
+ * row_end < 0: *count. dim: multiple of 256, at most 4096; scale / shift: [dim] fp32 or NULL. */
+int32_t fxr_ln_modulate_rows(int32_t dtype, const void* x, int64_t ld_x, int32_t dim,
+                             const int32_t* idx, const int32_t* count, int32_t row0,
+                             int32_t row_end, int32_t n_tokens, const float* scale,
+                             const float* shift, float eps, void* y, int64_t ld_y, void* stream);
+
+/* Executed-row GEMM with a fused epilogue (tcgen05, fp32 accumulation in tensor memory):
+ *   Y[r(m), :] = act([A0 | A1][m, :] . [W0 | W1]^T + bias0 + bias1)                 or
+ *   Y[r(m), :] = residual[r(m), :] + gate * ([A0 | A1][m, :] . [W0 | W1]^T + bias0 + bias1)
+ * for compact rows m in [row0, row_end). Each A operand is gathered (row idx[m] of a token-major
+ * buffer) or compact (row m); the output columns are cut into up to four parts, each written to
+ * its own buffer, scattered (row idx[m]) or compact (row m), with or without the tanh GELU. The
+ * residual (single output part only) is read at the output row. Recipes for the block:
+ *   Q/K/V:          a[0] = {LN rows, compact, W_qkv};   y = {Q, K, V scattered}, bias0 = b_qkv
+ *   MLP up:         a[0] = {LN rows, compact, W_mlp0};  y = {H compact, GELU},   bias0 = b_mlp0
+ *   out + MLP down: a[0] = {attention output, gathered, W_out}, a[1] = {H, compact, W_mlp2};
+ *                   y = {block output, scattered}, bias0 = b_out, bias1 = b_mlp2,
+ *                   residual = block input, gate = the gate row (NULL: 1, as the reference)
+ * K of each operand: multiple of 64; output part widths: multiples of 256; element type dtype
+ * (bf16/fp16) everywhere except the fp32 bias and gate. scratch: fxr_rows_gemm_scratch_size()
+ * bytes, ZERO before its first use and then reused as is (one scratch per stream; it balances the
+ * work of every SM by splitting tiles over CTAs — stream-K); NULL runs whole tiles per CTA. */
+#define FXR_ACT_NONE 0
+#define FXR_ACT_GELU_TANH 1
+
+typedef struct fxr_rows_operand {
+    const void* rows;        /* [*, ld] */
+    int64_t ld;              /* elements */
+    int32_t k;               /* columns of this operand (multiple of 64) */
+    int32_t gathered;        /* 1: row idx[m]; 0: row m */
+    const void* w;           /* [n_out, k] row-major */
+} fxr_rows_operand;
+
+typedef struct fxr_rows_output {
+    void* rows;              /* [*, ld] */
+    int64_t ld;
+    int32_t cols;            /* multiple of 256 */
+    int32_t scattered;       /* 1: row idx[m]; 0: row m */
+    int32_t act;             /* FXR_ACT_NONE / FXR_ACT_GELU_TANH */
+    int32_t reserved;
+} fxr_rows_output;
+
+typedef struct fxr_rows_gemm_desc {
+    int32_t dtype;           /* FXR_BF16 or FXR_F16 */
+    int32_t n_tokens;        /* bound of idx values and compact rows */
+    int32_t row0;            /* compact rows [row0, row_end) */
+    int32_t row_end;         /* < 0: *count */
+    int32_t n_operands;      /* 1 or 2 */
+    int32_t n_outputs;       /* 1 to 4 */
+    fxr_rows_operand a[2];
+    fxr_rows_output y[4];
+    const float* bias0;      /* [n_out] fp32 or NULL */
+    const float* bias1;
+    const void* residual;    /* [*, ld_residual] or NULL */
+    int64_t ld_residual;
+    const float* gate;       /* [n_out] fp32 or NULL */
+} fxr_rows_gemm_desc;
+
+size_t fxr_rows_gemm_scratch_size(void);
+int32_t fxr_rows_gemm(const fxr_rows_gemm_desc* d, const int32_t* idx, const int32_t* count,
+                      void* scratch, size_t scratch_bytes, void* stream);
+
+/* QKV projection of the executed tokens from token-major hidden states:
  *   [q | k | v][idx[m], :] = hidden[idx[m], :] . w_qkv^T (+ bias)   for m < *count
  * hidden: [n_tokens, ld_hidden] (k_dim columns, multiple of 64); w_qkv: [3C, k_dim] row-major
  * (C = n_heads * head_dim, multiple of 256), same element type as desc->dtype; bias: [3C] fp32 or
- * NULL; q/k/v: [n_tokens, ld_qkv] — rows of skipped tokens are left untouched. tcgen05 GEMM with
- * the A rows gathered by cp.async and W streamed by TMA, fp32 accumulation in tensor memory. */
+ * NULL; q/k/v: [n_tokens, ld_qkv] — rows of skipped tokens are left untouched. scratch as for
+ * fxr_rows_gemm (NULL allowed). */
 int32_t fxr_qkv_project(const fxr_frame_desc* desc, const void* hidden, int64_t ld_hidden,
                         int32_t k_dim, const void* w_qkv, const float* bias,
                         const int32_t* idx, const int32_t* count,
-                        void* q, void* k, void* v, void* stream);
+                        void* q, void* k, void* v, void* scratch, size_t scratch_bytes,
+                        void* stream);
 
 /* ---- independent edit streams in one set of launches -------------------------------------------
  * n_streams frames of the same geometry (the plugin's batch dimension; config 4 runs 8 streams of

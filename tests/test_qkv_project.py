@@ -13,16 +13,18 @@ import workloads as W
 def test_qkv_project_argument_checks():
     L = fxr.load()
     d = fxr.FrameConfig(n_tokens=1536, n_text=512, n_heads=4).desc()
-    assert L.fxr_qkv_project(ctypes.byref(d), None, 256, 100, *([None] * 8)) == fxr.FXR_ERR_UNSUPPORTED
+    rest = [None] * 8 + [0, None]        # w, bias, idx, count, q, k, v, scratch, bytes, stream
+    assert L.fxr_qkv_project(ctypes.byref(d), None, 256, 100, *rest) == fxr.FXR_ERR_UNSUPPORTED
     d3 = fxr.FrameConfig(n_tokens=1536, n_text=512, n_heads=3).desc()      # C = 384, not / 256
-    assert L.fxr_qkv_project(ctypes.byref(d3), None, 256, 256, *([None] * 8)) == fxr.FXR_ERR_UNSUPPORTED
-    assert L.fxr_qkv_project(ctypes.byref(d), None, 256, 256, *([None] * 8)) == fxr.FXR_ERR_INVALID
+    assert L.fxr_qkv_project(ctypes.byref(d3), None, 256, 256, *rest) == fxr.FXR_ERR_UNSUPPORTED
+    assert L.fxr_qkv_project(ctypes.byref(d), None, 256, 256, *rest) == fxr.FXR_ERR_INVALID
 
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("n,heads,k_dim,dtype,p", [(1536, 4, 256, "bf16", 0.25), (4608, 24, 3072, "bf16", 0.25),
                                                   (1536, 2, 1024, "f16", 0.6), (640, 2, 64, "bf16", 0.0)])
-def test_qkv_project_matches_fp32_matmul(cuda, n, heads, k_dim, dtype, p):
+@pytest.mark.parametrize("stream_k", [True, False])
+def test_qkv_project_matches_fp32_matmul(cuda, n, heads, k_dim, dtype, p, stream_k):
     import torch
     td = torch.bfloat16 if dtype == "bf16" else torch.float16
     C = heads * 128
@@ -40,7 +42,8 @@ def test_qkv_project_matches_fp32_matmul(cuda, n, heads, k_dim, dtype, p):
     count = torch.tensor([idx_h.size], dtype=torch.int32, device="cuda")
     outs = [torch.full((n, C), 7.0, device="cuda").to(td) for _ in range(3)]
     cfg = fxr.FrameConfig(n_tokens=n, n_text=128, n_heads=heads, dtype=dtype)
-    fxr.qkv_project(cfg, x, w, bias, idx, count, *outs)
+    scratch = fxr.rows_gemm_scratch() if stream_k else None
+    fxr.qkv_project(cfg, x, w, bias, idx, count, *outs, scratch=scratch)
     torch.cuda.synchronize()
     assert fxr.check_device_error() == 0
     rows = torch.from_numpy(idx_h).long().cuda()
