@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <array>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -338,7 +339,8 @@ int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
 template <typename T>
 int32_t launch_gather_streams(const fxr_frame_desc* d, int32_t n_streams, const fxr::GatherStream* gs,
                               const int32_t* pos, const float* nq, const float* nk, int64_t ld_qc,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, const float* nq_txt = nullptr,
+                              const float* nk_txt = nullptr, int32_t n_text_norm = 0) {
     if (n_streams < 1 || n_streams > fxr::kMaxBatch) return fail(FXR_ERR_INVALID, "1..%d streams per launch", fxr::kMaxBatch);
     fxr::GatherArgs a{};
     for (int32_t b = 0; b < n_streams; ++b) a.s[b] = gs[b];
@@ -346,6 +348,9 @@ int32_t launch_gather_streams(const fxr_frame_desc* d, int32_t n_streams, const 
     a.pos = pos;
     a.norm_q = nq;
     a.norm_k = nk;
+    a.norm_q_txt = nq_txt;
+    a.norm_k_txt = nk_txt;
+    a.n_text_norm = n_text_norm;
     a.ld_qkv = d->ld_qkv;
     a.ld_qc = ld_qc;
     a.ld_cache = d->ld_cache;
@@ -483,8 +488,12 @@ int32_t fxr_workspace_views(const fxr_frame_desc* desc, void* workspace, int32_t
 // Compaction of n_streams frames (CTA b: stream b); the attention's split counters of the launch
 // start at zero.
 static int32_t launch_compact_streams(fxr::CompactArgs a, int32_t n_streams, int32_t n_tokens,
-                                      const SplitArea& split, void* stream) {
+                                      const SplitArea& split, void* stream, void* zero2 = nullptr,
+                                      size_t zero2_bytes = 0, int32_t n_force = 0) {
     a.n = n_tokens;
+    a.zero2 = reinterpret_cast<uint4*>(zero2);
+    a.zero2_vec = (int32_t)(zero2_bytes / 16);
+    a.n_force = n_force;
     a.zero = reinterpret_cast<uint4*>(split.cnt);
     a.zero_vec = (int32_t)((size_t)split.slots * kSplitCntBytes / 16);
     cudaError_t e = launch_pdl(fxr::compact_kernel, dim3(n_streams), dim3(fxr::kCompactThreads), 0,
@@ -970,6 +979,191 @@ int32_t fxr_qkv_project(const fxr_frame_desc* desc, const void* hidden, int64_t 
     for (int p = 0; p < 3; ++p) g.y[p] = fxr_rows_output{parts[p], desc->ld_qkv, (int32_t)C, 1, FXR_ACT_NONE, 0};
     g.bias0 = bias;
     return fxr_rows_gemm(&g, idx, count, scratch, scratch_bytes, stream);
+}
+
+// ---- the double-stream block on the executed rows ---------------------------------------------
+// Workspace: the frame's views and split area, then Q/K/V, the LayerNorm rows, the attention rows
+// (all [N, C]), the MLP rows [N, H] and the GEMM scratch.
+struct BlockViews {
+    Views frame;
+    SplitArea split;
+    char* q;
+    char* k;
+    char* v;
+    char* xn;
+    char* attn;
+    char* h;
+    char* gemm;
+    size_t total;
+};
+
+static BlockViews carve_block(const fxr_frame_desc* d, int32_t hidden, void* ws) {
+    BlockViews b{};
+    char* base = static_cast<char*>(ws);
+    b.frame = carve(d, ws);
+    const size_t split_sz = split_bytes(kSplitSlotsPerSm * sm_count());
+    size_t off = align_up(b.frame.total + split_sz, 256);
+    if (base) b.split = split_area(b.frame.total, ws, b.frame.total + split_sz);
+    const size_t N = (size_t)(d->n_tokens > 0 ? d->n_tokens : 1);
+    const size_t row = (size_t)d->n_heads * d->head_dim * dtype_bytes(d->dtype);
+    char** parts[5] = {&b.q, &b.k, &b.v, &b.xn, &b.attn};
+    for (char** p : parts) {
+        *p = base ? base + off : nullptr;
+        off = align_up(off + N * row, 256);
+    }
+    b.h = base ? base + off : nullptr;
+    off = align_up(off + N * (size_t)hidden * dtype_bytes(d->dtype), 256);
+    b.gemm = base ? base + off : nullptr;
+    off += fxr_rows_gemm_scratch_size();
+    b.total = off;
+    return b;
+}
+
+size_t fxr_double_block_workspace_size(const fxr_frame_desc* desc, int32_t mlp_hidden) {
+    if (!desc || dtype_bytes(desc->dtype) == 0 || desc->n_heads <= 0 || desc->head_dim <= 0 || mlp_hidden <= 0)
+        return 0;
+    return carve_block(desc, mlp_hidden, nullptr).total;
+}
+
+static int32_t check_block_stream(const fxr_block_stream& s, const char* which) {
+    if (!s.w_qkv || !s.w_out || !s.w_mlp0 || !s.w_mlp2 || !s.norm_q || !s.norm_k)
+        return fail(FXR_ERR_INVALID, "%s stream: null weight", which);
+    const void* p16[] = {s.w_qkv, s.w_out, s.w_mlp0, s.w_mlp2, s.shift, s.scale, s.gate,
+                         s.b_qkv, s.b_out, s.b_mlp0, s.b_mlp2};
+    for (const void* p : p16)
+        if (!aligned16(p)) return fail(FXR_ERR_INVALID, "%s stream: weights must be 16-byte aligned", which);
+    return FXR_OK;
+}
+
+int32_t fxr_double_block_forward(const fxr_frame_desc* desc, const fxr_double_block* blk, const void* x_in,
+                                 void* x_out, int32_t* mask, uint8_t* valid, const int32_t* pos,
+                                 void* cache_k, void* cache_v, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+    int32_t st = check_desc(desc, true);
+    if (st != FXR_OK) return st;
+    if (!blk) return fail(FXR_ERR_INVALID, "null block");
+    const int32_t N = desc->n_tokens, T = desc->n_text, H = blk->mlp_hidden;
+    const int32_t C = desc->n_heads * desc->head_dim;
+    if (C % fxr::gemm::kBN || H <= 0 || H % fxr::gemm::kBN)
+        return fail(FXR_ERR_UNSUPPORTED, "n_heads * head_dim (%d) and mlp_hidden (%d) must be multiples of %d", C, H,
+                    fxr::gemm::kBN);
+    if (C > fxr::kLnMaxChunks * 256) return fail(FXR_ERR_UNSUPPORTED, "hidden size %d above %d", C, fxr::kLnMaxChunks * 256);
+    if (!(blk->ln_eps >= 0.f)) return fail(FXR_ERR_INVALID, "ln_eps must be >= 0");
+    if ((st = check_block_stream(blk->img, "image")) != FXR_OK) return st;
+    if (T > 0 && (st = check_block_stream(blk->txt, "text")) != FXR_OK) return st;
+    if (N == 0) return FXR_OK;
+    if (!x_in || !x_out || !mask || !cache_k || !cache_v || !workspace || (desc->rope_n_axes > 0 && !pos))
+        return fail(FXR_ERR_INVALID, "null pointer argument");
+    if (!aligned16(x_in) || !aligned16(x_out) || !aligned16(cache_k) || !aligned16(cache_v) || !aligned16(workspace))
+        return fail(FXR_ERR_INVALID, "x_in / x_out / caches / workspace must be 16-byte aligned");
+    const BlockViews b = carve_block(desc, H, workspace);
+    if (workspace_bytes < b.total)
+        return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, b.total);
+    // the frame steps see Q/K/V and the attention rows as contiguous [N, C] workspace buffers
+    fxr_frame_desc fd = *desc;
+    fd.ld_qkv = C;
+    fd.ld_out = C;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int32_t dt = desc->dtype;
+    int32_t* idx = b.frame.idx;
+    int32_t* count = b.frame.count;
+    char* gemm = b.gemm;
+    const size_t gemm_bytes = fxr_rows_gemm_scratch_size();
+    // 1. compaction; text tokens always execute; the GEMM sync words start from zero
+    {
+        fxr::CompactArgs ca{};
+        ca.s[0] = fxr::CompactStream{mask, valid, idx, count};
+        if ((st = launch_compact_streams(ca, 1, N, b.split, stream, gemm, fxr::gemm::kSyncBytes, T)) != FXR_OK)
+            return st;
+    }
+    const fxr_block_stream* ss[2] = {&blk->txt, &blk->img};
+    const int32_t r0[2] = {0, T}, r1[2] = {T, -1};
+    const int first = T > 0 ? 0 : 1;
+    // 2. LayerNorm + modulation of the executed rows (compact), 3. Q/K/V (scattered)
+    for (int k = first; k < 2; ++k) {
+        const fxr_block_stream& w = *ss[k];
+        if ((st = fxr_ln_modulate_rows(dt, x_in, C, C, idx, count, r0[k], r1[k], N, w.scale, w.shift, blk->ln_eps,
+                                       b.xn, C, stream)) != FXR_OK)
+            return st;
+    }
+    for (int k = first; k < 2; ++k) {
+        const fxr_block_stream& w = *ss[k];
+        fxr_rows_gemm_desc g{};
+        g.dtype = dt;
+        g.n_tokens = N;
+        g.row0 = r0[k];
+        g.row_end = r1[k];
+        g.n_operands = 1;
+        g.a[0] = fxr_rows_operand{b.xn, C, C, 0, w.w_qkv};
+        g.n_outputs = 3;
+        g.y[0] = fxr_rows_output{b.q, C, C, 1, FXR_ACT_NONE, 0};
+        g.y[1] = fxr_rows_output{b.k, C, C, 1, FXR_ACT_NONE, 0};
+        g.y[2] = fxr_rows_output{b.v, C, C, 1, FXR_ACT_NONE, 0};
+        g.bias0 = w.b_qkv;
+        if ((st = fxr_rows_gemm(&g, idx, count, gemm, gemm_bytes, stream)) != FXR_OK) return st;
+    }
+    // 4. gather + per-head QK-RMSNorm (each stream's weights) + RoPE, cache rows; 5. attention;
+    // 6. restore of the mask-1 cache rows
+    st = dt == FXR_BF16
+             ? launch_gather_streams<__nv_bfloat16>(&fd, 1, std::array<fxr::GatherStream, 1>{fxr::GatherStream{
+                                                                b.q, b.k, b.v, mask, idx, count, b.frame.qc,
+                                                                cache_k, cache_v, b.frame.save}}.data(),
+                                                    pos, blk->img.norm_q, blk->img.norm_k, b.frame.ld_qc, s,
+                                                    T > 0 ? blk->txt.norm_q : nullptr,
+                                                    T > 0 ? blk->txt.norm_k : nullptr, T)
+             : launch_gather_streams<__half>(&fd, 1, std::array<fxr::GatherStream, 1>{fxr::GatherStream{
+                                                         b.q, b.k, b.v, mask, idx, count, b.frame.qc, cache_k,
+                                                         cache_v, b.frame.save}}.data(),
+                                             pos, blk->img.norm_q, blk->img.norm_k, b.frame.ld_qc, s,
+                                             T > 0 ? blk->txt.norm_q : nullptr, T > 0 ? blk->txt.norm_k : nullptr,
+                                             T);
+    if (st != FXR_OK) return st;
+    OutSet os;
+    os.out = b.attn;
+    os.split = b.split;
+    st = dt == FXR_BF16 ? launch_attention<__nv_bfloat16>(&fd, b.frame.qc, b.frame.ld_qc, count, cache_k, cache_v,
+                                                          idx, os, s)
+                        : launch_attention<__half>(&fd, b.frame.qc, b.frame.ld_qc, count, cache_k, cache_v, idx,
+                                                   os, s);
+    if (st != FXR_OK) return st;
+    if ((st = fxr_restore_rows(&fd, mask, idx, count, b.frame.save, cache_k, cache_v, stream)) != FXR_OK) return st;
+    // 7. MLP up with GELU (compact), 8. out-projection + MLP down + gated residual (scattered)
+    for (int k = first; k < 2; ++k) {
+        const fxr_block_stream& w = *ss[k];
+        fxr_rows_gemm_desc g{};
+        g.dtype = dt;
+        g.n_tokens = N;
+        g.row0 = r0[k];
+        g.row_end = r1[k];
+        g.n_operands = 1;
+        g.a[0] = fxr_rows_operand{b.xn, C, C, 0, w.w_mlp0};
+        g.n_outputs = 1;
+        g.y[0] = fxr_rows_output{b.h, H, H, 0, FXR_ACT_GELU_TANH, 0};
+        g.bias0 = w.b_mlp0;
+        if ((st = fxr_rows_gemm(&g, idx, count, gemm, gemm_bytes, stream)) != FXR_OK) return st;
+    }
+    for (int k = first; k < 2; ++k) {
+        const fxr_block_stream& w = *ss[k];
+        fxr_rows_gemm_desc g{};
+        g.dtype = dt;
+        g.n_tokens = N;
+        g.row0 = r0[k];
+        g.row_end = r1[k];
+        g.n_operands = 2;
+        g.a[0] = fxr_rows_operand{b.attn, C, C, 1, w.w_out};
+        g.a[1] = fxr_rows_operand{b.h, H, H, 0, w.w_mlp2};
+        g.n_outputs = 1;
+        g.y[0] = fxr_rows_output{x_out, C, C, 1, FXR_ACT_NONE, 0};
+        g.bias0 = w.b_out;
+        g.bias1 = w.b_mlp2;
+        g.residual = x_in;
+        g.ld_residual = C;
+        g.gate = w.gate;
+        if ((st = fxr_rows_gemm(&g, idx, count, gemm, gemm_bytes, stream)) != FXR_OK) return st;
+    }
+    // 9. validity of the cache rows this frame updated
+    if (valid) return fxr_mark_updated(mask, valid, T, N, stream);
+    return FXR_OK;
 }
 
 size_t fxr_batch_workspace_size(const fxr_frame_desc* desc, int32_t n_streams) {

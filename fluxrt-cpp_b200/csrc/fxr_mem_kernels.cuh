@@ -41,6 +41,9 @@ struct CompactArgs {
     int32_t n;
     uint4* zero;                  // the attention's key-split arrival counters, zeroed by CTA 0
     int32_t zero_vec;
+    uint4* zero2;                 // a second area CTA 0 zeroes (the block's GEMM sync words)
+    int32_t zero2_vec;
+    int32_t n_force;              // tokens below this one execute whatever their mask (0 -> 2)
 };
 
 __global__ void __launch_bounds__(kCompactThreads, 1) compact_kernel(const __grid_constant__ CompactArgs a) {
@@ -55,8 +58,10 @@ __global__ void __launch_bounds__(kCompactThreads, 1) compact_kernel(const __gri
     pdl_launch_dependents();
     pdl_wait();  // the previous frame's kernels may still read mask / idx / count
     // the attention's key-split arrival counters of this frame (zero_vec 16-byte words)
-    if (blockIdx.x == 0)
+    if (blockIdx.x == 0) {
         for (int32_t e = threadIdx.x; e < a.zero_vec; e += kCompactThreads) a.zero[e] = make_uint4(0, 0, 0, 0);
+        for (int32_t e = threadIdx.x; e < a.zero2_vec; e += kCompactThreads) a.zero2[e] = make_uint4(0, 0, 0, 0);
+    }
     int32_t base = 0;
     for (int32_t c0 = 0; c0 < n; c0 += kCompactChunk) {
         const int32_t n_chunk = min(n - c0, kCompactChunk);
@@ -76,6 +81,10 @@ __global__ void __launch_bounds__(kCompactThreads, 1) compact_kernel(const __gri
             const int32_t e = e0 + g * 32;
             if (valid != nullptr && g < gpw && e < c0 + n_chunk && valid[e] == 0) {
                 if (mval[g] != 2) mask[e] = 2;
+                mval[g] = 2;
+            }
+            if (g < gpw && e < c0 + n_chunk && e < a.n_force && mval[g] == 0) {
+                mask[e] = 2;
                 mval[g] = 2;
             }
             ballot[g] = __ballot_sync(0xffffffffu, mval[g] != 0);
@@ -149,6 +158,9 @@ struct GatherArgs {
     const int32_t* pos;
     const float* norm_q;
     const float* norm_k;
+    const float* norm_q_txt;     // tokens below n_text_norm use these (a double-stream block's
+    const float* norm_k_txt;     // text stream); null: norm_q / norm_k for every token
+    int32_t n_text_norm;
     int64_t ld_qkv, ld_qc, ld_cache;
     int32_t n_tokens, n_heads, n_axes;
     float eps;
@@ -341,12 +353,11 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
         const bool isq = gw < kBulkGroupWarps / 2;           // warp-uniform: Q or K heads
         constexpr int kHeadStride = kBulkGroupWarps;         // half-warps per tensor
         const int hw0 = (gw % (kBulkGroupWarps / 2)) * 2;     // first head of this warp
-        float2 w2[4];
-        {
-            const float* wsrc = (isq ? a.norm_q : a.norm_k) + 8 * sub;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) w2[t] = make_float2(__ldg(wsrc + 2 * t), __ldg(wsrc + 2 * t + 1));
-        }
+        // norm weights: the image stream's (every token's without a text stream) and the text
+        // stream's (rows < n_text_norm); this lane's 8 are read per row (L1 hits)
+        const float* wimg = (isq ? a.norm_q : a.norm_k) + 8 * sub;
+        const float* wtxt = isq ? a.norm_q_txt : a.norm_k_txt;
+        if (wtxt != nullptr) wtxt += 8 * sub;
         const bool bulk_lane = gw == 0 && lane == 0;
         const int gtid = gw * 32 + lane;
         for (int32_t k = grp; k < rows_here; k += kBulkGroups) {
@@ -380,6 +391,12 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
                     if (mode == 1) fence_proxy_async();   // old V row read before it is overwritten
                     bulk_store(CV + (int64_t)i * a.ld_cache, smem_u32(stage + 2 * row_bytes), row_bytes);
                     bulk_commit();
+                }
+                float2 w2[4];
+                {
+                    const float* ws = (wtxt != nullptr && i < a.n_text_norm) ? wtxt : wimg;
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) w2[t] = make_float2(__ldg(ws + 2 * t), __ldg(ws + 2 * t + 1));
                 }
                 float cs[4], sn[4];
 #pragma unroll

@@ -39,6 +39,7 @@ EXPORTED = [
     "fxr_heads_nccl_workspace_size", "fxr_allgather_heads", "fxr_frame_forward_heads_nccl",
     "fxr_batch_workspace_size", "fxr_frame_forward_batch", "fxr_qkv_project",
     "fxr_ln_modulate_rows", "fxr_rows_gemm_scratch_size", "fxr_rows_gemm",
+    "fxr_double_block_workspace_size", "fxr_double_block_forward",
 ]
 
 FXR_ACT_NONE, FXR_ACT_GELU_TANH = 0, 1
@@ -76,6 +77,19 @@ class RowsGemmDesc(ctypes.Structure):
                 ("n_outputs", ctypes.c_int32), ("a", RowsOperand * 2), ("y", RowsOutput * 4),
                 ("bias0", ctypes.c_void_p), ("bias1", ctypes.c_void_p), ("residual", ctypes.c_void_p),
                 ("ld_residual", ctypes.c_int64), ("gate", ctypes.c_void_p)]
+
+
+class BlockStream(ctypes.Structure):
+    """Mirror of fxr_block_stream (include/fxr.h)."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ("shift", "scale", "gate", "w_qkv", "b_qkv", "norm_q",
+                                                "norm_k", "w_out", "b_out", "w_mlp0", "b_mlp0",
+                                                "w_mlp2", "b_mlp2")]
+
+
+class DoubleBlock(ctypes.Structure):
+    """Mirror of fxr_double_block (include/fxr.h)."""
+    _fields_ = [("txt", BlockStream), ("img", BlockStream), ("mlp_hidden", ctypes.c_int32),
+                ("ln_eps", ctypes.c_float)]
 
 
 class PluginField(ctypes.Structure):
@@ -174,6 +188,10 @@ def load(path: str | None = None) -> ctypes.CDLL:
     L.fxr_rows_gemm_scratch_size.argtypes = []
     L.fxr_rows_gemm_scratch_size.restype = ctypes.c_size_t
     L.fxr_rows_gemm.argtypes = [ctypes.POINTER(RowsGemmDesc), _vp, _vp, _vp, ctypes.c_size_t, _vp]
+    L.fxr_double_block_workspace_size.argtypes = [ctypes.POINTER(FrameDesc), _i32]
+    L.fxr_double_block_workspace_size.restype = ctypes.c_size_t
+    L.fxr_double_block_forward.argtypes = [ctypes.POINTER(FrameDesc), ctypes.POINTER(DoubleBlock)] + \
+        [_vp] * 8 + [ctypes.c_size_t, _vp]
     L.fxr_batch_workspace_size.argtypes = [ctypes.POINTER(FrameDesc), _i32]
     L.fxr_batch_workspace_size.restype = ctypes.c_size_t
     L.fxr_frame_forward_batch.argtypes = [ctypes.POINTER(FrameDesc), _i32, ctypes.POINTER(StreamFrame),
@@ -683,3 +701,32 @@ def rows_gemm(operands, outputs, idx, count, n_tokens, bias0=None, bias1=None, r
     d.ld_residual = residual.stride(0) if residual is not None else 0
     _check(load().fxr_rows_gemm(ctypes.byref(d), _ptr(idx), _ptr(count), _ptr(scratch),
                                 scratch.numel() if scratch is not None else 0, _stream(stream)))
+
+
+_BLOCK_FIELDS = ("shift", "scale", "gate", "w_qkv", "b_qkv", "norm_q", "norm_k", "w_out", "b_out",
+                 "w_mlp0", "b_mlp0", "w_mlp2", "b_mlp2")
+
+
+def block_stream(**tensors) -> BlockStream:
+    """fxr_block_stream from device tensors (missing or None fields are NULL)."""
+    bs = BlockStream()
+    for n in _BLOCK_FIELDS:
+        setattr(bs, n, _ptr(tensors.get(n)))
+    return bs
+
+
+def double_block_workspace_size(cfg: FrameConfig, mlp_hidden: int) -> int:
+    d = cfg.desc()
+    return int(load().fxr_double_block_workspace_size(ctypes.byref(d), mlp_hidden))
+
+
+def double_block_forward(cfg: FrameConfig, txt: dict, img: dict, mlp_hidden: int, x_in, x_out, mask,
+                         valid, pos, cache_k, cache_v, workspace, ln_eps=1e-6, stream=None):
+    """One double-stream block on the executed rows (fxr_double_block_forward). txt / img: dicts of
+    the fxr_block_stream fields (device tensors)."""
+    d = cfg.desc()
+    blk = DoubleBlock(block_stream(**txt), block_stream(**img), mlp_hidden, ln_eps)
+    _check(load().fxr_double_block_forward(ctypes.byref(d), ctypes.byref(blk), _ptr(x_in), _ptr(x_out),
+                                           _ptr(mask), _ptr(valid), _ptr(pos), _ptr(cache_k),
+                                           _ptr(cache_v), _ptr(workspace), workspace.numel(),
+                                           _stream(stream)))

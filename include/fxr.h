@@ -275,6 +275,49 @@ size_t fxr_rows_gemm_scratch_size(void);
 int32_t fxr_rows_gemm(const fxr_rows_gemm_desc* d, const int32_t* idx, const int32_t* count,
                       void* scratch, size_t scratch_bytes, void* stream);
 
+/* ---- the double-stream block on the executed rows -------------------------------------------------
+ * One FLUX.2 double-stream block over a frame whose tokens are text [0, n_text) then image
+ * [n_text, n_tokens), computing only the executed rows. The reference's Flux2DoubleBlockPlugin
+ * enqueue (flux2_double_block_plugin.cpp:330-460) runs every step on every token in fp32:
+ *   x_out = x_in + gate * (out_proj(attn(q, k, v)) + mlp(LN_mod(x_in))),  q/k/v = proj(LN_mod(x_in))
+ * with separate text / image weights. Here, per frame (13 launches, no host synchronisation):
+ *   compaction (text tokens always execute) -> LayerNorm + modulation of the executed rows ->
+ *   Q/K/V (text rows with the text weights, image rows with the image weights) -> gather with each
+ *   stream's QK-RMSNorm + RoPE, K/V cache rows -> joint attention of the executed queries over all
+ *   cache rows -> restore of mask-1 cache rows -> MLP up (tanh GELU) -> out-projection + MLP down +
+ *   gated residual into the executed rows of x_out -> validity of the updated cache rows.
+ * Rows of skipped image tokens of x_out are left untouched (the caller's previous output: the
+ * output cache). x_in / x_out: [n_tokens, C] contiguous, C = n_heads * head_dim (multiple of 256,
+ * at most 4096); cache_k / cache_v: [n_tokens, ld_cache]; desc->ld_qkv / ld_out are not used. */
+typedef struct fxr_block_stream {   /* one stream (text or image) of a double-stream block */
+    const float* shift;      /* [C] modulation shift (temb[0:C] in the reference) or NULL */
+    const float* scale;      /* [C] modulation scale (temb[C:2C]) or NULL */
+    const float* gate;       /* [C] residual gate or NULL (1, as the reference) */
+    const void* w_qkv;       /* [3C, C]: the rows of to_q, to_k, to_v stacked */
+    const float* b_qkv;      /* [3C] or NULL */
+    const float* norm_q;     /* [head_dim] QK-RMSNorm weights */
+    const float* norm_k;
+    const void* w_out;       /* [C, C] */
+    const float* b_out;      /* [C] or NULL */
+    const void* w_mlp0;      /* [H, C] */
+    const float* b_mlp0;     /* [H] or NULL */
+    const void* w_mlp2;      /* [C, H] */
+    const float* b_mlp2;     /* [C] or NULL */
+} fxr_block_stream;
+
+typedef struct fxr_double_block {
+    fxr_block_stream txt;    /* tokens [0, n_text) */
+    fxr_block_stream img;    /* tokens [n_text, n_tokens) */
+    int32_t mlp_hidden;      /* H: multiple of 256 (3C for FLUX.2) */
+    float ln_eps;            /* LayerNorm eps (1e-6 in the reference) */
+} fxr_double_block;
+
+size_t fxr_double_block_workspace_size(const fxr_frame_desc* desc, int32_t mlp_hidden);
+int32_t fxr_double_block_forward(const fxr_frame_desc* desc, const fxr_double_block* blk,
+                                 const void* x_in, void* x_out, int32_t* mask, uint8_t* valid,
+                                 const int32_t* pos, void* cache_k, void* cache_v,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* QKV projection of the executed tokens from token-major hidden states:
  *   [q | k | v][idx[m], :] = hidden[idx[m], :] . w_qkv^T (+ bias)   for m < *count
  * hidden: [n_tokens, ld_hidden] (k_dim columns, multiple of 64); w_qkv: [3C, k_dim] row-major
