@@ -47,6 +47,10 @@ def parse():
     ap.add_argument("--streams", type=int, default=None,
                     help="independent edit streams in total (one batched set of launches per GPU "
                          "per step; c4 default 8, spread over the GPUs)")
+    ap.add_argument("--path", choices=["attention", "block"], default="attention",
+                    help="attention: the sparse attention frame (the metric's path); block: the whole "
+                         "double-stream block on the executed rows (LayerNorm, Q/K/V, attention, MLP, "
+                         "out-projection, residual)")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
@@ -927,13 +931,355 @@ def run_streams(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------------------------
+# the whole double-stream block on the executed rows (--path block)
+# ---------------------------------------------------------------------------------------------
+BLOCK_METRIC = "double-block frames/s @1024², 25% active (executed rows only; LN+QKV+attn+MLP+out)"
+
+
+def block_weights(w, H: int, device, seed: int) -> dict:
+    """Random-init weights of one double-stream block (text and image streams), bf16 matrices."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    C = w.n_heads * HEAD_DIM
+    r = lambda *shape, sd=1.0: torch.randn(*shape, generator=g, device=device) * sd
+    out = {}
+    for name in ("txt", "img"):
+        out[name] = {"shift": r(C, sd=0.1), "scale": r(C, sd=0.1), "gate": 1.0 + r(C, sd=0.2),
+                     "w_qkv": r(3 * C, C, sd=C ** -0.5).bfloat16(), "b_qkv": r(3 * C, sd=0.05),
+                     "norm_q": 1.0 + r(HEAD_DIM, sd=0.1), "norm_k": 1.0 + r(HEAD_DIM, sd=0.1),
+                     "w_out": r(C, C, sd=C ** -0.5).bfloat16(), "b_out": r(C, sd=0.05),
+                     "w_mlp0": r(H, C, sd=C ** -0.5).bfloat16(), "b_mlp0": r(H, sd=0.05),
+                     "w_mlp2": r(C, H, sd=H ** -0.5).bfloat16(), "b_mlp2": r(C, sd=0.05)}
+    return out
+
+
+def block_gemm_flops(w, M: int, H: int) -> float:
+    C = w.n_heads * HEAD_DIM
+    return 2.0 * M * C * 3 * C + 2.0 * M * C * H + 2.0 * M * (C + H) * C
+
+
+def block_flops(w, M: int, H: int) -> float:
+    return block_gemm_flops(w, M, H) + attn_flops(w, M)
+
+
+def _graph_us(fn, reps: int = 20, rounds: int = 7) -> float:
+    """Median device time of one call, from CUDA graphs of `reps` back-to-back calls."""
+    import torch
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(rounds):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3 / reps)
+    return statistics.median(ts)
+
+
+def dense_block_torch(w, H, wts, x, pos_cos_sin):
+    """The same block computed densely on every token with torch bf16 (cuBLAS GEMMs, SDPA
+    attention): what running the block without the spatial cache costs on this GPU."""
+    import torch
+    import torch.nn.functional as F
+    T, C = w.n_text, w.n_heads * HEAD_DIM
+    cos, sin = pos_cos_sin
+    outs = []
+    qkv_all, xn_all = [], []
+    for name, sl in (("txt", slice(0, T)), ("img", slice(T, None))):
+        s = wts[name]
+        xn = (F.layer_norm(x[sl].float(), (C,), eps=1e-6) * (1 + s["scale"]) + s["shift"]).bfloat16()
+        xn_all.append(xn)
+        qkv_all.append(F.linear(xn, s["w_qkv"], s["b_qkv"].bfloat16()))
+    qkv = torch.cat(qkv_all)
+    q, k, v = qkv.split(C, dim=1)
+
+    def norm_rope(t, wn):
+        t = t.view(-1, w.n_heads, HEAD_DIM).float()
+        t = t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-6) * wn
+        t1, t2 = t[..., 0::2], t[..., 1::2]
+        return torch.stack((t1 * cos - t2 * sin, t1 * sin + t2 * cos), -1).flatten(-2).bfloat16()
+    qn = norm_rope(q, wts["img"]["norm_q"]).transpose(0, 1).unsqueeze(0)
+    kn = norm_rope(k, wts["img"]["norm_k"]).transpose(0, 1).unsqueeze(0)
+    vv = v.reshape(-1, w.n_heads, HEAD_DIM).transpose(0, 1).unsqueeze(0)
+    o = F.scaled_dot_product_attention(qn, kn, vv).squeeze(0).transpose(0, 1).reshape(-1, C)
+    for (name, sl), xn in zip((("txt", slice(0, T)), ("img", slice(T, None))), xn_all):
+        s = wts[name]
+        h = F.gelu(F.linear(xn, s["w_mlp0"], s["b_mlp0"].bfloat16()), approximate="tanh")
+        y = F.linear(o[sl], s["w_out"], s["b_out"].bfloat16()) + F.linear(h, s["w_mlp2"], s["b_mlp2"].bfloat16())
+        outs.append(x[sl] + s["gate"].bfloat16() * y)
+    return torch.cat(outs)
+
+
+def run_block(args):
+    import torch
+    import fxr
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    fxr.load()
+    w = workload(args)
+    cfg = frame_cfg(w)
+    pk = peaks()
+    N, T, C = w.n_tokens, w.n_text, w.n_heads * HEAD_DIM
+    H = 3 * C
+    wts = block_weights(w, H, device, args.seed + 17 * rank)
+    n_sets = 2
+    sets = []
+    for sidx in range(n_sets):
+        fr = make_device_frame(w, args.seed + 7919 * rank + sidx, device)
+        sets.append({"x_in": fr["q"], "x_out": fr["out"], "mask": fr["mask"], "pos": fr["pos"],
+                     "valid": torch.ones(N, dtype=torch.uint8, device=device),
+                     "cache_k": fr["cache_k"], "cache_v": fr["cache_v"], "M": fr["M"],
+                     "ws": torch.empty(fxr.double_block_workspace_size(cfg, H), dtype=torch.uint8,
+                                       device=device)})
+
+    def run(st):
+        fxr.double_block_forward(cfg, wts["txt"], wts["img"], H, st["x_in"], st["x_out"], st["mask"],
+                                 st["valid"], st["pos"], st["cache_k"], st["cache_v"], st["ws"])
+
+    for i in range(max(args.warmup, 3)):
+        run(sets[i % n_sets])
+    torch.cuda.synchronize()
+    if fxr.check_device_error() != 0:
+        raise RuntimeError("device error during warm-up")
+    graphs = []
+    for st in sets:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run(st)
+        graphs.append(g)
+    stream = torch.cuda.current_stream()
+    clocks = Clocks(local)
+    clocks.start()
+    t_end = time.time() + 1.0
+    i = 0
+    while time.time() < t_end:
+        graphs[i % n_sets].replay()
+        i += 1
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        graphs[i % n_sets].replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    t_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([t_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_ms = float(t.item())
+    if fxr.check_device_error() != 0:
+        raise RuntimeError("device error during the timed region")
+    ms = t_ms / args.steps
+    M_avg = statistics.mean(st["M"] for st in sets)
+    fl = block_flops(w, M_avg, H)
+
+    # ---- the block's kernels one at a time (image rows of set 0; graphs of 20 launches) ----
+    st = sets[0]
+    idx = torch.empty(N, dtype=torch.int32, device=device)
+    cnt = torch.empty(1, dtype=torch.int32, device=device)
+    fxr.mask_compact(st["mask"], None, idx, cnt)
+    xn = torch.randn(N, C, device=device).bfloat16()
+    qkv = [torch.empty(N, C, device=device, dtype=torch.bfloat16) for _ in range(3)]
+    hbuf = torch.randn(N, H, device=device).bfloat16() * 0.1
+    attn = torch.randn(N, C, device=device).bfloat16()
+    yout = torch.empty(N, C, device=device, dtype=torch.bfloat16)
+    scr = fxr.rows_gemm_scratch(device)
+    s_img = wts["img"]
+    kern = {
+        "ln_modulate": _graph_us(lambda: fxr.ln_modulate_rows(st["x_in"], idx, cnt, xn, s_img["scale"],
+                                                              s_img["shift"], row0=T)),
+        "qkv_gemm": _graph_us(lambda: fxr.rows_gemm([(xn, s_img["w_qkv"], False)],
+                                                    [(t, C, True, 0) for t in qkv], idx, cnt, N,
+                                                    bias0=s_img["b_qkv"], row0=T, scratch=scr)),
+        "mlp_up_gemm": _graph_us(lambda: fxr.rows_gemm([(xn, s_img["w_mlp0"], False)],
+                                                       [(hbuf, H, False, fxr.FXR_ACT_GELU_TANH)], idx, cnt, N,
+                                                       bias0=s_img["b_mlp0"], row0=T, scratch=scr)),
+        "out_down_gemm": _graph_us(lambda: fxr.rows_gemm([(attn, s_img["w_out"], True), (hbuf, s_img["w_mlp2"], False)],
+                                                         [(yout, C, True, 0)], idx, cnt, N, bias0=s_img["b_out"],
+                                                         bias1=s_img["b_mlp2"], residual=st["x_in"],
+                                                         gate=s_img["gate"], row0=T, scratch=scr)),
+    }
+    M_img = st["M"] - T
+    qkv_fl = 2.0 * M_img * C * 3 * C
+    achieved = qkv_fl / (kern["qkv_gemm"] * 1e-6) / 1e12
+    roof = {"bound": "tensor", "kernel": "fxr::gemm::rows_gemm_kernel (Q/K/V of the executed image rows)",
+            "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": round(achieved / pk["bf16_tflops"], 4), "peak_kind": f"{pk['source']} burst bf16 (cuBLAS)",
+            "traffic": profile_traffic(f"rows_gemm_qkv_{w.name}"), "algorithmic_flop_per_launch": qkv_fl}
+
+    # ---- the dense block on every token with torch (cuBLAS + SDPA), same GPU ----
+    import workloads as W
+    posn = torch.from_numpy(W.positions(w)).to(device)
+    ax = list(w.rope_axes)
+    ang = []
+    for a, d in enumerate(ax):
+        om = w.rope_theta ** (-torch.arange(0, d, 2, device=device, dtype=torch.float64) / d)
+        ang.append(posn[:, a:a + 1].double() * om)
+    ang = torch.cat(ang, dim=1).float()[:, None, :]
+    cs = (torch.cos(ang), torch.sin(ang))
+    dense_us = _graph_us(lambda: dense_block_torch(w, H, wts, st["x_in"], cs), reps=5, rounds=5)
+
+    # ---- end to end through the C ABI with pinned host buffers (x_in and mask in, x_out back) ----
+    host_x = st["x_in"].cpu().pin_memory()
+    host_m = torch.from_numpy(W.make_mask(w, np.random.default_rng(args.seed))).pin_memory()
+    host_o = torch.empty_like(host_x).pin_memory()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def one():
+        st["x_in"].copy_(host_x, non_blocking=True)
+        st["mask"].copy_(host_m, non_blocking=True)
+        run(st)
+        host_o.copy_(st["x_out"], non_blocking=True)
+    for _ in range(3):
+        one()
+    torch.cuda.synchronize()
+    reps = max(5, min(30, args.steps))
+    ev0.record(stream)
+    for _ in range(reps):
+        one()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ev0.elapsed_time(ev1) / reps
+    e2e = {"value": round(1e3 / e2e_ms, 2), "unit": "frames/s", "us_per_frame": round(e2e_ms * 1e3, 1),
+           "h2d_bytes_per_step": int(host_x.numel() * 2 + host_m.numel() * 4),
+           "d2h_bytes_per_step": int(host_o.numel() * 2),
+           "path": "fxr_double_block_forward via ctypes, pinned host x_in / mask in, x_out back"}
+    out = {
+        "metric": BLOCK_METRIC, "value": round(1e3 / ms * world, 2), "unit": "frames/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "us_per_frame": round(ms * 1e3, 2), "block_tflops": round(fl / (ms * 1e-3) / 1e12, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype, "impl": "ours",
+        "data": "synthetic: N(0,1) hidden states and caches, random-init block weights (seeded)",
+        "config": {"workload": w.name + "_double_block", "n_tokens": N, "n_text": T, "active": w.active,
+                   "M_avg": M_avg, "heads": w.n_heads, "hidden": C, "mlp_hidden": H,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "weights 377 MB per step > L2", "graph": True},
+        "roofline": roof,
+        "kernels_isolated_us": {k: round(v, 2) for k, v in kern.items()},
+        "dense_torch_same_gpu_us": round(dense_us, 1),
+        "e2e": e2e,
+        "gpu_launches": 13 * args.steps,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            out["cpu_baseline"] = cpu_block_baseline(w, H, args.seed)
+        except Exception as ex:  # the baseline is reported, not required
+            out["cpu_baseline"] = {"value": None, "error": str(ex)[:200]}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        graphs.clear()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_block_sample(w, H: int, seed: int, rows: int = 256) -> dict:
+    """The reference block's fp32 math on the host cores as the reference runs it, densely on every
+    token (flux2_double_block_plugin.cpp:330-460): LayerNorm + modulation and Q/K/V of all N
+    tokens, then QK-RMSNorm, attention, MLP and out-projection of a sample of `rows` query tokens
+    over all N keys, scaled to N rows. numpy BLAS; returns seconds per frame."""
+    rng = np.random.default_rng(seed)
+    N, C = w.n_tokens, w.n_heads * HEAD_DIM
+    f = lambda *shape, sd=1.0: (rng.standard_normal(shape, dtype=np.float32) * sd)
+    x = f(N, C)
+    wq, wo, w0, w2 = f(3 * C, C, sd=C ** -0.5), f(C, C, sd=C ** -0.5), f(H, C, sd=C ** -0.5), f(C, H, sd=H ** -0.5)
+    t0 = time.perf_counter()
+    mean = x.mean(1, keepdims=True)
+    xn = (x - mean) / np.sqrt(((x - mean) ** 2).mean(1, keepdims=True) + 1e-6)
+    qkv = xn @ wq.T
+    t_all = time.perf_counter() - t0
+    sel = rng.choice(N, size=rows, replace=False)
+    t1 = time.perf_counter()
+    q = qkv[sel, :C].reshape(rows, w.n_heads, HEAD_DIM)
+    k = qkv[:, C:2 * C].reshape(N, w.n_heads, HEAD_DIM)
+    v = qkv[:, 2 * C:].reshape(N, w.n_heads, HEAD_DIM)
+    q = q / np.sqrt((q ** 2).mean(-1, keepdims=True) + 1e-6)
+    k = k / np.sqrt((k ** 2).mean(-1, keepdims=True) + 1e-6)
+    o = np.empty((rows, w.n_heads, HEAD_DIM), np.float32)
+    for h in range(w.n_heads):
+        s = (q[:, h] @ k[:, h].T) / np.sqrt(HEAD_DIM)
+        s = np.exp(s - s.max(1, keepdims=True))
+        o[:, h] = (s / s.sum(1, keepdims=True)) @ v[:, h]
+    hh = xn[sel] @ w0.T
+    hh = 0.5 * hh * (1 + np.tanh(0.7978845608 * (hh + 0.044715 * hh ** 3)))
+    _ = x[sel] + o.reshape(rows, C) @ wo.T + hh @ w2.T
+    t_rows = time.perf_counter() - t1
+    return {"seconds_per_frame": t_all + t_rows * N / rows, "rows": rows}
+
+
+def cpu_block_baseline(w, H: int, seed: int) -> dict:
+    try:
+        import threadpoolctl
+        cores = max(info.get("num_threads", 1) for info in threadpoolctl.threadpool_info()) or 1
+    except Exception:
+        cores = os.cpu_count() or 1
+    s = cpu_block_sample(w, H, seed)
+    spf = s["seconds_per_frame"]
+    return {"value": round(1.0 / spf, 4), "unit": "frames/s", "cores": cores, "kind": "port",
+            "sample": f"one dense fp32 frame of {w.name}: LayerNorm + Q/K/V of all {w.n_tokens} tokens, "
+                      f"attention/MLP/out-projection of {s['rows']} sampled query tokens over all keys "
+                      f"scaled to {w.n_tokens} (numpy BLAS)",
+            "seconds_per_frame": round(spf, 3)}
+
+
+def run_block_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    w = workload(args)
+    H = 3 * w.n_heads * HEAD_DIM
+    cpu_block_sample(w, H, args.seed, rows=32)                 # warm the BLAS pool
+    steps = max(1, min(args.steps, 5))
+    t = [cpu_block_sample(w, H, args.seed + i)["seconds_per_frame"] for i in range(steps)]
+    spf = statistics.mean(t)
+    base = cpu_block_baseline(w, H, args.seed)
+    out = {"metric": BLOCK_METRIC, "value": round(1.0 / spf, 4), "unit": "frames/s", "n_gpus": world,
+           "steps": steps, "warmup": 1, "ms_per_step": round(spf * 1e3, 1), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+           "data": "synthetic (seeded)", "config": {"workload": w.name + "_double_block", "n_tokens": w.n_tokens},
+           "cpu_baseline": dict(base, value=round(1.0 / spf, 4)),
+           "e2e": {"value": round(1.0 / spf, 4), "unit": "frames/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0},
+           "note": "the reference block runs densely in fp32 (cublasSgemm per projection); this arm "
+                   "times the same dense fp32 math on the host cores with numpy BLAS"}
+    print(json.dumps(out), flush=True)
+
+
 def _heads_split(n_heads, world):
     return [n_heads // world + (1 if r < n_heads % world else 0) for r in range(world)]
 
 
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.path == "block":
+        (run_block_reference if args.impl == "reference" else run_block)(args)
+    elif args.impl == "reference":
         run_reference(args)
     elif args.split in ("heads", "heads_nccl"):
         run_heads(args)

@@ -258,6 +258,12 @@ def ref_kernels():
     for f in (L.ref_gather_tokens, L.ref_scatter_tokens):
         f.argtypes = [vp, vp, vp, i32, i32, vp]
         f.restype = None
+    L.ref_gelu.argtypes = [vp, i32, vp]
+    L.ref_gelu.restype = None
+    L.ref_bias_add.argtypes = [vp, vp, i32, i32, vp]
+    L.ref_bias_add.restype = None
+    L.ref_apply_modulation.argtypes = [vp, vp, vp, vp, i32, i32, vp]
+    L.ref_apply_modulation.restype = None
     L.ref_rms_norm.argtypes = [vp, vp, vp, ctypes.c_float, i32, i32, vp]
     L.ref_rms_norm.restype = None
     L.ref_attention_fwd.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]

@@ -1,7 +1,7 @@
 // ref_shim.cu — extern "C" entry points over fluxrt-cpp's own CUDA kernels (compiled from the
 // reference sources by oracle/build_ref.sh). TEST INFRASTRUCTURE ONLY: used by the GPU tests to
 // cross-check the bit-exact steps against the reference itself, and as a timing baseline.
-// Wrapped interfaces: gather_scatter_kernels.h:21-36, flux2_kernels.h:22-24,
+// Wrapped interfaces: gather_scatter_kernels.h:21-36,46-49, flux2_kernels.h:15-24,
 // attention_kernels.h:20-24, spatial_kv_cache.h:12-55.
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -26,6 +26,19 @@ void ref_scatter_tokens(const float* src, float* dst, const int32_t* idx, int32_
 void ref_rms_norm(const float* x, float* y, const float* w, float eps, int32_t rows, int32_t dim,
                   void* stream) {
     fluxrt::plugins::launch_rms_norm(x, y, w, eps, rows, dim, static_cast<cudaStream_t>(stream));
+}
+
+void ref_gelu(float* data, int32_t n, void* stream) {
+    fluxrt::plugins::launch_gelu(data, n, static_cast<cudaStream_t>(stream));
+}
+
+void ref_bias_add(float* data, const float* bias, int32_t rows, int32_t dim, void* stream) {
+    fluxrt::plugins::launch_bias_add(data, bias, rows, dim, static_cast<cudaStream_t>(stream));
+}
+
+void ref_apply_modulation(const float* x, const float* scale, const float* shift, float* out,
+                          int32_t rows, int32_t dim, void* stream) {
+    fluxrt::plugins::apply_modulation(x, scale, shift, out, rows, dim, static_cast<cudaStream_t>(stream));
 }
 
 void ref_attention_fwd(const float* q, const float* k, const float* v, float* out, int32_t b,

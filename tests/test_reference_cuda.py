@@ -1,11 +1,13 @@
 """Cross-check against the reference's own CUDA kernels, compiled for sm_100a from its sources by
 oracle/build_ref.sh into oracle/_ref (skipped when that library was not built).
 
-Bit-exact steps only: row gather/scatter (gather_scatter_kernels.cu:15-72) and the spatial-cache
+Row gather/scatter (gather_scatter_kernels.cu:15-72) and the spatial-cache
 protocol — preprocess, K/V merge + update, output merge + update + validity
 (spatial_kv_cache.cu:12-87, SpatialCache methods :153-196) — over two frames, so that the second
-frame runs on the state the first one left. The reference RMSNorm (uninitialised shared
-accumulator, flux2_kernels.cu:58-82) and attention (one warp's partial max and sum broadcast as
+frame runs on the state the first one left — bit-exact; the GELU, bias and modulation kernels
+(flux2_kernels.cu:14-56, gather_scatter_kernels.cu:77-99) against the block tests' restatements
+and the GEMM's fused epilogue. The reference RMSNorm and LayerNorm (uninitialised shared
+accumulators, flux2_kernels.cu:58-82, gather_scatter_kernels.cu:129-150) and attention (one warp's partial max and sum broadcast as
 the block's, attention_kernels.cu:117-139) are not deterministic oracles and are only timed
 (oracle/time_reference_cuda.py)."""
 import numpy as np
@@ -105,3 +107,52 @@ def test_spatial_cache_protocol_matches_reference_over_two_frames(ref):
     finally:
         torch.cuda.synchronize()
         ref.ref_cache_destroy(h)
+
+
+def test_gelu_and_modulation_restatements_match_reference(ref):
+    """The tanh GELU and the modulation that the block tests restate (tests/test_block_rows.py,
+    tests/test_double_block.py) against the reference's own gelu_kernel (flux2_kernels.cu:14-29)
+    and apply_modulation_kernel (gather_scatter_kernels.cu:77-99), fp32 on the GPU."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(1 << 16, device="cuda", generator=g) * 3
+    a = x.clone()
+    ref.ref_gelu(a.data_ptr(), a.numel(), _s())
+    mine = 0.5 * x * (1.0 + torch.tanh(0.7978845608 * (x + 0.044715 * x * x * x)))
+    torch.cuda.synchronize()
+    assert torch.allclose(a, mine, rtol=4e-6, atol=4e-7), float((a - mine).abs().max())
+    rows, dim = 257, 3072
+    xm = torch.randn(rows, dim, device="cuda", generator=g)
+    sc = torch.randn(dim, device="cuda", generator=g) * 0.2
+    sh = torch.randn(dim, device="cuda", generator=g) * 0.2
+    out = torch.empty_like(xm)
+    ref.ref_apply_modulation(xm.data_ptr(), sc.data_ptr(), sh.data_ptr(), out.data_ptr(), rows, dim, _s())
+    torch.cuda.synchronize()
+    assert torch.allclose(out, (1.0 + sc) * xm + sh, rtol=1e-6, atol=1e-6)
+
+
+def test_rows_gemm_gelu_epilogue_matches_reference_gelu(ref):
+    """The GEMM's fused bias + GELU epilogue against the reference's bias_add + gelu kernels
+    (flux2_kernels.cu:14-56): a one-hot W makes the product an exact copy of the A columns, so the
+    epilogue sees the same fp32 values the reference kernels get; ours rounds to bf16 once."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(6)
+    M, K, n_out = 640, 64, 256
+    a = (torch.rand(M, K, device="cuda", generator=g) * 12 - 6).bfloat16()
+    w = torch.zeros(n_out, K, device="cuda", dtype=torch.bfloat16)
+    w[torch.arange(n_out), torch.arange(n_out) % K] = 1.0
+    bias = torch.randn(n_out, device="cuda", generator=g) * 0.5
+    idx = torch.arange(M, dtype=torch.int32, device="cuda")
+    cnt = torch.tensor([M], dtype=torch.int32, device="cuda")
+    y = torch.empty(M, n_out, device="cuda", dtype=torch.bfloat16)
+    fxr.rows_gemm([(a, w, False)], [(y, n_out, False, fxr.FXR_ACT_GELU_TANH)], idx, cnt, M, bias0=bias)
+    r = a.float()[:, torch.arange(n_out, device="cuda") % K].contiguous()
+    ref.ref_bias_add(r.data_ptr(), bias.data_ptr(), M, n_out, _s())
+    ref.ref_gelu(r.data_ptr(), r.numel(), _s())
+    torch.cuda.synchronize()
+    assert fxr.check_device_error() == 0
+    rb = r.bfloat16().float()
+    diff = (y.float() - rb).abs()
+    ulp = 2.0 ** (torch.floor(torch.log2(rb.abs().clamp_min(1e-30))) - 7)
+    assert bool((diff <= ulp).all()), float((diff / ulp).max())   # one bf16 rounding apart at most
+    assert float((diff == 0).float().mean()) > 0.99
