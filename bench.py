@@ -47,10 +47,11 @@ def parse():
     ap.add_argument("--streams", type=int, default=None,
                     help="independent edit streams in total (one batched set of launches per GPU "
                          "per step; c4 default 8, spread over the GPUs)")
-    ap.add_argument("--path", choices=["attention", "block"], default="attention",
+    ap.add_argument("--path", choices=["attention", "block", "single"], default="attention",
                     help="attention: the sparse attention frame (the metric's path); block: the whole "
                          "double-stream block on the executed rows (LayerNorm, Q/K/V, attention, MLP, "
-                         "out-projection, residual)")
+                         "out-projection, residual); single: the single-stream block (fused "
+                         "projection, attention, output projection over [attention | MLP])")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
@@ -935,6 +936,20 @@ def run_streams(args):
 # the whole double-stream block on the executed rows (--path block)
 # ---------------------------------------------------------------------------------------------
 BLOCK_METRIC = "double-block frames/s @1024², 25% active (executed rows only; LN+QKV+attn+MLP+out)"
+SINGLE_METRIC = "single-block frames/s @1024², 25% active (executed rows only; LN+QKV/MLP+attn+out)"
+
+
+def single_weights(w, H: int, device, seed: int) -> dict:
+    """Random-init weights of one single-stream block, bf16 matrices."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    C = w.n_heads * HEAD_DIM
+    r = lambda *shape, sd=1.0: torch.randn(*shape, generator=g, device=device) * sd
+    return {"shift": r(C, sd=0.1), "scale": r(C, sd=0.1), "gate": 1.0 + r(C, sd=0.2),
+            "w_qkv_mlp": r(3 * C + H, C, sd=C ** -0.5).bfloat16(), "b_qkv_mlp": r(3 * C + H, sd=0.05),
+            "norm_q": 1.0 + r(HEAD_DIM, sd=0.1), "norm_k": 1.0 + r(HEAD_DIM, sd=0.1),
+            "w_out": r(C, C + H, sd=(C + H) ** -0.5).bfloat16(), "b_out": r(C, sd=0.05)}
 
 
 def block_weights(w, H: int, device, seed: int) -> dict:
@@ -1038,7 +1053,8 @@ def run_block(args):
     pk = peaks()
     N, T, C = w.n_tokens, w.n_text, w.n_heads * HEAD_DIM
     H = 3 * C
-    wts = block_weights(w, H, device, args.seed + 17 * rank)
+    single = args.path == "single"
+    wts = (single_weights if single else block_weights)(w, H, device, args.seed + 17 * rank)
     n_sets = 2
     sets = []
     for sidx in range(n_sets):
@@ -1050,8 +1066,12 @@ def run_block(args):
                                        device=device)})
 
     def run(st):
-        fxr.double_block_forward(cfg, wts["txt"], wts["img"], H, st["x_in"], st["x_out"], st["mask"],
-                                 st["valid"], st["pos"], st["cache_k"], st["cache_v"], st["ws"])
+        if single:
+            fxr.single_block_forward(cfg, wts, H, st["x_in"], st["x_out"], st["mask"], st["valid"],
+                                     st["pos"], st["cache_k"], st["cache_v"], st["ws"])
+        else:
+            fxr.double_block_forward(cfg, wts["txt"], wts["img"], H, st["x_in"], st["x_out"], st["mask"],
+                                     st["valid"], st["pos"], st["cache_k"], st["cache_v"], st["ws"])
 
     for i in range(max(args.warmup, 3)):
         run(sets[i % n_sets])
@@ -1096,6 +1116,15 @@ def run_block(args):
     ms = t_ms / args.steps
     M_avg = statistics.mean(st["M"] for st in sets)
     fl = block_flops(w, M_avg, H)
+    if single:
+        out = single_block_report(args, w, cfg, wts, sets, run, H, ms, fl, M_avg, clk, pk, world)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        if world > 1:
+            graphs.clear()
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     # ---- the block's kernels one at a time (image rows of set 0; graphs of 20 launches) ----
     st = sets[0]
@@ -1198,6 +1227,53 @@ def run_block(args):
         dist.destroy_process_group()
 
 
+def single_block_report(args, w, cfg, wts, sets, run, H, ms, fl, M_avg, clk, pk, world) -> dict:
+    """JSON line of the single-stream block: the fused projection GEMM as the roofline kernel."""
+    import torch
+    import fxr
+    device = sets[0]["x_in"].device
+    N, C = w.n_tokens, w.n_heads * HEAD_DIM
+    st = sets[0]
+    idx = torch.empty(N, dtype=torch.int32, device=device)
+    cnt = torch.empty(1, dtype=torch.int32, device=device)
+    fxr.mask_compact(st["mask"], None, idx, cnt)
+    M = int(cnt.item())
+    xn = torch.randn(N, C, device=device).bfloat16()
+    qkv = [torch.empty(N, C, device=device, dtype=torch.bfloat16) for _ in range(3)]
+    hbuf = torch.empty(N, H, device=device, dtype=torch.bfloat16)
+    attn = torch.randn(N, C, device=device).bfloat16()
+    yout = torch.empty(N, C, device=device, dtype=torch.bfloat16)
+    scr = fxr.rows_gemm_scratch(device)
+    w_out = wts["w_out"]
+    kern = {
+        "fused_proj_gemm": _graph_us(lambda: fxr.rows_gemm([(xn, wts["w_qkv_mlp"], False)],
+                                                           [(t, C, True, 0) for t in qkv] +
+                                                           [(hbuf, H, False, fxr.FXR_ACT_GELU_TANH)],
+                                                           idx, cnt, N, bias0=wts["b_qkv_mlp"], scratch=scr)),
+        "out_gemm": _graph_us(lambda: fxr.rows_gemm([(attn, w_out[:, :C], True), (hbuf, w_out[:, C:], False)],
+                                                    [(yout, C, True, 0)], idx, cnt, N, bias0=wts["b_out"],
+                                                    residual=st["x_in"], gate=wts["gate"], scratch=scr)),
+    }
+    proj_fl = 2.0 * M * C * (3 * C + H)
+    achieved = proj_fl / (kern["fused_proj_gemm"] * 1e-6) / 1e12
+    roof = {"bound": "tensor", "kernel": "fxr::gemm::rows_gemm_kernel (fused Q/K/V + MLP-in projection)",
+            "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": round(achieved / pk["bf16_tflops"], 4), "peak_kind": f"{pk['source']} burst bf16 (cuBLAS)",
+            "traffic": None, "algorithmic_flop_per_launch": proj_fl}
+    return {
+        "metric": SINGLE_METRIC, "value": round(1e3 / ms * world, 2), "unit": "frames/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "us_per_frame": round(ms * 1e3, 2), "block_tflops": round(fl / (ms * 1e-3) / 1e12, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype, "impl": "ours",
+        "data": "synthetic: N(0,1) hidden states and caches, random-init block weights (seeded)",
+        "config": {"workload": w.name + "_single_block", "n_tokens": N, "active": w.active, "M_avg": M_avg,
+                   "heads": w.n_heads, "hidden": C, "mlp_hidden": H, "graph": True},
+        "roofline": roof, "kernels_isolated_us": {k: round(v, 2) for k, v in kern.items()},
+        "gpu_launches": 8 * args.steps, "clocks": clk,
+        "e2e": None, "note": "e2e and the CPU arm are reported by --path block",
+    }
+
+
 def cpu_block_sample(w, H: int, seed: int, rows: int = 256) -> dict:
     """The reference block's fp32 math on the host cores as the reference runs it, densely on every
     token (flux2_double_block_plugin.cpp:330-460): LayerNorm + modulation and Q/K/V of all N
@@ -1277,7 +1353,7 @@ def _heads_split(n_heads, world):
 
 def main():
     args = parse()
-    if args.path == "block":
+    if args.path in ("block", "single"):
         (run_block_reference if args.impl == "reference" else run_block)(args)
     elif args.impl == "reference":
         run_reference(args)

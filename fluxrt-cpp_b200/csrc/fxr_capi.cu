@@ -858,6 +858,8 @@ int32_t fxr_rows_gemm(const fxr_rows_gemm_desc* d, const int32_t* idx, const int
         if (o.ld < o.k || o.ld % 8) return fail(FXR_ERR_INVALID, "operand %d: ld must be >= k and a multiple of 8", q);
         if (!o.rows || !o.w || !aligned16(o.rows) || !aligned16(o.w))
             return fail(FXR_ERR_INVALID, "operand %d: null or unaligned rows / w", q);
+        if (o.ld_w != 0 && (o.ld_w < o.k || o.ld_w % 8))
+            return fail(FXR_ERR_INVALID, "operand %d: ld_w must be 0 or >= k and a multiple of 8", q);
     }
     if (!aligned16(d->bias0) || !aligned16(d->bias1) || !aligned16(d->gate))
         return fail(FXR_ERR_INVALID, "bias0 / bias1 / gate must be 16-byte aligned");
@@ -887,9 +889,10 @@ int32_t fxr_rows_gemm(const fxr_rows_gemm_desc* d, const int32_t* idx, const int
     }
     int32_t st;
     CUtensorMap tw0, tw1;
-    if ((st = make_tmap(&tw0, d->a[0].w, d->dtype, d->a[0].k, n_out, d->a[0].k, G::kBN)) != FXR_OK) return st;
+    auto ldw = [](const fxr_rows_operand& o) { return o.ld_w ? o.ld_w : (int64_t)o.k; };
+    if ((st = make_tmap(&tw0, d->a[0].w, d->dtype, d->a[0].k, n_out, ldw(d->a[0]), G::kBN)) != FXR_OK) return st;
     if (d->n_operands == 2) {
-        if ((st = make_tmap(&tw1, d->a[1].w, d->dtype, d->a[1].k, n_out, d->a[1].k, G::kBN)) != FXR_OK) return st;
+        if ((st = make_tmap(&tw1, d->a[1].w, d->dtype, d->a[1].k, n_out, ldw(d->a[1]), G::kBN)) != FXR_OK) return st;
     } else {
         tw1 = tw0;
     }
@@ -973,7 +976,7 @@ int32_t fxr_qkv_project(const fxr_frame_desc* desc, const void* hidden, int64_t 
     g.row0 = 0;
     g.row_end = -1;
     g.n_operands = 1;
-    g.a[0] = fxr_rows_operand{hidden, ld_hidden, k_dim, 1, w_qkv};
+    g.a[0] = fxr_rows_operand{hidden, ld_hidden, k_dim, 1, w_qkv, 0};
     g.n_outputs = 3;
     void* parts[3] = {q, k, v};
     for (int p = 0; p < 3; ++p) g.y[p] = fxr_rows_output{parts[p], desc->ld_qkv, (int32_t)C, 1, FXR_ACT_NONE, 0};
@@ -1094,7 +1097,7 @@ int32_t fxr_double_block_forward(const fxr_frame_desc* desc, const fxr_double_bl
         g.row0 = r0[k];
         g.row_end = r1[k];
         g.n_operands = 1;
-        g.a[0] = fxr_rows_operand{b.xn, C, C, 0, w.w_qkv};
+        g.a[0] = fxr_rows_operand{b.xn, C, C, 0, w.w_qkv, 0};
         g.n_outputs = 3;
         g.y[0] = fxr_rows_output{b.q, C, C, 1, FXR_ACT_NONE, 0};
         g.y[1] = fxr_rows_output{b.k, C, C, 1, FXR_ACT_NONE, 0};
@@ -1136,7 +1139,7 @@ int32_t fxr_double_block_forward(const fxr_frame_desc* desc, const fxr_double_bl
         g.row0 = r0[k];
         g.row_end = r1[k];
         g.n_operands = 1;
-        g.a[0] = fxr_rows_operand{b.xn, C, C, 0, w.w_mlp0};
+        g.a[0] = fxr_rows_operand{b.xn, C, C, 0, w.w_mlp0, 0};
         g.n_outputs = 1;
         g.y[0] = fxr_rows_output{b.h, H, H, 0, FXR_ACT_GELU_TANH, 0};
         g.bias0 = w.b_mlp0;
@@ -1150,8 +1153,8 @@ int32_t fxr_double_block_forward(const fxr_frame_desc* desc, const fxr_double_bl
         g.row0 = r0[k];
         g.row_end = r1[k];
         g.n_operands = 2;
-        g.a[0] = fxr_rows_operand{b.attn, C, C, 1, w.w_out};
-        g.a[1] = fxr_rows_operand{b.h, H, H, 0, w.w_mlp2};
+        g.a[0] = fxr_rows_operand{b.attn, C, C, 1, w.w_out, 0};
+        g.a[1] = fxr_rows_operand{b.h, H, H, 0, w.w_mlp2, 0};
         g.n_outputs = 1;
         g.y[0] = fxr_rows_output{x_out, C, C, 1, FXR_ACT_NONE, 0};
         g.bias0 = w.b_out;
@@ -1162,6 +1165,105 @@ int32_t fxr_double_block_forward(const fxr_frame_desc* desc, const fxr_double_bl
         if ((st = fxr_rows_gemm(&g, idx, count, gemm, gemm_bytes, stream)) != FXR_OK) return st;
     }
     // 9. validity of the cache rows this frame updated
+    if (valid) return fxr_mark_updated(mask, valid, T, N, stream);
+    return FXR_OK;
+}
+
+// ---- the single-stream block on the executed rows ----------------------------------------------
+size_t fxr_single_block_workspace_size(const fxr_frame_desc* desc, int32_t mlp_hidden) {
+    return fxr_double_block_workspace_size(desc, mlp_hidden);   // the same buffers
+}
+
+int32_t fxr_single_block_forward(const fxr_frame_desc* desc, const fxr_single_block* blk, const void* x_in,
+                                 void* x_out, int32_t* mask, uint8_t* valid, const int32_t* pos,
+                                 void* cache_k, void* cache_v, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+    int32_t st = check_desc(desc, true);
+    if (st != FXR_OK) return st;
+    if (!blk) return fail(FXR_ERR_INVALID, "null block");
+    const int32_t N = desc->n_tokens, T = desc->n_text, H = blk->mlp_hidden;
+    const int32_t C = desc->n_heads * desc->head_dim;
+    if (C % fxr::gemm::kBN || H <= 0 || H % fxr::gemm::kBN)
+        return fail(FXR_ERR_UNSUPPORTED, "n_heads * head_dim (%d) and mlp_hidden (%d) must be multiples of %d", C, H,
+                    fxr::gemm::kBN);
+    if (C > fxr::kLnMaxChunks * 256) return fail(FXR_ERR_UNSUPPORTED, "hidden size %d above %d", C, fxr::kLnMaxChunks * 256);
+    if (!(blk->ln_eps >= 0.f)) return fail(FXR_ERR_INVALID, "ln_eps must be >= 0");
+    if (!blk->w_qkv_mlp || !blk->w_out || !blk->norm_q || !blk->norm_k) return fail(FXR_ERR_INVALID, "null weight");
+    const void* p16[] = {blk->w_qkv_mlp, blk->w_out, blk->shift, blk->scale, blk->gate, blk->b_qkv_mlp, blk->b_out};
+    for (const void* p : p16)
+        if (!aligned16(p)) return fail(FXR_ERR_INVALID, "weights must be 16-byte aligned");
+    if (N == 0) return FXR_OK;
+    if (!x_in || !x_out || !mask || !cache_k || !cache_v || !workspace || (desc->rope_n_axes > 0 && !pos))
+        return fail(FXR_ERR_INVALID, "null pointer argument");
+    if (!aligned16(x_in) || !aligned16(x_out) || !aligned16(cache_k) || !aligned16(cache_v) || !aligned16(workspace))
+        return fail(FXR_ERR_INVALID, "x_in / x_out / caches / workspace must be 16-byte aligned");
+    const BlockViews b = carve_block(desc, H, workspace);
+    if (workspace_bytes < b.total)
+        return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, b.total);
+    fxr_frame_desc fd = *desc;
+    fd.ld_qkv = C;
+    fd.ld_out = C;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int32_t dt = desc->dtype;
+    int32_t* idx = b.frame.idx;
+    int32_t* count = b.frame.count;
+    const size_t gemm_bytes = fxr_rows_gemm_scratch_size();
+    {
+        fxr::CompactArgs ca{};
+        ca.s[0] = fxr::CompactStream{mask, valid, idx, count};
+        if ((st = launch_compact_streams(ca, 1, N, b.split, stream, b.gemm, fxr::gemm::kSyncBytes, T)) != FXR_OK)
+            return st;
+    }
+    if ((st = fxr_ln_modulate_rows(dt, x_in, C, C, idx, count, 0, -1, N, blk->scale, blk->shift, blk->ln_eps,
+                                   b.xn, C, stream)) != FXR_OK)
+        return st;
+    {   // the fused projection: Q, K, V scattered to their token rows, the MLP rows compact + GELU
+        fxr_rows_gemm_desc g{};
+        g.dtype = dt;
+        g.n_tokens = N;
+        g.row0 = 0;
+        g.row_end = -1;
+        g.n_operands = 1;
+        g.a[0] = fxr_rows_operand{b.xn, C, C, 0, blk->w_qkv_mlp, 0};
+        g.n_outputs = 4;
+        g.y[0] = fxr_rows_output{b.q, C, C, 1, FXR_ACT_NONE, 0};
+        g.y[1] = fxr_rows_output{b.k, C, C, 1, FXR_ACT_NONE, 0};
+        g.y[2] = fxr_rows_output{b.v, C, C, 1, FXR_ACT_NONE, 0};
+        g.y[3] = fxr_rows_output{b.h, H, H, 0, FXR_ACT_GELU_TANH, 0};
+        g.bias0 = blk->b_qkv_mlp;
+        if ((st = fxr_rows_gemm(&g, idx, count, b.gemm, gemm_bytes, stream)) != FXR_OK) return st;
+    }
+    const fxr::GatherStream gs{b.q, b.k, b.v, mask, idx, count, b.frame.qc, cache_k, cache_v, b.frame.save};
+    st = dt == FXR_BF16 ? launch_gather_streams<__nv_bfloat16>(&fd, 1, &gs, pos, blk->norm_q, blk->norm_k, b.frame.ld_qc, s)
+                        : launch_gather_streams<__half>(&fd, 1, &gs, pos, blk->norm_q, blk->norm_k, b.frame.ld_qc, s);
+    if (st != FXR_OK) return st;
+    OutSet os;
+    os.out = b.attn;
+    os.split = b.split;
+    st = dt == FXR_BF16 ? launch_attention<__nv_bfloat16>(&fd, b.frame.qc, b.frame.ld_qc, count, cache_k, cache_v,
+                                                          idx, os, s)
+                        : launch_attention<__half>(&fd, b.frame.qc, b.frame.ld_qc, count, cache_k, cache_v, idx,
+                                                   os, s);
+    if (st != FXR_OK) return st;
+    if ((st = fxr_restore_rows(&fd, mask, idx, count, b.frame.save, cache_k, cache_v, stream)) != FXR_OK) return st;
+    {   // x_out = x_in + gate * ([attention | MLP] . W_out^T + b_out): W_out's two column blocks
+        fxr_rows_gemm_desc g{};
+        g.dtype = dt;
+        g.n_tokens = N;
+        g.row0 = 0;
+        g.row_end = -1;
+        g.n_operands = 2;
+        g.a[0] = fxr_rows_operand{b.attn, C, C, 1, blk->w_out, (int64_t)C + H};
+        g.a[1] = fxr_rows_operand{b.h, H, H, 0, static_cast<const char*>(blk->w_out) + (size_t)C * dtype_bytes(dt),
+                                  (int64_t)C + H};
+        g.n_outputs = 1;
+        g.y[0] = fxr_rows_output{x_out, C, C, 1, FXR_ACT_NONE, 0};
+        g.bias0 = blk->b_out;
+        g.residual = x_in;
+        g.ld_residual = C;
+        g.gate = blk->gate;
+        if ((st = fxr_rows_gemm(&g, idx, count, b.gemm, gemm_bytes, stream)) != FXR_OK) return st;
+    }
     if (valid) return fxr_mark_updated(mask, valid, T, N, stream);
     return FXR_OK;
 }

@@ -40,6 +40,7 @@ EXPORTED = [
     "fxr_batch_workspace_size", "fxr_frame_forward_batch", "fxr_qkv_project",
     "fxr_ln_modulate_rows", "fxr_rows_gemm_scratch_size", "fxr_rows_gemm",
     "fxr_double_block_workspace_size", "fxr_double_block_forward",
+    "fxr_single_block_workspace_size", "fxr_single_block_forward",
 ]
 
 FXR_ACT_NONE, FXR_ACT_GELU_TANH = 0, 1
@@ -61,7 +62,7 @@ class FxrError(RuntimeError):
 class RowsOperand(ctypes.Structure):
     """Mirror of fxr_rows_operand (include/fxr.h)."""
     _fields_ = [("rows", ctypes.c_void_p), ("ld", ctypes.c_int64), ("k", ctypes.c_int32),
-                ("gathered", ctypes.c_int32), ("w", ctypes.c_void_p)]
+                ("gathered", ctypes.c_int32), ("w", ctypes.c_void_p), ("ld_w", ctypes.c_int64)]
 
 
 class RowsOutput(ctypes.Structure):
@@ -90,6 +91,13 @@ class DoubleBlock(ctypes.Structure):
     """Mirror of fxr_double_block (include/fxr.h)."""
     _fields_ = [("txt", BlockStream), ("img", BlockStream), ("mlp_hidden", ctypes.c_int32),
                 ("ln_eps", ctypes.c_float)]
+
+
+class SingleBlock(ctypes.Structure):
+    """Mirror of fxr_single_block (include/fxr.h)."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ("shift", "scale", "gate", "w_qkv_mlp", "b_qkv_mlp",
+                                                "norm_q", "norm_k", "w_out", "b_out")] + \
+        [("mlp_hidden", ctypes.c_int32), ("ln_eps", ctypes.c_float)]
 
 
 class PluginField(ctypes.Structure):
@@ -188,6 +196,10 @@ def load(path: str | None = None) -> ctypes.CDLL:
     L.fxr_rows_gemm_scratch_size.argtypes = []
     L.fxr_rows_gemm_scratch_size.restype = ctypes.c_size_t
     L.fxr_rows_gemm.argtypes = [ctypes.POINTER(RowsGemmDesc), _vp, _vp, _vp, ctypes.c_size_t, _vp]
+    L.fxr_single_block_workspace_size.argtypes = [ctypes.POINTER(FrameDesc), _i32]
+    L.fxr_single_block_workspace_size.restype = ctypes.c_size_t
+    L.fxr_single_block_forward.argtypes = [ctypes.POINTER(FrameDesc), ctypes.POINTER(SingleBlock)] + \
+        [_vp] * 8 + [ctypes.c_size_t, _vp]
     L.fxr_double_block_workspace_size.argtypes = [ctypes.POINTER(FrameDesc), _i32]
     L.fxr_double_block_workspace_size.restype = ctypes.c_size_t
     L.fxr_double_block_forward.argtypes = [ctypes.POINTER(FrameDesc), ctypes.POINTER(DoubleBlock)] + \
@@ -692,8 +704,9 @@ def rows_gemm(operands, outputs, idx, count, n_tokens, bias0=None, bias1=None, r
     d.n_tokens = n_tokens
     d.row0, d.row_end = row0, row_end
     d.n_operands, d.n_outputs = len(operands), len(outputs)
-    for i, (rows, w, gathered) in enumerate(operands):
-        d.a[i] = RowsOperand(_ptr(rows), rows.stride(0), w.shape[1], 1 if gathered else 0, _ptr(w))
+    for i, (rows, w, gathered) in enumerate(operands):   # w may be a column block of a wider W
+        d.a[i] = RowsOperand(_ptr(rows), rows.stride(0), w.shape[1], 1 if gathered else 0, _ptr(w),
+                             w.stride(0))
     for i, (rows, cols, scattered, act) in enumerate(outputs):
         d.y[i] = RowsOutput(_ptr(rows), rows.stride(0), cols, 1 if scattered else 0, act, 0)
     d.bias0, d.bias1, d.gate = _ptr(bias0), _ptr(bias1), _ptr(gate)
@@ -727,6 +740,26 @@ def double_block_forward(cfg: FrameConfig, txt: dict, img: dict, mlp_hidden: int
     d = cfg.desc()
     blk = DoubleBlock(block_stream(**txt), block_stream(**img), mlp_hidden, ln_eps)
     _check(load().fxr_double_block_forward(ctypes.byref(d), ctypes.byref(blk), _ptr(x_in), _ptr(x_out),
+                                           _ptr(mask), _ptr(valid), _ptr(pos), _ptr(cache_k),
+                                           _ptr(cache_v), _ptr(workspace), workspace.numel(),
+                                           _stream(stream)))
+
+
+def single_block_workspace_size(cfg: FrameConfig, mlp_hidden: int) -> int:
+    d = cfg.desc()
+    return int(load().fxr_single_block_workspace_size(ctypes.byref(d), mlp_hidden))
+
+
+def single_block_forward(cfg: FrameConfig, wts: dict, mlp_hidden: int, x_in, x_out, mask, valid, pos,
+                         cache_k, cache_v, workspace, ln_eps=1e-6, stream=None):
+    """One single-stream block on the executed rows (fxr_single_block_forward). wts: dict of the
+    fxr_single_block weight fields (device tensors)."""
+    d = cfg.desc()
+    blk = SingleBlock()
+    for n in ("shift", "scale", "gate", "w_qkv_mlp", "b_qkv_mlp", "norm_q", "norm_k", "w_out", "b_out"):
+        setattr(blk, n, _ptr(wts.get(n)))
+    blk.mlp_hidden, blk.ln_eps = mlp_hidden, ln_eps
+    _check(load().fxr_single_block_forward(ctypes.byref(d), ctypes.byref(blk), _ptr(x_in), _ptr(x_out),
                                            _ptr(mask), _ptr(valid), _ptr(pos), _ptr(cache_k),
                                            _ptr(cache_v), _ptr(workspace), workspace.numel(),
                                            _stream(stream)))

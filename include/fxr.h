@@ -243,7 +243,8 @@ typedef struct fxr_rows_operand {
     int64_t ld;              /* elements */
     int32_t k;               /* columns of this operand (multiple of 64) */
     int32_t gathered;        /* 1: row idx[m]; 0: row m */
-    const void* w;           /* [n_out, k] row-major */
+    const void* w;           /* [n_out, k] with row stride ld_w (a column block of a wider W) */
+    int64_t ld_w;            /* elements between W rows; 0: k */
 } fxr_rows_operand;
 
 typedef struct fxr_rows_output {
@@ -314,6 +315,38 @@ typedef struct fxr_double_block {
 
 size_t fxr_double_block_workspace_size(const fxr_frame_desc* desc, int32_t mlp_hidden);
 int32_t fxr_double_block_forward(const fxr_frame_desc* desc, const fxr_double_block* blk,
+                                 const void* x_in, void* x_out, int32_t* mask, uint8_t* valid,
+                                 const int32_t* pos, void* cache_k, void* cache_v,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- the single-stream block on the executed rows ------------------------------------------------
+ * A FLUX.2 single-stream block: one set of weights over the joint text + image sequence, the
+ * attention and the MLP fed by one fused projection and merged by one output projection
+ * (to_qkv_mlp_proj and to_out, exported by tools/export_block_weights.py:79-113; the reference plans
+ * the plugin, results.md:95, and has no kernel code for it):
+ *   xn = LN_mod(x_in);  [q | k | v | h] = xn . W_qkv_mlp^T + b;  h = GELU(h)
+ *   x_out = x_in + gate * ([attn(q, k, v) | h] . W_out^T + b_out)
+ * on the executed rows only (8 launches: compaction, LayerNorm + modulation, the fused projection
+ * with Q/K/V scattered and the MLP rows compact, gather + QK-RMSNorm + RoPE, attention, restore, the
+ * two-operand output projection with the gated residual, cache validity). The MLP activation is
+ * the tanh GELU of the reference's double block (flux2_kernels.cu:14-21). Shapes and the output
+ * cache as for fxr_double_block_forward. */
+typedef struct fxr_single_block {
+    const float* shift;      /* [C] modulation or NULL */
+    const float* scale;      /* [C] or NULL */
+    const float* gate;       /* [C] or NULL (1) */
+    const void* w_qkv_mlp;   /* [3C + H, C]: to_q, to_k, to_v rows, then the MLP-in rows */
+    const float* b_qkv_mlp;  /* [3C + H] or NULL */
+    const float* norm_q;     /* [head_dim] */
+    const float* norm_k;
+    const void* w_out;       /* [C, C + H]: columns [0, C) take the attention rows, [C, C + H) the MLP */
+    const float* b_out;      /* [C] or NULL */
+    int32_t mlp_hidden;      /* H: multiple of 256 */
+    float ln_eps;
+} fxr_single_block;
+
+size_t fxr_single_block_workspace_size(const fxr_frame_desc* desc, int32_t mlp_hidden);
+int32_t fxr_single_block_forward(const fxr_frame_desc* desc, const fxr_single_block* blk,
                                  const void* x_in, void* x_out, int32_t* mask, uint8_t* valid,
                                  const int32_t* pos, void* cache_k, void* cache_v,
                                  void* workspace, size_t workspace_bytes, void* stream);

@@ -45,6 +45,12 @@ def test_rows_gemm_argument_checks():
     d.a[0] = fxr.RowsOperand(24, 256, 256, 1, 16)            # unaligned rows
     assert call(d) == fxr.FXR_ERR_INVALID
     d = _desc()
+    d.a[0] = fxr.RowsOperand(16, 256, 256, 1, 16, 128)       # W row stride below k
+    assert call(d) == fxr.FXR_ERR_INVALID
+    d = _desc()
+    d.a[0] = fxr.RowsOperand(16, 256, 256, 1, 16, 260)       # W row stride not a multiple of 8
+    assert call(d) == fxr.FXR_ERR_INVALID
+    d = _desc()
     d.y[0] = fxr.RowsOutput(16, 256, 256, 1, 7, 0)           # unknown activation
     assert call(d) == fxr.FXR_ERR_INVALID
     d = _desc(n_outputs=2, residual=16, ld_residual=512)     # residual with two parts

@@ -1,7 +1,9 @@
 """The double-stream block on the executed rows (fxr_double_block_forward) against a CPU restatement
 of the reference block (flux2_double_block_plugin.cpp:330-460: LayerNorm + modulation, Q/K/V, QK
 RMSNorm, attention, out-projection, GELU MLP, residual) with joint text + image attention over the
-spatial K/V cache, fp32 arithmetic rounded to bf16 where the kernels store. Attention, RMSNorm and
+spatial K/V cache, fp32 arithmetic rounded to bf16 where the kernels store; and the single-stream
+block (fxr_single_block_forward: one fused to_qkv_mlp_proj, one to_out over [attention | MLP],
+tools/export_block_weights.py:79-113) against the same kind of restatement. Attention, RMSNorm and
 RoPE come from the oracle (oracle/fxr_oracle.c)."""
 import ctypes
 
@@ -177,3 +179,83 @@ def test_double_block_matches_reference(cuda, p, seed):
         ec = _ulp_err(gc[upd], ref[key][upd])
         print(f"{key} updated rows: max {ec.max():.1f} steps, >1 step {np.mean(ec > 1):.2e}, mean {ec.mean():.3f}")
         assert ec.max() <= 2 and np.mean(ec > 1) < 1e-4, (key, ec.max(), ec.mean())
+
+
+def _reference_single_block(w, fr, x_in, valid, wt, H):
+    """fp32 restatement of the single-stream block, bf16 at the kernels' storage points."""
+    import oracle
+    bf = lambda a: W.round_storage(a, "bf16")
+    N, T, C, D = w.n_tokens, w.n_text, w.n_heads * w.head_dim, w.head_dim
+    mask = fr["mask"].copy()
+    mask[valid == 0] = 2
+    mask[:T][mask[:T] == 0] = 2
+    idx = np.nonzero(mask)[0]
+    xn = bf(_ln_mod(x_in[idx], wt["scale"], wt["shift"]))
+    proj = xn @ wt["w_qkv_mlp"].T + wt["b_qkv_mlp"]
+    q, k, v = bf(proj[:, :C]), bf(proj[:, C:2 * C]), bf(proj[:, 2 * C:3 * C])
+    h = bf(_gelu(proj[:, 3 * C:]))
+    rope = lambda x, t: np.concatenate([oracle.rope_row(x[j * D:(j + 1) * D], fr["pos"][t], w.rope_axes,
+                                                        w.rope_theta) for j in range(w.n_heads)])
+    ck, cv = fr["cache_k"].copy(), fr["cache_v"].copy()
+    k_att, v_att = ck.copy(), cv.copy()
+    qn = np.zeros_like(q)
+    for r, t in enumerate(idx):
+        qn[r] = bf(rope(oracle.rms_norm(q[r].reshape(-1, D), wt["norm_q"]).reshape(-1), t))
+        k_att[t] = bf(rope(oracle.rms_norm(k[r].reshape(-1, D), wt["norm_k"]).reshape(-1), t))
+        v_att[t] = v[r]
+    o = bf(oracle.attention(qn, k_att, v_att, w.n_heads, D))
+    x_out = bf(x_in[idx] + wt["gate"] * (np.concatenate([o, h], axis=1) @ wt["w_out"].T + wt["b_out"]))
+    upd = mask == 2
+    ck[upd], cv[upd] = k_att[upd], v_att[upd]
+    return {"idx": idx, "x_out": x_out, "cache_k": ck, "cache_v": cv, "mask": mask}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("p,seed", [(0.3, 13), (0.02, 14)])
+def test_single_block_matches_reference(cuda, p, seed):
+    import torch
+    w = W.Workload("sblk_512px_h6", 32, 32, 256, n_heads=6)
+    H = 3 * w.n_heads * w.head_dim
+    N, T, C, D = w.n_tokens, w.n_text, w.n_heads * w.head_dim, w.head_dim
+    rng = np.random.default_rng(seed)
+    fr = W.make_frame(w, seed=seed, p=p)
+    fr["mask"][T + 3] = 1
+    valid = (rng.random(N) < 0.9).astype(np.uint8)
+    valid[:T] = 1
+    x_in = W.round_storage(rng.normal(0, 1, size=(N, C)).astype(np.float32), "bf16")
+    x_prev = W.round_storage(rng.normal(0, 1, size=(N, C)).astype(np.float32), "bf16")
+    g = lambda *shape, sd=1.0: W.round_storage(rng.normal(0, sd, size=shape).astype(np.float32), "bf16")
+    f = lambda *shape, mu=0.0, sd=1.0: rng.normal(mu, sd, size=shape).astype(np.float32)
+    wt = {"shift": f(C, sd=0.1), "scale": f(C, sd=0.1), "gate": f(C, mu=1.0, sd=0.2),
+          "w_qkv_mlp": g(3 * C + H, C, sd=C ** -0.5), "b_qkv_mlp": f(3 * C + H, sd=0.05),
+          "norm_q": f(D, mu=1.0, sd=0.1), "norm_k": f(D, mu=1.0, sd=0.1),
+          "w_out": g(C, C + H, sd=(C + H) ** -0.5), "b_out": f(C, sd=0.05)}
+    ref = _reference_single_block(w, fr, x_in, valid, wt, H)
+
+    dev = lambda a, dt=torch.bfloat16: torch.from_numpy(np.ascontiguousarray(a)).to("cuda").to(dt)
+    tw = {k: dev(v, torch.bfloat16 if k.startswith("w_") else torch.float32) for k, v in wt.items()}
+    cfg = fxr.FrameConfig(n_tokens=N, n_text=T, n_heads=w.n_heads, dtype="bf16", rope_axes=w.rope_axes,
+                          rope_theta=w.rope_theta)
+    xi, xo = dev(x_in), dev(x_prev)
+    mask = torch.from_numpy(fr["mask"].copy()).cuda()
+    vd = torch.from_numpy(valid.copy()).cuda()
+    pos = torch.from_numpy(fr["pos"]).cuda()
+    ck, cv = dev(fr["cache_k"]), dev(fr["cache_v"])
+    ws = torch.empty(fxr.single_block_workspace_size(cfg, H), dtype=torch.uint8, device="cuda")
+    fxr.single_block_forward(cfg, tw, H, xi, xo, mask, vd, pos, ck, cv, ws)
+    torch.cuda.synchronize()
+    assert fxr.check_device_error() == 0
+    idx = ref["idx"]
+    assert np.array_equal(mask.cpu().numpy(), ref["mask"])
+    got = xo.float().cpu().numpy()
+    e = _ulp_err(got[idx], ref["x_out"])
+    print(f"single block x_out rows {idx.size}: max {e.max():.1f} steps, mean {e.mean():.3f}")
+    assert e.max() <= 2 and e.mean() < 0.05, (e.max(), e.mean())
+    skipped = np.setdiff1d(np.arange(N), idx)
+    assert np.array_equal(got[skipped], x_prev[skipped])
+    for key in ("cache_k", "cache_v"):
+        gc = (ck if key == "cache_k" else cv).float().cpu().numpy()
+        upd = ref["mask"] == 2
+        assert np.array_equal(gc[~upd], fr[key][~upd]), key
+        ec = _ulp_err(gc[upd], ref[key][upd])
+        assert ec.max() <= 2 and np.mean(ec > 1) < 1e-4, (key, ec.max())
