@@ -248,16 +248,25 @@ def run_ours(args):
     if fxr.check_device_error() != 0:
         raise RuntimeError("device error during warm-up")
 
+    # Graphs: one per input set, and one holding the n_sets frames back to back as a stream of
+    # frames is enqueued (programmatic dependent launch then also overlaps one frame's first kernel
+    # with the previous frame's last); K frames = K // n_sets replays of the latter + the rest.
     graphs = []
     use_graph = not args.no_graph
+    run_graph = None
     if use_graph:
         for s in range(n_sets):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 run_frame(cfg, frames[s], wss[s])
             graphs.append(g)
+        run_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(run_graph):
+            for s in range(n_sets):
+                run_frame(cfg, frames[s], wss[s])
         for s in range(n_sets):
             graphs[s].replay()
+        run_graph.replay()
         torch.cuda.synchronize()
 
     def step(i):
@@ -266,24 +275,31 @@ def run_ours(args):
         else:
             run_frame(cfg, frames[i % n_sets], wss[i % n_sets])
 
+    def steps(k):
+        """k frames in order, n_sets per graph replay where possible."""
+        i = 0
+        if use_graph:
+            while k - i >= n_sets:
+                run_graph.replay()
+                i += n_sets
+        while i < k:
+            step(i)
+            i += 1
+
     clocks = Clocks(local)
     clocks.start()
     # soak for >= 1 s so the sampler sees the loaded clock even when K is small
     t_end = time.time() + 1.0
-    i = 0
     while time.time() < t_end:
-        step(i)
-        i += 1
-        if i % 64 == 0:
-            torch.cuda.synchronize()
+        steps(64)
+        torch.cuda.synchronize()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
-        step(i)
+    steps(args.steps)
     e1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
@@ -340,7 +356,7 @@ def run_ours(args):
                    "rope_axes": list(w.rope_axes), "rope_theta": w.rope_theta,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": f"{n_sets} rotating input sets, {n_sets * 6 * w.n_tokens * w.n_heads * HEAD_DIM * 2 / 2**20:.0f} MiB > L2",
-                   "graph": use_graph},
+                   "graph": f"{n_sets} consecutive frames per CUDA graph" if use_graph else False},
         "roofline": roof,
         "kernels": {"gather": mem,
                     "in_frame_us": {k[:-3]: round(v, 2) for k, v in kern.items()},
@@ -364,6 +380,7 @@ def run_ours(args):
         for g_ in graphs:
             del g_
         graphs.clear()
+        del run_graph
         dist.barrier()
         dist.destroy_process_group()
 
@@ -1078,28 +1095,40 @@ def run_block(args):
     torch.cuda.synchronize()
     if fxr.check_device_error() != 0:
         raise RuntimeError("device error during warm-up")
+    # one graph per input set, and one holding both frames back to back (a stream of frames)
     graphs = []
     for st in sets:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             run(st)
         graphs.append(g)
+    run_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(run_graph):
+        for st in sets:
+            run(st)
+
+    def steps(k):
+        i = 0
+        while k - i >= n_sets:
+            run_graph.replay()
+            i += n_sets
+        while i < k:
+            graphs[i % n_sets].replay()
+            i += 1
     stream = torch.cuda.current_stream()
     clocks = Clocks(local)
     clocks.start()
     t_end = time.time() + 1.0
-    i = 0
     while time.time() < t_end:
-        graphs[i % n_sets].replay()
-        i += 1
+        steps(16)
+        torch.cuda.synchronize()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
-        graphs[i % n_sets].replay()
+    steps(args.steps)
     e1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
@@ -1206,7 +1235,7 @@ def run_block(args):
         "config": {"workload": w.name + "_double_block", "n_tokens": N, "n_text": T, "active": w.active,
                    "M_avg": M_avg, "heads": w.n_heads, "hidden": C, "mlp_hidden": H,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
-                   "l2": "weights 377 MB per step > L2", "graph": True},
+                   "l2": "weights 377 MB per step > L2", "graph": "2 consecutive frames per CUDA graph"},
         "roofline": roof,
         "kernels_isolated_us": {k: round(v, 2) for k, v in kern.items()},
         "dense_torch_same_gpu_us": round(dense_us, 1),
