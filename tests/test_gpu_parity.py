@@ -239,7 +239,7 @@ def test_frame_forward_deterministic_and_noop(cuda):
 
 
 def test_full_size_c2_properties(cuda):
-    """BASELINE-size frame (1024^2, 25 %, 24 heads, bf16): checks that need no full oracle run:
+    """Full-size frame (1024^2, 25 %, 24 heads, bf16): checks that need no full oracle run:
     untouched rows, cache bookkeeping, and a sampled subset of executed rows against the oracle."""
     w = W.C2
     fr = W.make_frame(w, seed=41)
