@@ -231,9 +231,11 @@ size_t split_bytes(int32_t slots) {
     return align_up((size_t)slots * kSplitCntBytes, 256) + (size_t)slots * kSplitSlotBytes;
 }
 
-SplitArea split_area(size_t base, void* ws, size_t ws_bytes) {
+// Launches with more than kSplitMaxHeads heads never split: no area, so the compaction zeroes no
+// arrival counters for them.
+SplitArea split_area(size_t base, void* ws, size_t ws_bytes, int32_t n_heads) {
     SplitArea a;
-    if (!ws || ws_bytes <= base) return a;
+    if (!ws || ws_bytes <= base || n_heads > kSplitMaxHeads) return a;
     const int32_t max_slots = kSplitSlotsPerSm * sm_count();
     int32_t slots = (int32_t)std::min<size_t>(max_slots, (ws_bytes - base) / (kSplitSlotBytes + kSplitCntBytes));
     while (slots > 0 && split_bytes(slots) > ws_bytes - base) --slots;
@@ -783,7 +785,7 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void*
     if (workspace_bytes < w.total)
         return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, w.total);
     if (!aligned16(workspace)) return fail(FXR_ERR_INVALID, "workspace must be 16-byte aligned");
-    const SplitArea split = split_area(w.total, workspace, workspace_bytes);
+    const SplitArea split = split_area(w.total, workspace, workspace_bytes, desc->n_heads);
     if ((st = launch_compact(mask, valid, desc->n_tokens, w.idx, w.count, split, stream)) != FXR_OK) return st;
     if ((st = fxr_gather_norm_rope(desc, q, k, v, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc,
                                    w.ld_qc, cache_k, cache_v, w.save, stream)) != FXR_OK)
@@ -1006,7 +1008,7 @@ static BlockViews carve_block(const fxr_frame_desc* d, int32_t hidden, void* ws)
     b.frame = carve(d, ws);
     const size_t split_sz = split_bytes(kSplitSlotsPerSm * sm_count());
     size_t off = align_up(b.frame.total + split_sz, 256);
-    if (base) b.split = split_area(b.frame.total, ws, b.frame.total + split_sz);
+    if (base) b.split = split_area(b.frame.total, ws, b.frame.total + split_sz, d->n_heads);
     const size_t N = (size_t)(d->n_tokens > 0 ? d->n_tokens : 1);
     const size_t row = (size_t)d->n_heads * d->head_dim * dtype_bytes(d->dtype);
     char** parts[5] = {&b.q, &b.k, &b.v, &b.xn, &b.attn};
@@ -1423,7 +1425,7 @@ int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g, c
     const size_t col = (size_t)g->head0 * desc->head_dim * eb;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     OutSet os;
-    os.split = split_area(need, workspace, workspace_bytes);
+    os.split = split_area(need, workspace, workspace_bytes, sd.n_heads);
     if ((st = launch_compact(mask, valid, sd.n_tokens, w.frame.idx, w.frame.count, os.split, stream)) != FXR_OK)
         return st;
     if ((st = fxr_gather_norm_rope(&sd, static_cast<const char*>(q) + col, static_cast<const char*>(k) + col,
@@ -1600,7 +1602,7 @@ int32_t fxr_frame_forward_heads_nccl(const fxr_frame_desc* desc, const fxr_head_
     sd.n_heads = g->n_heads;
     sd.ld_cache = (int64_t)g->n_heads * desc->head_dim;
     const size_t col = (size_t)g->head0 * desc->head_dim * dtype_bytes(desc->dtype);
-    const SplitArea split = split_area(w.total, workspace, workspace_bytes);
+    const SplitArea split = split_area(w.total, workspace, workspace_bytes, sd.n_heads);
     if ((st = launch_compact(mask, valid, sd.n_tokens, w.frame.idx, w.frame.count, split, stream)) != FXR_OK)
         return st;
     if (g->n_heads > 0) {

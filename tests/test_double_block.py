@@ -47,10 +47,10 @@ def _gelu(x):
 
 
 def _reference_block(w, fr, x_in, valid, streams, H):
-    """fp32 restatement, bf16 at the kernels' storage points; returns the executed token list, their
-    block outputs, the caches, the preprocessed mask and the validity flags."""
+    """fp32 restatement, rounded to the storage type where the kernels store; returns the executed
+    token list, their block outputs, the caches, the preprocessed mask and the validity flags."""
     import oracle
-    bf = lambda a: W.round_storage(a, "bf16")
+    bf = lambda a: W.round_storage(a, w.dtype)
     N, T, C, D = w.n_tokens, w.n_text, w.n_heads * w.head_dim, w.head_dim
     mask = fr["mask"].copy()
     mask[valid == 0] = 2
@@ -100,7 +100,7 @@ def _reference_block(w, fr, x_in, valid, streams, H):
 
 def _streams(w, H, rng):
     C, D = w.n_heads * w.head_dim, w.head_dim
-    g = lambda *shape, sd=1.0: W.round_storage(rng.normal(0, sd, size=shape).astype(np.float32), "bf16")
+    g = lambda *shape, sd=1.0: W.round_storage(rng.normal(0, sd, size=shape).astype(np.float32), w.dtype)
     f = lambda *shape, mu=0.0, sd=1.0: rng.normal(mu, sd, size=shape).astype(np.float32)
     out = {}
     for name in ("txt", "img"):
@@ -115,20 +115,21 @@ def _streams(w, H, rng):
     return out
 
 
-def _ulp_err(got, ref):
-    """|got - ref| in bf16 steps of max(|ref|, the RMS of ref): values near zero are judged on the
-    scale of the tensor, not on their own tiny step."""
+def _ulp_err(got, ref, dtype="bf16"):
+    """|got - ref| in storage steps (bf16 / fp16) of max(|ref|, the RMS of ref): values near zero are
+    judged on the scale of the tensor, not on their own tiny step."""
     rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)))
     mag = np.maximum(np.abs(ref), rms)
-    ulp = 2.0 ** (np.floor(np.log2(mag)) - 7)
+    ulp = 2.0 ** (np.floor(np.log2(mag)) - (7 if dtype == "bf16" else 10))
     return np.abs(got - ref) / ulp
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("p,seed", [(0.3, 3), (0.05, 4)])
-def test_double_block_matches_reference(cuda, p, seed):
+@pytest.mark.parametrize("p,seed,dtype", [(0.3, 3, "bf16"), (0.05, 4, "bf16"), (0.3, 5, "f16")])
+def test_double_block_matches_reference(cuda, p, seed, dtype):
     import torch
-    w = W.Workload("blk_512px_h6", 32, 32, 256, n_heads=6)
+    w = W.Workload("blk_512px_h6", 32, 32, 256, n_heads=6, dtype=dtype)
+    td = torch.bfloat16 if dtype == "bf16" else torch.float16
     H = 3 * w.n_heads * w.head_dim
     N, T, C = w.n_tokens, w.n_text, w.n_heads * w.head_dim
     rng = np.random.default_rng(seed)
@@ -139,15 +140,15 @@ def test_double_block_matches_reference(cuda, p, seed):
     fr["mask"][7] = 1
     valid = (rng.random(N) < 0.9).astype(np.uint8)
     valid[:T] = 1
-    x_in = W.round_storage(rng.normal(0, 1, size=(N, C)).astype(np.float32), "bf16")
-    x_prev = W.round_storage(rng.normal(0, 1, size=(N, C)).astype(np.float32), "bf16")
+    x_in = W.round_storage(rng.normal(0, 1, size=(N, C)).astype(np.float32), dtype)
+    x_prev = W.round_storage(rng.normal(0, 1, size=(N, C)).astype(np.float32), dtype)
     streams = _streams(w, H, rng)
     ref = _reference_block(w, fr, x_in, valid, streams, H)
 
-    dev = lambda a, dt=torch.bfloat16: torch.from_numpy(np.ascontiguousarray(a)).to("cuda").to(dt)
-    tw = {n: {k: dev(v, torch.bfloat16 if k.startswith("w_") else torch.float32) for k, v in s.items()}
+    dev = lambda a, dt=td: torch.from_numpy(np.ascontiguousarray(a)).to("cuda").to(dt)
+    tw = {n: {k: dev(v, td if k.startswith("w_") else torch.float32) for k, v in s.items()}
           for n, s in streams.items()}
-    cfg = fxr.FrameConfig(n_tokens=N, n_text=T, n_heads=w.n_heads, dtype="bf16", rope_axes=w.rope_axes,
+    cfg = fxr.FrameConfig(n_tokens=N, n_text=T, n_heads=w.n_heads, dtype=dtype, rope_axes=w.rope_axes,
                           rope_theta=w.rope_theta)
     xi, xo = dev(x_in), dev(x_prev)
     mask = torch.from_numpy(fr["mask"].copy()).cuda()
@@ -163,7 +164,7 @@ def test_double_block_matches_reference(cuda, p, seed):
     assert np.array_equal(mask.cpu().numpy(), ref["mask"])
     assert np.array_equal(vd.cpu().numpy(), ref["valid"])
     got = xo.float().cpu().numpy()
-    e = _ulp_err(got[idx], ref["x_out"])
+    e = _ulp_err(got[idx], ref["x_out"], dtype)
     wr, wc = np.unravel_index(int(np.argmax(e)), e.shape)
     print(f"x_out rows {idx.size}: max {e.max():.1f} steps (got {got[idx][wr, wc]:.5f} ref "
           f"{ref['x_out'][wr, wc]:.5f}), >2 steps {np.mean(e > 2):.2e}, mean {e.mean():.3f}")
@@ -176,15 +177,16 @@ def test_double_block_matches_reference(cuda, p, seed):
         gc = (ck if key == "cache_k" else cv).float().cpu().numpy()
         upd = ref["mask"] == 2
         assert np.array_equal(gc[~upd], fr[key][~upd]), key      # skipped and mask-1 rows restored
-        ec = _ulp_err(gc[upd], ref[key][upd])
+        ec = _ulp_err(gc[upd], ref[key][upd], dtype)
         print(f"{key} updated rows: max {ec.max():.1f} steps, >1 step {np.mean(ec > 1):.2e}, mean {ec.mean():.3f}")
         assert ec.max() <= 2 and np.mean(ec > 1) < 1e-4, (key, ec.max(), ec.mean())
 
 
 def _reference_single_block(w, fr, x_in, valid, wt, H):
-    """fp32 restatement of the single-stream block, bf16 at the kernels' storage points."""
+    """fp32 restatement of the single-stream block, rounded to the storage type where the kernels
+    store."""
     import oracle
-    bf = lambda a: W.round_storage(a, "bf16")
+    bf = lambda a: W.round_storage(a, w.dtype)
     N, T, C, D = w.n_tokens, w.n_text, w.n_heads * w.head_dim, w.head_dim
     mask = fr["mask"].copy()
     mask[valid == 0] = 2
@@ -211,10 +213,11 @@ def _reference_single_block(w, fr, x_in, valid, wt, H):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("p,seed", [(0.3, 13), (0.02, 14)])
-def test_single_block_matches_reference(cuda, p, seed):
+@pytest.mark.parametrize("p,seed,dtype", [(0.3, 13, "bf16"), (0.02, 14, "bf16"), (0.3, 15, "f16")])
+def test_single_block_matches_reference(cuda, p, seed, dtype):
     import torch
-    w = W.Workload("sblk_512px_h6", 32, 32, 256, n_heads=6)
+    w = W.Workload("sblk_512px_h6", 32, 32, 256, n_heads=6, dtype=dtype)
+    td = torch.bfloat16 if dtype == "bf16" else torch.float16
     H = 3 * w.n_heads * w.head_dim
     N, T, C, D = w.n_tokens, w.n_text, w.n_heads * w.head_dim, w.head_dim
     rng = np.random.default_rng(seed)
@@ -222,9 +225,9 @@ def test_single_block_matches_reference(cuda, p, seed):
     fr["mask"][T + 3] = 1
     valid = (rng.random(N) < 0.9).astype(np.uint8)
     valid[:T] = 1
-    x_in = W.round_storage(rng.normal(0, 1, size=(N, C)).astype(np.float32), "bf16")
-    x_prev = W.round_storage(rng.normal(0, 1, size=(N, C)).astype(np.float32), "bf16")
-    g = lambda *shape, sd=1.0: W.round_storage(rng.normal(0, sd, size=shape).astype(np.float32), "bf16")
+    x_in = W.round_storage(rng.normal(0, 1, size=(N, C)).astype(np.float32), dtype)
+    x_prev = W.round_storage(rng.normal(0, 1, size=(N, C)).astype(np.float32), dtype)
+    g = lambda *shape, sd=1.0: W.round_storage(rng.normal(0, sd, size=shape).astype(np.float32), dtype)
     f = lambda *shape, mu=0.0, sd=1.0: rng.normal(mu, sd, size=shape).astype(np.float32)
     wt = {"shift": f(C, sd=0.1), "scale": f(C, sd=0.1), "gate": f(C, mu=1.0, sd=0.2),
           "w_qkv_mlp": g(3 * C + H, C, sd=C ** -0.5), "b_qkv_mlp": f(3 * C + H, sd=0.05),
@@ -232,9 +235,9 @@ def test_single_block_matches_reference(cuda, p, seed):
           "w_out": g(C, C + H, sd=(C + H) ** -0.5), "b_out": f(C, sd=0.05)}
     ref = _reference_single_block(w, fr, x_in, valid, wt, H)
 
-    dev = lambda a, dt=torch.bfloat16: torch.from_numpy(np.ascontiguousarray(a)).to("cuda").to(dt)
-    tw = {k: dev(v, torch.bfloat16 if k.startswith("w_") else torch.float32) for k, v in wt.items()}
-    cfg = fxr.FrameConfig(n_tokens=N, n_text=T, n_heads=w.n_heads, dtype="bf16", rope_axes=w.rope_axes,
+    dev = lambda a, dt=td: torch.from_numpy(np.ascontiguousarray(a)).to("cuda").to(dt)
+    tw = {k: dev(v, td if k.startswith("w_") else torch.float32) for k, v in wt.items()}
+    cfg = fxr.FrameConfig(n_tokens=N, n_text=T, n_heads=w.n_heads, dtype=dtype, rope_axes=w.rope_axes,
                           rope_theta=w.rope_theta)
     xi, xo = dev(x_in), dev(x_prev)
     mask = torch.from_numpy(fr["mask"].copy()).cuda()
@@ -248,7 +251,7 @@ def test_single_block_matches_reference(cuda, p, seed):
     idx = ref["idx"]
     assert np.array_equal(mask.cpu().numpy(), ref["mask"])
     got = xo.float().cpu().numpy()
-    e = _ulp_err(got[idx], ref["x_out"])
+    e = _ulp_err(got[idx], ref["x_out"], dtype)
     print(f"single block x_out rows {idx.size}: max {e.max():.1f} steps, mean {e.mean():.3f}")
     assert e.max() <= 2 and e.mean() < 0.05, (e.max(), e.mean())
     skipped = np.setdiff1d(np.arange(N), idx)
@@ -257,5 +260,5 @@ def test_single_block_matches_reference(cuda, p, seed):
         gc = (ck if key == "cache_k" else cv).float().cpu().numpy()
         upd = ref["mask"] == 2
         assert np.array_equal(gc[~upd], fr[key][~upd]), key
-        ec = _ulp_err(gc[upd], ref[key][upd])
+        ec = _ulp_err(gc[upd], ref[key][upd], dtype)
         assert ec.max() <= 2 and np.mean(ec > 1) < 1e-4, (key, ec.max())
