@@ -246,3 +246,72 @@ int32_t fxo_frame_forward(const float* q, const float* k, const float* v,
     free(av);
     return M;
 }
+
+/* gather_scatter_kernels.cu:106-169 (formula, without the uninitialised shared accumulators)
+ * followed by apply_modulation (gather_scatter_kernels.cu:77-99). */
+void fxo_layer_norm_modulate(const float* x, int64_t ld_x, float* y, const float* scale,
+                             const float* shift, float eps, int64_t rows, int32_t dim) {
+    #pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+        const float* xr = x + r * ld_x;
+        float* yr = y + r * (int64_t)dim;
+        double s = 0.0;
+        for (int32_t i = 0; i < dim; ++i) s += (double)xr[i];
+        const double mean = s / (double)dim;
+        double ss = 0.0;
+        for (int32_t i = 0; i < dim; ++i) {
+            const double d = (double)xr[i] - mean;
+            ss += d * d;
+        }
+        const double rstd = 1.0 / sqrt(ss / (double)dim + (double)eps);
+        for (int32_t i = 0; i < dim; ++i) {
+            double v = ((double)xr[i] - mean) * rstd;
+            if (scale) v *= 1.0 + (double)scale[i];
+            if (shift) v += (double)shift[i];
+            yr[i] = (float)v;
+        }
+    }
+}
+
+/* flux2_kernels.cu:14-29. */
+void fxo_gelu_tanh(float* x, int64_t n) {
+    #pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        const double v = (double)x[i];
+        x[i] = (float)(0.5 * v * (1.0 + tanh(0.7978845608 * (v + 0.044715 * v * v * v))));
+    }
+}
+
+/* flux2_double_block_plugin.cpp:28-45 (Y = X W^T) + bias_add (flux2_kernels.cu:34-53). */
+void fxo_linear(const float* x, int64_t ld_x, int64_t rows, int32_t k, const float* w, const float* b,
+                float* y, int32_t n) {
+    #pragma omp parallel for schedule(dynamic, 4)
+    for (int64_t r = 0; r < rows; ++r) {
+        const float* xr = x + r * ld_x;
+        float* yr = y + r * (int64_t)n;
+        for (int32_t j = 0; j < n; ++j) {
+            const float* wj = w + (int64_t)j * k;
+            double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+            int32_t i = 0;
+            for (; i + 4 <= k; i += 4) {
+                a0 += (double)xr[i] * (double)wj[i];
+                a1 += (double)xr[i + 1] * (double)wj[i + 1];
+                a2 += (double)xr[i + 2] * (double)wj[i + 2];
+                a3 += (double)xr[i + 3] * (double)wj[i + 3];
+            }
+            for (; i < k; ++i) a0 += (double)xr[i] * (double)wj[i];
+            yr[j] = (float)((a0 + a1) + (a2 + a3) + (b ? (double)b[j] : 0.0));
+        }
+    }
+}
+
+/* flux2_kernels.cu:116-135 with a per-channel gate (flux2_double_block_plugin.cpp:449-458). */
+void fxo_gated_residual(const float* x, int64_t ld_x, const float* gate, const float* proj, float* out,
+                        int64_t rows, int32_t dim) {
+    #pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; ++r)
+        for (int32_t i = 0; i < dim; ++i) {
+            const int64_t o = r * (int64_t)dim + i;
+            out[o] = x[r * ld_x + i] + (gate ? gate[i] : 1.0f) * proj[o];
+        }
+}

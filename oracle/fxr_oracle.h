@@ -18,6 +18,10 @@
  *   - RMSNorm: pinned against an independent torch fp32 evaluation of the formula in
  *     src/inference/plugins/flux2_kernels.cu:58-82.
  *   - attention: pinned against torch.nn.functional.scaled_dot_product_attention (fp32, CPU).
+ *   - LayerNorm: pinned against the known answer of src/spike/test_gather_scatter.cpp:106-133;
+ *     modulation, tanh GELU and bias add: pinned on a GPU against the reference's own
+ *     apply_modulation / gelu / bias_add kernels compiled from source; linear projection and
+ *     gated residual: checked against numpy fp64 (the reference calls cublasSgemm there).
  *   - RoPE: parity unpinned. The reference has no RoPE code; the formula follows the
  *     published FLUX rotary embedding (interleaved pairs, per-axis frequencies
  *     theta^(-2j/d_a)) and is checked only through its algebraic properties.
@@ -80,6 +84,34 @@ void fxo_kv_sync(float* keys, float* values, float* cached_keys, float* cached_v
  * mask index T+i: pred = execute ? pred : cache; if update: cache = old pred, valid[T+i] = 1. */
 void fxo_output_cache_sync(float* pred, float* cache, const int32_t* mask, uint8_t* valid,
                            int32_t n_text, int32_t n_image, int32_t channels);
+
+/* Block-row math around the attention slice (the dense steps of one double- or single-stream
+ * block, restated row by row so that a caller can apply them to the executed rows only).
+ *
+ * LayerNorm without affine weights + modulation (gather_scatter_kernels.cu:106-169 then
+ * apply_modulation, gather_scatter_kernels.cu:77-99; called at flux2_double_block_plugin.cpp:373-383):
+ *   y = (1 + scale) * (x - mean) * rsqrt(var + eps) + shift, biased variance over dim.
+ * scale/shift may be NULL (plain LayerNorm, the reference's gamma = beta = NULL call). The reference
+ * kernel accumulates into uninitialised shared scalars (gather_scatter_kernels.cu:127-147); this
+ * restates the formula. Pinned against the known answer of test_gather_scatter.cpp:106-133.
+ * x: [rows, ld_x], y: [rows, dim]; mean and variance in double. */
+void fxo_layer_norm_modulate(const float* x, int64_t ld_x, float* y, const float* scale,
+                             const float* shift, float eps, int64_t rows, int32_t dim);
+
+/* tanh GELU in place (flux2_kernels.cu:14-29): x * 0.5 * (1 + tanh(0.7978845608 * (x + 0.044715 x^3))). */
+void fxo_gelu_tanh(float* x, int64_t n);
+
+/* Linear projection y = x W^T + b (the plugin's row-major cublasSgemm, flux2_double_block_plugin.cpp:28-45,
+ * followed by bias_add, flux2_kernels.cu:34-53). x: [rows, k] (row stride ld_x), W: [n, k], b: [n] or
+ * NULL, y: [rows, n]. Products accumulate in double and round once to fp32. */
+void fxo_linear(const float* x, int64_t ld_x, int64_t rows, int32_t k, const float* w, const float* b,
+                float* y, int32_t n);
+
+/* Gated residual out = x + gate * proj (scale_add, flux2_kernels.cu:116-135, with the per-channel gate
+ * of the modulation vector that flux2_double_block_plugin.cpp:449-458 leaves at 1.0). x: [rows, ld_x],
+ * proj/out: [rows, dim]; gate: [dim] or NULL (= 1.0, the reference as written). */
+void fxo_gated_residual(const float* x, int64_t ld_x, const float* gate, const float* proj, float* out,
+                        int64_t rows, int32_t dim);
 
 /* One frame of the sparse attention slice, fp32 end to end (storage rounding is the caller's).
  *   q, k, v      [N, C] fresh projections (C = H*D), fp32

@@ -60,6 +60,12 @@ def lib(native: bool = False) -> ctypes.CDLL:
                                 ctypes.c_float, _f32p, _i64]
     L.fxo_kv_sync.argtypes = [_f32p, _f32p, _f32p, _f32p, _i32p, _i32, _i64]
     L.fxo_output_cache_sync.argtypes = [_f32p, _f32p, _i32p, _u8p, _i32, _i32, _i32]
+    L.fxo_layer_norm_modulate.argtypes = [_f32p, _i64, _f32p, _f32p, _f32p, ctypes.c_float, _i64, _i32]
+    L.fxo_gelu_tanh.argtypes = [_f32p, _i64]
+    L.fxo_linear.argtypes = [_f32p, _i64, _i64, _i32, _f32p, _f32p, _f32p, _i32]
+    L.fxo_gated_residual.argtypes = [_f32p, _i64, _f32p, _f32p, _f32p, _i64, _i32]
+    for fn in (L.fxo_layer_norm_modulate, L.fxo_gelu_tanh, L.fxo_linear, L.fxo_gated_residual):
+        fn.restype = None
     L.fxo_frame_forward.argtypes = [_f32p, _f32p, _f32p, _i32p, _u8p, _i32p, _f32p, _f32p,
                                     _f32p, _f32p, _f32p, _f32p, _i32p,
                                     _i32, _i32, _i32, _i32, _i32p, ctypes.c_float,
@@ -188,6 +194,48 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, n_heads: int, head_di
     lib().fxo_attention(_p(q, _f32p), C, M, _p(k, _f32p), _p(v, _f32p), k.shape[1], k.shape[0],
                         n_heads, head_dim, scale, _p(o, _f32p), C)
     return o
+
+
+def _f32(a):
+    return None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+
+
+def layer_norm_modulate(x: np.ndarray, scale=None, shift=None, eps: float = 1e-6) -> np.ndarray:
+    """LayerNorm without affine weights, then (1 + scale) * . + shift; x [rows, dim]."""
+    x = _f32(x)
+    rows, dim = x.shape
+    sc, sh = _f32(scale), _f32(shift)
+    y = np.empty_like(x)
+    lib().fxo_layer_norm_modulate(_p(x, _f32p), dim, _p(y, _f32p), _p(sc, _f32p), _p(sh, _f32p),
+                                  eps, rows, dim)
+    return y
+
+
+def gelu_tanh(x: np.ndarray) -> np.ndarray:
+    y = _f32(x).copy()
+    lib().fxo_gelu_tanh(_p(y, _f32p), y.size)
+    return y
+
+
+def linear(x: np.ndarray, w: np.ndarray, b=None) -> np.ndarray:
+    """y = x W^T + b; x [rows, k], W [n, k]."""
+    x, w, b = _f32(x), _f32(w), _f32(b)
+    rows, k = x.shape
+    n = w.shape[0]
+    assert w.shape[1] == k and (b is None or b.size == n)
+    y = np.empty((rows, n), dtype=np.float32)
+    lib().fxo_linear(_p(x, _f32p), k, rows, k, _p(w, _f32p), _p(b, _f32p), _p(y, _f32p), n)
+    return y
+
+
+def gated_residual(x: np.ndarray, proj: np.ndarray, gate=None) -> np.ndarray:
+    """x + gate * proj (gate per channel, None = 1.0)."""
+    x, proj, gate = _f32(x), _f32(proj), _f32(gate)
+    rows, dim = x.shape
+    out = np.empty_like(proj)
+    lib().fxo_gated_residual(_p(x, _f32p), dim, _p(gate, _f32p), _p(proj, _f32p), _p(out, _f32p),
+                             rows, dim)
+    return out
 
 
 def kv_sync(keys, values, cached_keys, cached_values, mask):

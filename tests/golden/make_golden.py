@@ -7,6 +7,7 @@ Sources (paths inside the fluxrt-cpp project):
   gather      src/spike/test_gather_scatter.cpp:39-68   (tokens {0,2,3} of 4, dim 3)
   scatter     src/spike/test_gather_scatter.cpp:73-103  (rows {1,3}; untouched rows stay -1)
   cache       src/spike/test_spatial_cache.cu:20-93     (preprocess -> all 2; restore 1/50/9/130)
+  layer_norm  src/spike/test_gather_scatter.cpp:106-133 (LayerNorm of rows 1..4 and 5..8, dim 4)
   cache_mixed src/spike/test_spatial_cache_trt.cpp:243-296 (reset + partial validity; logic
               ported at a small size: the original runs 256 text + 4096 image tokens behind a
               TensorRT engine, here 4 text + 8 image tokens with the same half split)
@@ -66,6 +67,16 @@ def main():
         # then an all-zero mask preprocesses to: text 2 (the output cache never marks text
         # valid), first half of image 0, second half 2 (:268-292)
         "final_expected": [2] * txt + [0] * half + [2] * (img - half),
+    }
+    # --- layer_norm_modulated without gamma/beta (test_gather_scatter.cpp:106-133) ---
+    cases["layer_norm"] = {
+        "seq_len": 2,
+        "dim": 4,
+        "eps": 1e-6,
+        "x": [1, 2, 3, 4, 5, 6, 7, 8],
+        # both rows have variance 1.25 about their mean, so both normalise to the same values
+        "expected_row": [-1.3416407, -0.4472136, 0.4472136, 1.3416407],
+        "tol": 1e-4,
     }
     with open(os.path.join(HERE, "reference_kat.json"), "w") as f:
         json.dump(cases, f, indent=1, sort_keys=True)

@@ -3,8 +3,9 @@ of the reference block (flux2_double_block_plugin.cpp:330-460: LayerNorm + modul
 RMSNorm, attention, out-projection, GELU MLP, residual) with joint text + image attention over the
 spatial K/V cache, fp32 arithmetic rounded to bf16 where the kernels store; and the single-stream
 block (fxr_single_block_forward: one fused to_qkv_mlp_proj, one to_out over [attention | MLP],
-tools/export_block_weights.py:79-113) against the same kind of restatement. Attention, RMSNorm and
-RoPE come from the oracle (oracle/fxr_oracle.c)."""
+tools/export_block_weights.py:79-113) against the same kind of restatement. Every step of the
+restatement is the oracle's (oracle/fxr_oracle.c): LayerNorm + modulation, linear projections, tanh
+GELU, gated residual, QK-RMSNorm, RoPE and attention."""
 import ctypes
 
 import numpy as np
@@ -36,16 +37,6 @@ def test_double_block_argument_checks():
     assert fxr.double_block_workspace_size(cfg, 4608) > ws
 
 
-def _ln_mod(x, scale, shift, eps=1e-6):
-    mean = x.mean(axis=1, keepdims=True)
-    var = ((x - mean) ** 2).mean(axis=1, keepdims=True)
-    return (1.0 + scale) * ((x - mean) / np.sqrt(var + eps)) + shift
-
-
-def _gelu(x):
-    return 0.5 * x * (1.0 + np.tanh(0.7978845608 * (x + 0.044715 * x * x * x)))
-
-
 def _reference_block(w, fr, x_in, valid, streams, H):
     """fp32 restatement, rounded to the storage type where the kernels store; returns the executed
     token list, their block outputs, the caches, the preprocessed mask and the validity flags."""
@@ -69,10 +60,10 @@ def _reference_block(w, fr, x_in, valid, streams, H):
         if rows.size == 0:
             continue
         toks = idx[rows]
-        xn[rows] = bf(_ln_mod(x_in[toks], s["scale"], s["shift"]))
-        qkv = bf(xn[rows] @ s["w_qkv"].T + s["b_qkv"])
+        xn[rows] = bf(oracle.layer_norm_modulate(x_in[toks], s["scale"], s["shift"]))
+        qkv = bf(oracle.linear(xn[rows], s["w_qkv"], s["b_qkv"]))
         q[toks], k[toks], v[toks] = qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:]
-        hmid[rows] = bf(_gelu(xn[rows] @ s["w_mlp0"].T + s["b_mlp0"]))
+        hmid[rows] = bf(oracle.gelu_tanh(oracle.linear(xn[rows], s["w_mlp0"], s["b_mlp0"])))
         rope = lambda x, t: np.concatenate([oracle.rope_row(x[h * D:(h + 1) * D], fr["pos"][t], w.rope_axes,
                                                             w.rope_theta) for h in range(w.n_heads)])
         for r, t in zip(rows, toks):
@@ -89,8 +80,8 @@ def _reference_block(w, fr, x_in, valid, streams, H):
         if rows.size == 0:
             continue
         toks = idx[rows]
-        proj = o[rows] @ s["w_out"].T + s["b_out"] + hmid[rows] @ s["w_mlp2"].T + s["b_mlp2"]
-        x_out[rows] = bf(x_in[toks] + s["gate"] * proj)
+        proj = oracle.linear(o[rows], s["w_out"], s["b_out"]) + oracle.linear(hmid[rows], s["w_mlp2"], s["b_mlp2"])
+        x_out[rows] = bf(oracle.gated_residual(x_in[toks], proj, s["gate"]))
     upd = mask == 2
     ck[upd], cv[upd] = k_att[upd], v_att[upd]
     valid_out = valid.copy()
@@ -192,10 +183,10 @@ def _reference_single_block(w, fr, x_in, valid, wt, H):
     mask[valid == 0] = 2
     mask[:T][mask[:T] == 0] = 2
     idx = np.nonzero(mask)[0]
-    xn = bf(_ln_mod(x_in[idx], wt["scale"], wt["shift"]))
-    proj = xn @ wt["w_qkv_mlp"].T + wt["b_qkv_mlp"]
+    xn = bf(oracle.layer_norm_modulate(x_in[idx], wt["scale"], wt["shift"]))
+    proj = oracle.linear(xn, wt["w_qkv_mlp"], wt["b_qkv_mlp"])
     q, k, v = bf(proj[:, :C]), bf(proj[:, C:2 * C]), bf(proj[:, 2 * C:3 * C])
-    h = bf(_gelu(proj[:, 3 * C:]))
+    h = bf(oracle.gelu_tanh(proj[:, 3 * C:]))
     rope = lambda x, t: np.concatenate([oracle.rope_row(x[j * D:(j + 1) * D], fr["pos"][t], w.rope_axes,
                                                         w.rope_theta) for j in range(w.n_heads)])
     ck, cv = fr["cache_k"].copy(), fr["cache_v"].copy()
@@ -206,7 +197,8 @@ def _reference_single_block(w, fr, x_in, valid, wt, H):
         k_att[t] = bf(rope(oracle.rms_norm(k[r].reshape(-1, D), wt["norm_k"]).reshape(-1), t))
         v_att[t] = v[r]
     o = bf(oracle.attention(qn, k_att, v_att, w.n_heads, D))
-    x_out = bf(x_in[idx] + wt["gate"] * (np.concatenate([o, h], axis=1) @ wt["w_out"].T + wt["b_out"]))
+    x_out = bf(oracle.gated_residual(x_in[idx], oracle.linear(np.concatenate([o, h], axis=1), wt["w_out"],
+                                                              wt["b_out"]), wt["gate"]))
     upd = mask == 2
     ck[upd], cv[upd] = k_att[upd], v_att[upd]
     return {"idx": idx, "x_out": x_out, "cache_k": ck, "cache_v": cv, "mask": mask}

@@ -103,6 +103,52 @@ def test_rms_norm_vs_torch():
     np.testing.assert_allclose(got, ref.numpy(), rtol=2e-6, atol=2e-6)
 
 
+def test_layer_norm_known_answer():
+    c = KAT["layer_norm"]
+    x = np.array(c["x"], dtype=np.float32).reshape(c["seq_len"], c["dim"])
+    got = O.layer_norm_modulate(x, eps=c["eps"])
+    for row in got:
+        assert np.abs(row - np.array(c["expected_row"], dtype=np.float32)).max() <= c["tol"]
+
+
+@pytest.mark.parametrize("rows,dim", [(1, 4), (33, 256), (8, 3072)])
+def test_layer_norm_modulate_vs_torch(rows, dim):
+    rng = np.random.default_rng(rows + dim)
+    x = rng.normal(0.3, 2.0, size=(rows, dim)).astype(np.float32)
+    sc = rng.normal(0, 0.1, size=dim).astype(np.float32)
+    sh = rng.normal(0, 0.1, size=dim).astype(np.float32)
+    got = O.layer_norm_modulate(x, sc, sh, 1e-6)
+    ln = torch.nn.functional.layer_norm(torch.from_numpy(x).double(), (dim,), eps=1e-6)
+    ref = (1 + torch.from_numpy(sc).double()) * ln + torch.from_numpy(sh).double()
+    np.testing.assert_allclose(got, ref.numpy(), rtol=1e-6, atol=1e-6)
+    # plain LayerNorm: the reference's gamma = beta = NULL call
+    np.testing.assert_allclose(O.layer_norm_modulate(x, eps=1e-6), ln.numpy(), rtol=1e-6, atol=1e-6)
+
+
+def test_gelu_tanh_vs_torch():
+    x = np.linspace(-8, 8, 4001, dtype=np.float32)
+    ref = torch.nn.functional.gelu(torch.from_numpy(x).double(), approximate="tanh").numpy()
+    np.testing.assert_allclose(O.gelu_tanh(x), ref, rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("rows,k,n,bias", [(1, 64, 3, True), (37, 130, 256, True), (5, 256, 17, False)])
+def test_linear_vs_numpy_f64(rows, k, n, bias):
+    rng = np.random.default_rng(rows * k + n)
+    x = rng.normal(size=(rows, k)).astype(np.float32)
+    w = rng.normal(size=(n, k)).astype(np.float32)
+    b = rng.normal(size=n).astype(np.float32) if bias else None
+    ref = x.astype(np.float64) @ w.astype(np.float64).T + (b.astype(np.float64) if bias else 0.0)
+    np.testing.assert_allclose(O.linear(x, w, b), ref, rtol=1e-6, atol=1e-5)
+
+
+def test_gated_residual():
+    rng = np.random.default_rng(11)
+    x, p = rng.normal(size=(2, 9, 16)).astype(np.float32)
+    g = rng.normal(size=16).astype(np.float32)
+    np.testing.assert_array_equal(O.gated_residual(x, p, g), x + g * p)
+    np.testing.assert_array_equal(O.gated_residual(x, p), x + p)       # the reference's gate = 1.0
+
+
 @pytest.mark.parametrize("M,N,H", [(1, 1, 1), (5, 37, 2), (130, 300, 3)])
 def test_attention_vs_torch_sdpa(M, N, H):
     rng = np.random.default_rng(M * 1000 + N)

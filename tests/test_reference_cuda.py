@@ -5,8 +5,8 @@ Row gather/scatter (gather_scatter_kernels.cu:15-72) and the spatial-cache
 protocol — preprocess, K/V merge + update, output merge + update + validity
 (spatial_kv_cache.cu:12-87, SpatialCache methods :153-196) — over two frames, so that the second
 frame runs on the state the first one left — bit-exact; the GELU, bias and modulation kernels
-(flux2_kernels.cu:14-56, gather_scatter_kernels.cu:77-99) against the block tests' restatements
-and the GEMM's fused epilogue. The reference RMSNorm and LayerNorm (uninitialised shared
+(flux2_kernels.cu:14-56, gather_scatter_kernels.cu:77-99) against the oracle's restatements
+(oracle/fxr_oracle.c) and the GEMM's fused epilogue. The reference RMSNorm and LayerNorm (uninitialised shared
 accumulators, flux2_kernels.cu:58-82, gather_scatter_kernels.cu:129-150) and attention (one warp's partial max and sum broadcast as
 the block's, attention_kernels.cu:117-139) are not deterministic oracles and are only timed
 (oracle/time_reference_cuda.py)."""
@@ -109,26 +109,37 @@ def test_spatial_cache_protocol_matches_reference_over_two_frames(ref):
         ref.ref_cache_destroy(h)
 
 
-def test_gelu_and_modulation_restatements_match_reference(ref):
-    """The tanh GELU and the modulation that the block tests restate (tests/test_block_rows.py,
-    tests/test_double_block.py) against the reference's own gelu_kernel (flux2_kernels.cu:14-29)
-    and apply_modulation_kernel (gather_scatter_kernels.cu:77-99), fp32 on the GPU."""
+def test_gelu_modulation_and_bias_restatements_match_reference(ref):
+    """The oracle's tanh GELU, modulation and linear bias (fxo_gelu_tanh, fxo_layer_norm_modulate,
+    fxo_linear: the restatement the block tests check against) against the reference's own
+    gelu_kernel (flux2_kernels.cu:14-29), apply_modulation_kernel (gather_scatter_kernels.cu:77-99)
+    and bias_add_kernel (flux2_kernels.cu:34-53), fp32 on the GPU."""
     import torch
     g = torch.Generator(device="cuda").manual_seed(5)
     x = torch.randn(1 << 16, device="cuda", generator=g) * 3
     a = x.clone()
     ref.ref_gelu(a.data_ptr(), a.numel(), _s())
-    mine = 0.5 * x * (1.0 + torch.tanh(0.7978845608 * (x + 0.044715 * x * x * x)))
     torch.cuda.synchronize()
-    assert torch.allclose(a, mine, rtol=4e-6, atol=4e-7), float((a - mine).abs().max())
+    mine = O.gelu_tanh(x.cpu().numpy())
+    np.testing.assert_allclose(a.cpu().numpy(), mine, rtol=4e-6, atol=4e-7)
     rows, dim = 257, 3072
-    xm = torch.randn(rows, dim, device="cuda", generator=g)
+    # modulation of already-normalised rows: LayerNorm leaves a zero-mean, unit-variance row unchanged
+    xm = torch.randn(rows, dim, device="cuda", generator=g, dtype=torch.float64)
+    xm = ((xm - xm.mean(1, keepdim=True)) / xm.std(1, unbiased=False, keepdim=True)).float()
     sc = torch.randn(dim, device="cuda", generator=g) * 0.2
     sh = torch.randn(dim, device="cuda", generator=g) * 0.2
     out = torch.empty_like(xm)
     ref.ref_apply_modulation(xm.data_ptr(), sc.data_ptr(), sh.data_ptr(), out.data_ptr(), rows, dim, _s())
     torch.cuda.synchronize()
-    assert torch.allclose(out, (1.0 + sc) * xm + sh, rtol=1e-6, atol=1e-6)
+    mine = O.layer_norm_modulate(xm.cpu().numpy(), sc.cpu().numpy(), sh.cpu().numpy(), eps=0.0)
+    np.testing.assert_allclose(out.cpu().numpy(), mine, rtol=2e-6, atol=2e-6)
+    # bias add: a zero product leaves the bias broadcast over the rows
+    bias = torch.randn(dim, device="cuda", generator=g)
+    z = torch.zeros(rows, dim, device="cuda")
+    ref.ref_bias_add(z.data_ptr(), bias.data_ptr(), rows, dim, _s())
+    torch.cuda.synchronize()
+    mine = O.linear(np.zeros((rows, 8), np.float32), np.zeros((dim, 8), np.float32), bias.cpu().numpy())
+    np.testing.assert_array_equal(z.cpu().numpy(), mine)
 
 
 def test_rows_gemm_gelu_epilogue_matches_reference_gelu(ref):
