@@ -773,10 +773,41 @@ int32_t fxr_attention_f32_bhsd(const float* q, const float* k, const float* v, f
     return FXR_OK;
 }
 
-int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void* k, const void* v,
-                          int32_t* mask, const uint8_t* valid, const int32_t* pos,
-                          const float* norm_q, const float* norm_k, void* cache_k, void* cache_v,
-                          void* out, void* workspace, size_t workspace_bytes, void* stream) {
+// Device-side addresses of a host-buffer frame's page-locked rows (fxr_frame_forward_host).
+struct HostIo {
+    const void* q;
+    const void* k;
+    const void* v;
+    void* out;
+};
+
+// Executed rows idx[0..M) of n tensors from src to dst at the same row positions (one side mapped
+// host memory), chained to the previous launch on the stream.
+static int32_t launch_host_rows(const void* const* src, void* const* dst, int n, int64_t ld_elems,
+                                int64_t row_bytes, size_t elem_bytes, const int32_t* idx,
+                                const int32_t* count, int32_t n_tokens, cudaStream_t s) {
+    fxr::HostRowsArgs a{};
+    for (int t = 0; t < n; ++t) {
+        a.src[t] = static_cast<const uint4*>(src[t]);
+        a.dst[t] = static_cast<uint4*>(dst[t]);
+    }
+    a.idx = idx;
+    a.count = count;
+    a.ld_vec = ld_elems * (int64_t)elem_bytes / 16;
+    a.row_vec = (int32_t)(row_bytes / 16);
+    a.n_tensors = n;
+    a.n_tokens = n_tokens;
+    const int grid = 2 * sm_count();
+    cudaError_t e = launch_pdl(fxr::host_rows_kernel, dim3(grid), dim3(fxr::kHostRowsThreads), 0, s, a);
+    if (e != cudaSuccess) return cuda_status(e, "host_rows_kernel launch");
+    return FXR_OK;
+}
+
+static int32_t frame_forward_impl(const fxr_frame_desc* desc, const void* q, const void* k, const void* v,
+                                  int32_t* mask, const uint8_t* valid, const int32_t* pos,
+                                  const float* norm_q, const float* norm_k, void* cache_k, void* cache_v,
+                                  void* out, void* workspace, size_t workspace_bytes, void* stream,
+                                  const HostIo* host) {
     int32_t st = check_desc(desc, true);
     if (st != FXR_OK) return st;
     if (desc->n_tokens == 0) return FXR_OK;
@@ -787,6 +818,16 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void*
     if (!aligned16(workspace)) return fail(FXR_ERR_INVALID, "workspace must be 16-byte aligned");
     const SplitArea split = split_area(w.total, workspace, workspace_bytes, desc->n_heads);
     if ((st = launch_compact(mask, valid, desc->n_tokens, w.idx, w.count, split, stream)) != FXR_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t eb = dtype_bytes(desc->dtype);
+    const int64_t row_bytes = (int64_t)desc->n_heads * desc->head_dim * (int64_t)eb;
+    if (host) {
+        const void* src[3] = {host->q, host->k, host->v};
+        void* dst[3] = {const_cast<void*>(q), const_cast<void*>(k), const_cast<void*>(v)};
+        if ((st = launch_host_rows(src, dst, 3, desc->ld_qkv, row_bytes, eb, w.idx, w.count, desc->n_tokens,
+                                   s)) != FXR_OK)
+            return st;
+    }
     if ((st = fxr_gather_norm_rope(desc, q, k, v, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc,
                                    w.ld_qc, cache_k, cache_v, w.save, stream)) != FXR_OK)
         return st;
@@ -795,12 +836,116 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void*
     OutSet os;
     os.out = out;
     os.split = split;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     st = desc->dtype == FXR_BF16
              ? launch_attention<__nv_bfloat16>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s)
              : launch_attention<__half>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s);
     if (st != FXR_OK) return st;
-    return fxr_restore_rows(desc, mask, w.idx, w.count, w.save, cache_k, cache_v, stream);
+    if ((st = fxr_restore_rows(desc, mask, w.idx, w.count, w.save, cache_k, cache_v, stream)) != FXR_OK)
+        return st;
+    if (host) {
+        const void* src[1] = {out};
+        void* dst[1] = {host->out};
+        return launch_host_rows(src, dst, 1, desc->ld_out, row_bytes, eb, w.idx, w.count, desc->n_tokens, s);
+    }
+    return FXR_OK;
+}
+
+int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void* k, const void* v,
+                          int32_t* mask, const uint8_t* valid, const int32_t* pos,
+                          const float* norm_q, const float* norm_k, void* cache_k, void* cache_v,
+                          void* out, void* workspace, size_t workspace_bytes, void* stream) {
+    return frame_forward_impl(desc, q, k, v, mask, valid, pos, norm_q, norm_k, cache_k, cache_v, out,
+                              workspace, workspace_bytes, stream, nullptr);
+}
+
+// Staging rows of a host-buffer frame at the start of its workspace: the mask copy, then Q, K, V
+// (row stride ld_qkv) and the output (ld_out); the frame's own workspace follows.
+struct HostStage {
+    int32_t* mask;
+    void* q;
+    void* k;
+    void* v;
+    void* out;
+    size_t total;
+};
+
+static HostStage carve_host(const fxr_frame_desc* d, void* ws) {
+    HostStage h{};
+    const size_t N = (size_t)(d->n_tokens > 0 ? d->n_tokens : 1);
+    const size_t eb = dtype_bytes(d->dtype);
+    char* b = static_cast<char*>(ws);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        void* p = b ? b + off : nullptr;
+        off += align_up(bytes, 256);
+        return p;
+    };
+    h.mask = static_cast<int32_t*>(take(N * sizeof(int32_t)));
+    h.q = take(N * (size_t)d->ld_qkv * eb);
+    h.k = take(N * (size_t)d->ld_qkv * eb);
+    h.v = take(N * (size_t)d->ld_qkv * eb);
+    h.out = take(N * (size_t)d->ld_out * eb);
+    h.total = off;
+    return h;
+}
+
+size_t fxr_frame_host_workspace_size(const fxr_frame_desc* desc) {
+    if (check_desc(desc, true) != FXR_OK) return 0;
+    return carve_host(desc, nullptr).total + fxr_workspace_size(desc);
+}
+
+// Device-side address of page-locked, mapped host memory covering [p, p + bytes); null otherwise
+// (pageable memory, device memory, or a range whose two ends do not map contiguously).
+static const void* mapped_host_range(const void* p, size_t bytes) {
+    if (!p || bytes == 0) return nullptr;
+    cudaPointerAttributes a0{}, a1{};
+    const char* last = static_cast<const char*>(p) + bytes - 1;
+    if (cudaPointerGetAttributes(&a0, p) != cudaSuccess || cudaPointerGetAttributes(&a1, last) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (a0.type != cudaMemoryTypeHost || a1.type != cudaMemoryTypeHost || !a0.devicePointer ||
+        static_cast<const char*>(a1.devicePointer) != static_cast<const char*>(a0.devicePointer) + bytes - 1)
+        return nullptr;
+    return a0.devicePointer;
+}
+
+int32_t fxr_frame_forward_host(const fxr_frame_desc* desc, const void* host_q, const void* host_k,
+                               const void* host_v, const int32_t* host_mask, const uint8_t* valid,
+                               const int32_t* pos, const float* norm_q, const float* norm_k, void* cache_k,
+                               void* cache_v, void* host_out, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+    int32_t st = check_desc(desc, true);
+    if (st != FXR_OK) return st;
+    if (desc->n_tokens == 0) return FXR_OK;
+    if (!workspace) return fail(FXR_ERR_INVALID, "null workspace");
+    if (!aligned16(workspace)) return fail(FXR_ERR_INVALID, "workspace must be 16-byte aligned");
+    const HostStage h = carve_host(desc, workspace);
+    const size_t need = h.total + carve(desc, nullptr).total;
+    if (workspace_bytes < need)
+        return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, need);
+    if (!host_q || !host_k || !host_v || !host_mask || !host_out)
+        return fail(FXR_ERR_INVALID, "null host buffer");
+    const size_t N = (size_t)desc->n_tokens, eb = dtype_bytes(desc->dtype);
+    const size_t C = (size_t)desc->n_heads * desc->head_dim;
+    const size_t qkv_bytes = ((N - 1) * (size_t)desc->ld_qkv + C) * eb;
+    const size_t out_bytes = ((N - 1) * (size_t)desc->ld_out + C) * eb;
+    HostIo io;
+    io.q = mapped_host_range(host_q, qkv_bytes);
+    io.k = mapped_host_range(host_k, qkv_bytes);
+    io.v = mapped_host_range(host_v, qkv_bytes);
+    io.out = const_cast<void*>(mapped_host_range(host_out, out_bytes));
+    if (!io.q || !io.k || !io.v || !io.out)
+        return fail(FXR_ERR_INVALID, "host_q / host_k / host_v / host_out must be page-locked host memory mapped "
+                                     "into the device address space");
+    if (!aligned16(io.q) || !aligned16(io.k) || !aligned16(io.v) || !aligned16(io.out))
+        return fail(FXR_ERR_INVALID, "host buffers must be 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(h.mask, host_mask, N * sizeof(int32_t), cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cuda_status(e, "mask copy");
+    char* frame_ws = static_cast<char*>(workspace) + h.total;
+    return frame_forward_impl(desc, h.q, h.k, h.v, h.mask, valid, pos, norm_q, norm_k, cache_k, cache_v, h.out,
+                              frame_ws, workspace_bytes - h.total, stream, &io);
 }
 
 size_t fxr_rows_gemm_scratch_size(void) {

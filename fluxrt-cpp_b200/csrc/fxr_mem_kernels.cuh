@@ -4,6 +4,7 @@
 //                            RMSNorm + multi-axis RoPE, cache-row write
 //   arrival_wait_kernel      end of a head-split frame: waits for every GPU's O rows
 //   restore_rows_kernel      puts back the cache rows of mask==1 tokens after the attention
+//   host_rows_kernel         executed rows between page-locked host memory and the device (PCIe)
 //   rows_copy_kernel         byte-exact indexed row gather / scatter
 //   kv_sync_kernel           reference full-frame K/V merge + update
 //   out_cache_sync_kernel    reference output-cache merge + valid update
@@ -486,6 +487,55 @@ __global__ void __launch_bounds__(256) restore_rows_kernel(const __grid_constant
         for (int32_t e = lane; e < row_vec; e += 32) {
             dk[e] = s[e];
             dv[e] = s[row_vec + e];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Executed rows across PCIe for a frame whose tensors live in page-locked host memory: the rows
+// idx[0..M) of up to three tensors move between the host and the device at the same row position
+// (dst row i = src row i), so only executed rows cross the bus. One side is mapped host memory read
+// or written by the SMs directly (zero-copy); a warp moves one row of one tensor, each lane four
+// 16-byte vectors at a time with the loads issued before the stores, which keeps enough reads in
+// flight to cover the PCIe round trip. 128-thread CTAs at under 40 registers fit next to a
+// persistent attention CTA on the same SM, so the next frame's upload runs during this frame's
+// attention.
+// ---------------------------------------------------------------------------------------------
+constexpr int kHostRowsThreads = 128;
+constexpr int kHostRowsUnroll = 4;
+
+struct HostRowsArgs {
+    const uint4* src[3];
+    uint4* dst[3];
+    const int32_t* idx;
+    const int32_t* count;
+    int64_t ld_vec;        // row stride of every tensor, 16-byte units
+    int32_t row_vec;       // 16-byte units per row
+    int32_t n_tensors, n_tokens;
+};
+
+__global__ void __launch_bounds__(kHostRowsThreads) host_rows_kernel(const __grid_constant__ HostRowsArgs a) {
+    pdl_wait();   // idx / count of the compaction; for the download, the frame's output rows
+    const int32_t M = min(*a.count, a.n_tokens);
+    const int lane = threadIdx.x & 31;
+    const int32_t warps = kHostRowsThreads / 32;
+    const int64_t items = (int64_t)M * a.n_tensors;
+    for (int64_t it = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); it < items;
+         it += (int64_t)gridDim.x * warps) {
+        const int32_t m = (int32_t)(it / a.n_tensors);
+        const int32_t t = (int32_t)(it - (int64_t)m * a.n_tensors);
+        const int32_t i = a.idx[m];
+        if (i < 0 || i >= a.n_tokens) continue;
+        const uint4* s = a.src[t] + (int64_t)i * a.ld_vec;
+        uint4* d = a.dst[t] + (int64_t)i * a.ld_vec;
+        for (int32_t j0 = lane; j0 < a.row_vec; j0 += 32 * kHostRowsUnroll) {
+            uint4 v[kHostRowsUnroll];
+#pragma unroll
+            for (int u = 0; u < kHostRowsUnroll; ++u)
+                if (j0 + 32 * u < a.row_vec) v[u] = s[j0 + 32 * u];
+#pragma unroll
+            for (int u = 0; u < kHostRowsUnroll; ++u)
+                if (j0 + 32 * u < a.row_vec) d[j0 + 32 * u] = v[u];
         }
     }
 }

@@ -30,6 +30,7 @@ EXPORTED = [
     "fxr_mark_updated", "fxr_gather_norm_rope", "fxr_attention_active", "fxr_restore_rows",
     "fxr_gather_rows", "fxr_scatter_rows", "fxr_kv_sync", "fxr_output_cache_sync",
     "fxr_rms_norm", "fxr_attention_f32_bhsd", "fxr_frame_forward", "fxr_frame_forward_noalloc",
+    "fxr_frame_host_workspace_size", "fxr_frame_forward_host",
     "fxr_plugin_create", "fxr_plugin_clone", "fxr_plugin_destroy", "fxr_plugin_name",
     "fxr_plugin_version", "fxr_plugin_namespace", "fxr_plugin_fields", "fxr_plugin_output_desc",
     "fxr_plugin_supports", "fxr_plugin_configure", "fxr_plugin_workspace_size",
@@ -189,6 +190,9 @@ def load(path: str | None = None) -> ctypes.CDLL:
     L.fxr_frame_forward.argtypes = [ctypes.POINTER(FrameDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]
     L.fxr_frame_forward_noalloc.argtypes = [ctypes.POINTER(FrameDesc)] + [_vp] * 12
+    L.fxr_frame_host_workspace_size.argtypes = [ctypes.POINTER(FrameDesc)]
+    L.fxr_frame_host_workspace_size.restype = ctypes.c_size_t
+    L.fxr_frame_forward_host.argtypes = [ctypes.POINTER(FrameDesc)] + [_vp] * 12 + [ctypes.c_size_t, _vp]
     L.fxr_qkv_project.argtypes = [ctypes.POINTER(FrameDesc), _vp, _i64, _i32, _vp, _vp, _vp, _vp,
                                   _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]
     L.fxr_ln_modulate_rows.argtypes = [_i32, _vp, _i64, _i32, _vp, _vp, _i32, _i32, _i32, _vp, _vp,
@@ -392,6 +396,23 @@ def rms_norm(x, y, w, eps: float = 1e-6, stream=None):
     dim = x.shape[-1]
     _check(load().fxr_rms_norm(_ptr(x), _ptr(y), _ptr(w), eps, x.numel() // dim, dim,
                                dtype_code(x.dtype), _stream(stream)))
+
+
+def frame_host_workspace_size(cfg: FrameConfig) -> int:
+    d = cfg.desc()
+    return int(load().fxr_frame_host_workspace_size(ctypes.byref(d)))
+
+
+def frame_forward_host(cfg: FrameConfig, host_q, host_k, host_v, host_mask, valid, pos, norm_q, norm_k,
+                       cache_k, cache_v, host_out, workspace, stream=None):
+    """fxr_frame_forward_host: Q, K, V, mask and out are page-locked CPU tensors (pin_memory());
+    only the executed rows cross PCIe. Asynchronous on `stream`."""
+    d = cfg.desc()
+    _check(load().fxr_frame_forward_host(ctypes.byref(d), _ptr(host_q), _ptr(host_k), _ptr(host_v),
+                                         _ptr(host_mask), _ptr(valid), _ptr(pos), _ptr(norm_q),
+                                         _ptr(norm_k), _ptr(cache_k), _ptr(cache_v), _ptr(host_out),
+                                         _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                         _stream(stream)))
 
 
 def frame_forward(cfg: FrameConfig, q, k, v, mask, valid, pos, norm_q, norm_k, cache_k, cache_v,

@@ -183,6 +183,37 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc,
                           void* cache_k, void* cache_v, void* out,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/* One frame whose per-frame tensors live in page-locked host memory, for a streaming host that
+ * produces each frame's projections on the CPU side and wants the output back. The reference moves
+ * such tensors whole with Tensor::upload / Tensor::download (src/utils/tensor.cpp:50-56); here only
+ * the executed rows cross PCIe:
+ *   1. the mask is copied to the workspace and compacted on the device;
+ *   2. a zero-copy kernel reads the executed tokens' Q, K, V rows from host memory into device
+ *      staging rows (other rows are never read: the attention takes their K/V from the cache);
+ *   3. the frame runs as fxr_frame_forward on the staging buffers;
+ *   4. a zero-copy kernel writes the executed tokens' output rows into host_out.
+ * Arguments:
+ *   host_q, host_k, host_v  [n_tokens, n_heads * head_dim] dtype, page-locked host memory mapped
+ *                           into the device's address space (cudaHostAlloc / cudaMallocHost memory
+ *                           always is under unified addressing; cudaHostRegister with the mapped
+ *                           flag); other memory is rejected with FXR_ERR_INVALID
+ *   host_mask               [n_tokens] int32 mask in host memory (read only; its preprocessed copy
+ *                           stays in the workspace)
+ *   host_out                [n_tokens, n_heads * head_dim] dtype, page-locked and mapped like
+ *                           host_q: the rows of executed tokens receive the attention output and
+ *                           every other row keeps what it held (the output cache of the previous frame)
+ *   valid, pos, norm_q, norm_k, cache_k, cache_v   device memory, as for fxr_frame_forward
+ *   workspace               at least fxr_frame_host_workspace_size(desc) bytes of device memory
+ * Asynchronous on `stream`; host_out is complete once the stream has passed this call, and the
+ * host buffers must stay untouched until then. Six kernel launches and one 4 * n_tokens byte copy. */
+size_t fxr_frame_host_workspace_size(const fxr_frame_desc* desc);
+int32_t fxr_frame_forward_host(const fxr_frame_desc* desc,
+                               const void* host_q, const void* host_k, const void* host_v,
+                               const int32_t* host_mask, const uint8_t* valid, const int32_t* pos,
+                               const float* norm_q, const float* norm_k,
+                               void* cache_k, void* cache_v, void* host_out,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
 /* fxr_frame_forward without a workspace argument, for callers that cannot allocate device memory
  * when they run a frame: for example a plugin enqueue inside an inference engine that owns every
  * device allocation, or a latency-critical loop that must not risk the device-wide
