@@ -797,7 +797,7 @@ static int32_t launch_host_rows(const void* const* src, void* const* dst, int n,
     a.row_vec = (int32_t)(row_bytes / 16);
     a.n_tensors = n;
     a.n_tokens = n_tokens;
-    const int grid = 2 * sm_count();
+    const int grid = std::min(fxr::kHostRowsCtas, sm_count());
     cudaError_t e = launch_pdl(fxr::host_rows_kernel, dim3(grid), dim3(fxr::kHostRowsThreads), 0, s, a);
     if (e != cudaSuccess) return cuda_status(e, "host_rows_kernel launch");
     return FXR_OK;

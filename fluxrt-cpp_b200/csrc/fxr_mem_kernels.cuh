@@ -495,14 +495,16 @@ __global__ void __launch_bounds__(256) restore_rows_kernel(const __grid_constant
 // Executed rows across PCIe for a frame whose tensors live in page-locked host memory: the rows
 // idx[0..M) of up to three tensors move between the host and the device at the same row position
 // (dst row i = src row i), so only executed rows cross the bus. One side is mapped host memory read
-// or written by the SMs directly (zero-copy); a warp moves one row of one tensor, each lane four
-// 16-byte vectors at a time with the loads issued before the stores, which keeps enough reads in
-// flight to cover the PCIe round trip. 128-thread CTAs at under 40 registers fit next to a
-// persistent attention CTA on the same SM, so the next frame's upload runs during this frame's
-// attention.
+// or written by the SMs directly (zero-copy); a warp moves one row of one tensor, each lane eight
+// 16-byte vectors at a time with the loads issued before the stores. 64 CTAs of 64 threads keep
+// 512 KB of reads in flight, enough to fill PCIe (one CTA per SM reaches the same rate as two), and
+// each CTA is small enough (under 3.6K registers) to sit beside a persistent gather or attention
+// CTA on its SM: the next frame's upload then runs under this frame's kernels instead of keeping
+// them off the SMs it holds.
 // ---------------------------------------------------------------------------------------------
-constexpr int kHostRowsThreads = 128;
-constexpr int kHostRowsUnroll = 4;
+constexpr int kHostRowsThreads = 64;
+constexpr int kHostRowsUnroll = 8;
+constexpr int kHostRowsCtas = 64;
 
 struct HostRowsArgs {
     const uint4* src[3];
