@@ -1185,10 +1185,32 @@ static int32_t check_block_stream(const fxr_block_stream& s, const char* which) 
     return FXR_OK;
 }
 
-int32_t fxr_double_block_forward(const fxr_frame_desc* desc, const fxr_double_block* blk, const void* x_in,
+// Device-side addresses of a host-buffer block's page-locked hidden states.
+struct BlockHostIo {
+    const void* x_in;
+    void* x_out;
+};
+
+static int32_t block_upload(const BlockHostIo* host, const void* x_in, int32_t C, size_t eb, const int32_t* idx,
+                            const int32_t* count, int32_t N, cudaStream_t s) {
+    if (!host) return FXR_OK;
+    const void* src[1] = {host->x_in};
+    void* dst[1] = {const_cast<void*>(x_in)};
+    return launch_host_rows(src, dst, 1, C, (int64_t)C * (int64_t)eb, eb, idx, count, N, s);
+}
+
+static int32_t block_download(const BlockHostIo* host, const void* x_out, int32_t C, size_t eb, const int32_t* idx,
+                              const int32_t* count, int32_t N, cudaStream_t s) {
+    if (!host) return FXR_OK;
+    const void* src[1] = {x_out};
+    void* dst[1] = {host->x_out};
+    return launch_host_rows(src, dst, 1, C, (int64_t)C * (int64_t)eb, eb, idx, count, N, s);
+}
+
+static int32_t double_block_impl(const fxr_frame_desc* desc, const fxr_double_block* blk, const void* x_in,
                                  void* x_out, int32_t* mask, uint8_t* valid, const int32_t* pos,
                                  void* cache_k, void* cache_v, void* workspace, size_t workspace_bytes,
-                                 void* stream) {
+                                 void* stream, const BlockHostIo* host) {
     int32_t st = check_desc(desc, true);
     if (st != FXR_OK) return st;
     if (!blk) return fail(FXR_ERR_INVALID, "null block");
@@ -1226,6 +1248,7 @@ int32_t fxr_double_block_forward(const fxr_frame_desc* desc, const fxr_double_bl
         if ((st = launch_compact_streams(ca, 1, N, b.split, stream, gemm, fxr::gemm::kSyncBytes, T)) != FXR_OK)
             return st;
     }
+    if ((st = block_upload(host, x_in, C, dtype_bytes(dt), idx, count, N, s)) != FXR_OK) return st;
     const fxr_block_stream* ss[2] = {&blk->txt, &blk->img};
     const int32_t r0[2] = {0, T}, r1[2] = {T, -1};
     const int first = T > 0 ? 0 : 1;
@@ -1311,9 +1334,18 @@ int32_t fxr_double_block_forward(const fxr_frame_desc* desc, const fxr_double_bl
         g.gate = w.gate;
         if ((st = fxr_rows_gemm(&g, idx, count, gemm, gemm_bytes, stream)) != FXR_OK) return st;
     }
+    if ((st = block_download(host, x_out, C, dtype_bytes(dt), idx, count, N, s)) != FXR_OK) return st;
     // 9. validity of the cache rows this frame updated
     if (valid) return fxr_mark_updated(mask, valid, T, N, stream);
     return FXR_OK;
+}
+
+int32_t fxr_double_block_forward(const fxr_frame_desc* desc, const fxr_double_block* blk, const void* x_in,
+                                 void* x_out, int32_t* mask, uint8_t* valid, const int32_t* pos,
+                                 void* cache_k, void* cache_v, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+    return double_block_impl(desc, blk, x_in, x_out, mask, valid, pos, cache_k, cache_v, workspace,
+                             workspace_bytes, stream, nullptr);
 }
 
 // ---- the single-stream block on the executed rows ----------------------------------------------
@@ -1321,10 +1353,10 @@ size_t fxr_single_block_workspace_size(const fxr_frame_desc* desc, int32_t mlp_h
     return fxr_double_block_workspace_size(desc, mlp_hidden);   // the same buffers
 }
 
-int32_t fxr_single_block_forward(const fxr_frame_desc* desc, const fxr_single_block* blk, const void* x_in,
+static int32_t single_block_impl(const fxr_frame_desc* desc, const fxr_single_block* blk, const void* x_in,
                                  void* x_out, int32_t* mask, uint8_t* valid, const int32_t* pos,
                                  void* cache_k, void* cache_v, void* workspace, size_t workspace_bytes,
-                                 void* stream) {
+                                 void* stream, const BlockHostIo* host) {
     int32_t st = check_desc(desc, true);
     if (st != FXR_OK) return st;
     if (!blk) return fail(FXR_ERR_INVALID, "null block");
@@ -1361,6 +1393,7 @@ int32_t fxr_single_block_forward(const fxr_frame_desc* desc, const fxr_single_bl
         if ((st = launch_compact_streams(ca, 1, N, b.split, stream, b.gemm, fxr::gemm::kSyncBytes, T)) != FXR_OK)
             return st;
     }
+    if ((st = block_upload(host, x_in, C, dtype_bytes(dt), idx, count, N, s)) != FXR_OK) return st;
     if ((st = fxr_ln_modulate_rows(dt, x_in, C, C, idx, count, 0, -1, N, blk->scale, blk->shift, blk->ln_eps,
                                    b.xn, C, stream)) != FXR_OK)
         return st;
@@ -1411,8 +1444,112 @@ int32_t fxr_single_block_forward(const fxr_frame_desc* desc, const fxr_single_bl
         g.gate = blk->gate;
         if ((st = fxr_rows_gemm(&g, idx, count, b.gemm, gemm_bytes, stream)) != FXR_OK) return st;
     }
+    if ((st = block_download(host, x_out, C, dtype_bytes(dt), idx, count, N, s)) != FXR_OK) return st;
     if (valid) return fxr_mark_updated(mask, valid, T, N, stream);
     return FXR_OK;
+}
+
+int32_t fxr_single_block_forward(const fxr_frame_desc* desc, const fxr_single_block* blk, const void* x_in,
+                                 void* x_out, int32_t* mask, uint8_t* valid, const int32_t* pos,
+                                 void* cache_k, void* cache_v, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+    return single_block_impl(desc, blk, x_in, x_out, mask, valid, pos, cache_k, cache_v, workspace,
+                             workspace_bytes, stream, nullptr);
+}
+
+// ---- blocks with host-resident hidden states ----------------------------------------------------
+// Staging at the start of the workspace: the mask copy, x_in and x_out rows [N, C]; the block's own
+// workspace follows.
+struct BlockHostStage {
+    int32_t* mask;
+    void* x_in;
+    void* x_out;
+    size_t total;
+};
+
+static BlockHostStage carve_block_host(const fxr_frame_desc* d, void* ws) {
+    BlockHostStage h{};
+    const size_t N = (size_t)(d->n_tokens > 0 ? d->n_tokens : 1);
+    const size_t row = (size_t)d->n_heads * d->head_dim * dtype_bytes(d->dtype);
+    char* b = static_cast<char*>(ws);
+    size_t off = 0;
+    h.mask = reinterpret_cast<int32_t*>(b ? b + off : nullptr);
+    off = align_up(off + N * sizeof(int32_t), 256);
+    h.x_in = b ? b + off : nullptr;
+    off = align_up(off + N * row, 256);
+    h.x_out = b ? b + off : nullptr;
+    off = align_up(off + N * row, 256);
+    h.total = off;
+    return h;
+}
+
+size_t fxr_block_host_workspace_size(const fxr_frame_desc* desc, int32_t mlp_hidden) {
+    const size_t inner = fxr_double_block_workspace_size(desc, mlp_hidden);
+    if (inner == 0) return 0;
+    return carve_block_host(desc, nullptr).total + inner;
+}
+
+// Validates the host side of a block call and stages it: the mask is copied, the host rows'
+// device-side addresses returned in io; *inner / *inner_bytes receive the block's workspace.
+static int32_t block_host_stage(const fxr_frame_desc* desc, int32_t mlp_hidden, const void* host_x_in,
+                                void* host_x_out, const int32_t* host_mask, void* workspace, size_t workspace_bytes,
+                                void* stream, BlockHostStage* h, BlockHostIo* io, void** inner, size_t* inner_bytes) {
+    int32_t st = check_desc(desc, true);
+    if (st != FXR_OK) return st;
+    if (!workspace) return fail(FXR_ERR_INVALID, "null workspace");
+    if (!aligned16(workspace)) return fail(FXR_ERR_INVALID, "workspace must be 16-byte aligned");
+    *h = carve_block_host(desc, workspace);
+    if (mlp_hidden <= 0) return fail(FXR_ERR_UNSUPPORTED, "mlp_hidden %d", mlp_hidden);
+    const size_t need = h->total + carve_block(desc, mlp_hidden, nullptr).total;
+    if (workspace_bytes < need) return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, need);
+    if (!host_x_in || !host_x_out || !host_mask) return fail(FXR_ERR_INVALID, "null host buffer");
+    const size_t bytes = (size_t)desc->n_tokens * desc->n_heads * desc->head_dim * dtype_bytes(desc->dtype);
+    io->x_in = mapped_host_range(host_x_in, bytes);
+    io->x_out = const_cast<void*>(mapped_host_range(host_x_out, bytes));
+    if (!io->x_in || !io->x_out)
+        return fail(FXR_ERR_INVALID, "host_x_in / host_x_out must be page-locked host memory mapped into the device "
+                                     "address space");
+    if (!aligned16(io->x_in) || !aligned16(io->x_out)) return fail(FXR_ERR_INVALID, "host buffers must be 16-byte aligned");
+    cudaError_t e = cudaMemcpyAsync(h->mask, host_mask, (size_t)desc->n_tokens * sizeof(int32_t),
+                                    cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_status(e, "mask copy");
+    *inner = static_cast<char*>(workspace) + h->total;
+    *inner_bytes = workspace_bytes - h->total;
+    return FXR_OK;
+}
+
+int32_t fxr_double_block_forward_host(const fxr_frame_desc* desc, const fxr_double_block* blk,
+                                      const void* host_x_in, void* host_x_out, const int32_t* host_mask,
+                                      uint8_t* valid, const int32_t* pos, void* cache_k, void* cache_v,
+                                      void* workspace, size_t workspace_bytes, void* stream) {
+    if (!blk) return fail(FXR_ERR_INVALID, "null block");
+    if (desc && desc->n_tokens == 0) return check_desc(desc, true);
+    BlockHostStage h{};
+    BlockHostIo io{};
+    void* inner = nullptr;
+    size_t inner_bytes = 0;
+    int32_t st = block_host_stage(desc, blk->mlp_hidden, host_x_in, host_x_out, host_mask, workspace, workspace_bytes,
+                                  stream, &h, &io, &inner, &inner_bytes);
+    if (st != FXR_OK) return st;
+    return double_block_impl(desc, blk, h.x_in, h.x_out, h.mask, valid, pos, cache_k, cache_v, inner, inner_bytes,
+                             stream, &io);
+}
+
+int32_t fxr_single_block_forward_host(const fxr_frame_desc* desc, const fxr_single_block* blk,
+                                      const void* host_x_in, void* host_x_out, const int32_t* host_mask,
+                                      uint8_t* valid, const int32_t* pos, void* cache_k, void* cache_v,
+                                      void* workspace, size_t workspace_bytes, void* stream) {
+    if (!blk) return fail(FXR_ERR_INVALID, "null block");
+    if (desc && desc->n_tokens == 0) return check_desc(desc, true);
+    BlockHostStage h{};
+    BlockHostIo io{};
+    void* inner = nullptr;
+    size_t inner_bytes = 0;
+    int32_t st = block_host_stage(desc, blk->mlp_hidden, host_x_in, host_x_out, host_mask, workspace, workspace_bytes,
+                                  stream, &h, &io, &inner, &inner_bytes);
+    if (st != FXR_OK) return st;
+    return single_block_impl(desc, blk, h.x_in, h.x_out, h.mask, valid, pos, cache_k, cache_v, inner, inner_bytes,
+                             stream, &io);
 }
 
 size_t fxr_batch_workspace_size(const fxr_frame_desc* desc, int32_t n_streams) {

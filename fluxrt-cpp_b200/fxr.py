@@ -42,6 +42,7 @@ EXPORTED = [
     "fxr_ln_modulate_rows", "fxr_rows_gemm_scratch_size", "fxr_rows_gemm",
     "fxr_double_block_workspace_size", "fxr_double_block_forward",
     "fxr_single_block_workspace_size", "fxr_single_block_forward",
+    "fxr_block_host_workspace_size", "fxr_double_block_forward_host", "fxr_single_block_forward_host",
 ]
 
 FXR_ACT_NONE, FXR_ACT_GELU_TANH = 0, 1
@@ -208,6 +209,10 @@ def load(path: str | None = None) -> ctypes.CDLL:
     L.fxr_double_block_workspace_size.restype = ctypes.c_size_t
     L.fxr_double_block_forward.argtypes = [ctypes.POINTER(FrameDesc), ctypes.POINTER(DoubleBlock)] + \
         [_vp] * 8 + [ctypes.c_size_t, _vp]
+    L.fxr_double_block_forward_host.argtypes = L.fxr_double_block_forward.argtypes
+    L.fxr_single_block_forward_host.argtypes = L.fxr_single_block_forward.argtypes
+    L.fxr_block_host_workspace_size.argtypes = [ctypes.POINTER(FrameDesc), _i32]
+    L.fxr_block_host_workspace_size.restype = ctypes.c_size_t
     L.fxr_batch_workspace_size.argtypes = [ctypes.POINTER(FrameDesc), _i32]
     L.fxr_batch_workspace_size.restype = ctypes.c_size_t
     L.fxr_frame_forward_batch.argtypes = [ctypes.POINTER(FrameDesc), _i32, ctypes.POINTER(StreamFrame),
@@ -754,16 +759,21 @@ def double_block_workspace_size(cfg: FrameConfig, mlp_hidden: int) -> int:
     return int(load().fxr_double_block_workspace_size(ctypes.byref(d), mlp_hidden))
 
 
+def block_host_workspace_size(cfg: FrameConfig, mlp_hidden: int) -> int:
+    d = cfg.desc()
+    return int(load().fxr_block_host_workspace_size(ctypes.byref(d), mlp_hidden))
+
+
 def double_block_forward(cfg: FrameConfig, txt: dict, img: dict, mlp_hidden: int, x_in, x_out, mask,
-                         valid, pos, cache_k, cache_v, workspace, ln_eps=1e-6, stream=None):
+                         valid, pos, cache_k, cache_v, workspace, ln_eps=1e-6, stream=None, host=False):
     """One double-stream block on the executed rows (fxr_double_block_forward). txt / img: dicts of
-    the fxr_block_stream fields (device tensors)."""
+    the fxr_block_stream fields (device tensors). host=True: x_in, x_out and mask are page-locked CPU
+    tensors (fxr_double_block_forward_host; workspace of block_host_workspace_size bytes)."""
     d = cfg.desc()
     blk = DoubleBlock(block_stream(**txt), block_stream(**img), mlp_hidden, ln_eps)
-    _check(load().fxr_double_block_forward(ctypes.byref(d), ctypes.byref(blk), _ptr(x_in), _ptr(x_out),
-                                           _ptr(mask), _ptr(valid), _ptr(pos), _ptr(cache_k),
-                                           _ptr(cache_v), _ptr(workspace), workspace.numel(),
-                                           _stream(stream)))
+    fn = load().fxr_double_block_forward_host if host else load().fxr_double_block_forward
+    _check(fn(ctypes.byref(d), ctypes.byref(blk), _ptr(x_in), _ptr(x_out), _ptr(mask), _ptr(valid),
+              _ptr(pos), _ptr(cache_k), _ptr(cache_v), _ptr(workspace), workspace.numel(), _stream(stream)))
 
 
 def single_block_workspace_size(cfg: FrameConfig, mlp_hidden: int) -> int:
@@ -772,15 +782,14 @@ def single_block_workspace_size(cfg: FrameConfig, mlp_hidden: int) -> int:
 
 
 def single_block_forward(cfg: FrameConfig, wts: dict, mlp_hidden: int, x_in, x_out, mask, valid, pos,
-                         cache_k, cache_v, workspace, ln_eps=1e-6, stream=None):
+                         cache_k, cache_v, workspace, ln_eps=1e-6, stream=None, host=False):
     """One single-stream block on the executed rows (fxr_single_block_forward). wts: dict of the
-    fxr_single_block weight fields (device tensors)."""
+    fxr_single_block weight fields (device tensors). host=True as for double_block_forward."""
     d = cfg.desc()
     blk = SingleBlock()
     for n in ("shift", "scale", "gate", "w_qkv_mlp", "b_qkv_mlp", "norm_q", "norm_k", "w_out", "b_out"):
         setattr(blk, n, _ptr(wts.get(n)))
     blk.mlp_hidden, blk.ln_eps = mlp_hidden, ln_eps
-    _check(load().fxr_single_block_forward(ctypes.byref(d), ctypes.byref(blk), _ptr(x_in), _ptr(x_out),
-                                           _ptr(mask), _ptr(valid), _ptr(pos), _ptr(cache_k),
-                                           _ptr(cache_v), _ptr(workspace), workspace.numel(),
-                                           _stream(stream)))
+    fn = load().fxr_single_block_forward_host if host else load().fxr_single_block_forward
+    _check(fn(ctypes.byref(d), ctypes.byref(blk), _ptr(x_in), _ptr(x_out), _ptr(mask), _ptr(valid),
+              _ptr(pos), _ptr(cache_k), _ptr(cache_v), _ptr(workspace), workspace.numel(), _stream(stream)))

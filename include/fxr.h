@@ -382,6 +382,24 @@ int32_t fxr_single_block_forward(const fxr_frame_desc* desc, const fxr_single_bl
                                  const int32_t* pos, void* cache_k, void* cache_v,
                                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* The two blocks with the hidden states in page-locked host memory (as fxr_frame_forward_host for
+ * the attention slice; the reference moves whole tensors, src/utils/tensor.cpp:50-56): host_mask
+ * (int32, read only) is copied to the workspace; after the compaction a zero-copy kernel reads the
+ * executed rows of host_x_in into device staging rows; the block runs on them; a zero-copy kernel
+ * writes the executed rows of x_out into host_x_out, whose other rows keep the previous frame's
+ * output. host_x_in / host_x_out: [n_tokens, C] page-locked and mapped (as for
+ * fxr_frame_forward_host, else FXR_ERR_INVALID); valid, pos and the caches are device memory.
+ * Workspace: fxr_block_host_workspace_size(desc, mlp_hidden) bytes, for either block. */
+size_t fxr_block_host_workspace_size(const fxr_frame_desc* desc, int32_t mlp_hidden);
+int32_t fxr_double_block_forward_host(const fxr_frame_desc* desc, const fxr_double_block* blk,
+                                      const void* host_x_in, void* host_x_out, const int32_t* host_mask,
+                                      uint8_t* valid, const int32_t* pos, void* cache_k, void* cache_v,
+                                      void* workspace, size_t workspace_bytes, void* stream);
+int32_t fxr_single_block_forward_host(const fxr_frame_desc* desc, const fxr_single_block* blk,
+                                      const void* host_x_in, void* host_x_out, const int32_t* host_mask,
+                                      uint8_t* valid, const int32_t* pos, void* cache_k, void* cache_v,
+                                      void* workspace, size_t workspace_bytes, void* stream);
+
 /* QKV projection of the executed tokens from token-major hidden states:
  *   [q | k | v][idx[m], :] = hidden[idx[m], :] . w_qkv^T (+ bias)   for m < *count
  * hidden: [n_tokens, ld_hidden] (k_dim columns, multiple of 64); w_qkv: [3C, k_dim] row-major

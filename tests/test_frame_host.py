@@ -106,3 +106,80 @@ def test_host_frame_rejects_unmapped_memory(cuda):
                                    bad, ws)
     torch.cuda.synchronize()
     assert fxr.check_device_error() == 0
+
+
+def test_host_block_argument_checks():
+    L = fxr.load()
+    cfg = fxr.FrameConfig(n_tokens=1280, n_text=256, n_heads=6)
+    d = cfg.desc()
+    blk = fxr.DoubleBlock()
+    blk.mlp_hidden, blk.ln_eps = 2304, 1e-6
+    args = lambda ws=16, ws_bytes=1 << 40, host=16: (ctypes.byref(d), ctypes.byref(blk), host, host, host, None,
+                                                     None, None, None, ws, ws_bytes, None)
+    for fn in (L.fxr_double_block_forward_host, ):
+        assert fn(*args(ws=None)) == fxr.FXR_ERR_INVALID
+        assert fn(*args(ws=8)) == fxr.FXR_ERR_INVALID
+        assert fn(*args(ws_bytes=1 << 20)) == fxr.FXR_ERR_WORKSPACE
+        assert fn(*args(host=None)) == fxr.FXR_ERR_INVALID
+    assert L.fxr_double_block_forward_host(ctypes.byref(d), None, *([None] * 7), 16, 1 << 40, None) \
+        == fxr.FXR_ERR_INVALID                                             # null block
+    ws = fxr.block_host_workspace_size(cfg, 2304)
+    assert ws >= fxr.double_block_workspace_size(cfg, 2304) + 1280 * 4 + 2 * 1280 * 768 * 2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kind", ["double", "single"])
+def test_host_blocks_match_device_blocks(cuda, kind):
+    """Two consecutive block frames from host buffers against the device entry: bit for bit."""
+    import torch
+    w = W.Workload("hblk_512px_h6", 32, 32, 256, n_heads=6, dtype="bf16", active=0.3)
+    N, T, C, D = w.n_tokens, w.n_text, w.n_heads * w.head_dim, w.head_dim
+    H = 3 * C
+    cfg = fxr.FrameConfig(n_tokens=N, n_text=T, n_heads=w.n_heads, dtype="bf16", rope_axes=w.rope_axes,
+                          rope_theta=w.rope_theta)
+    g = torch.Generator(device="cuda").manual_seed(31)
+    rw = lambda *shape, sd: (torch.randn(*shape, device="cuda", generator=g) * sd).bfloat16()
+    rf = lambda *shape, mu=0.0, sd=1.0: torch.randn(*shape, device="cuda", generator=g) * sd + mu
+    if kind == "double":
+        mk = lambda: {"shift": rf(C, sd=0.1), "scale": rf(C, sd=0.1), "gate": rf(C, mu=1.0, sd=0.2),
+                      "w_qkv": rw(3 * C, C, sd=C ** -0.5), "b_qkv": rf(3 * C, sd=0.05),
+                      "norm_q": rf(D, mu=1.0, sd=0.1), "norm_k": rf(D, mu=1.0, sd=0.1),
+                      "w_out": rw(C, C, sd=C ** -0.5), "b_out": rf(C, sd=0.05),
+                      "w_mlp0": rw(H, C, sd=C ** -0.5), "b_mlp0": rf(H, sd=0.05),
+                      "w_mlp2": rw(C, H, sd=H ** -0.5), "b_mlp2": rf(C, sd=0.05)}
+        txt, img = mk(), mk()
+        run = lambda *a, **k: fxr.double_block_forward(cfg, txt, img, H, *a, **k)
+    else:
+        wts = {"shift": rf(C, sd=0.1), "scale": rf(C, sd=0.1), "gate": rf(C, mu=1.0, sd=0.2),
+               "w_qkv_mlp": rw(3 * C + H, C, sd=C ** -0.5), "b_qkv_mlp": rf(3 * C + H, sd=0.05),
+               "norm_q": rf(D, mu=1.0, sd=0.1), "norm_k": rf(D, mu=1.0, sd=0.1),
+               "w_out": rw(C, C + H, sd=(C + H) ** -0.5), "b_out": rf(C, sd=0.05)}
+        run = lambda *a, **k: fxr.single_block_forward(cfg, wts, H, *a, **k)
+    f0 = W.make_frame(w, seed=41)
+    pos = torch.from_numpy(f0["pos"]).cuda()
+    d_ck = torch.from_numpy(f0["cache_k"]).cuda().bfloat16()
+    d_cv = torch.from_numpy(f0["cache_v"]).cuda().bfloat16()
+    h_ck, h_cv = d_ck.clone(), d_cv.clone()
+    d_valid = (torch.rand(N, device="cuda", generator=g) < 0.9).to(torch.uint8)
+    h_valid = d_valid.clone()
+    d_out = torch.randn(N, C, device="cuda", generator=g).bfloat16()
+    h_out = d_out.cpu().pin_memory()
+    ws_d = torch.empty(fxr.double_block_workspace_size(cfg, H), dtype=torch.uint8, device="cuda")
+    ws_h = torch.empty(fxr.block_host_workspace_size(cfg, H), dtype=torch.uint8, device="cuda")
+    for i in range(2):
+        mask = W.make_frame(w, seed=50 + i)["mask"].copy()
+        mask[T + 7] = 1
+        x = torch.randn(N, C, device="cuda", generator=g).bfloat16()
+        hx, hmask = x.cpu().pin_memory(), torch.from_numpy(mask).pin_memory()
+        before = h_out.clone()
+        dmask = torch.from_numpy(mask).cuda()
+        run(x, d_out, dmask, d_valid, pos, d_ck, d_cv, ws_d)
+        run(hx, h_out, hmask, h_valid, pos, h_ck, h_cv, ws_h, host=True)
+        torch.cuda.synchronize()
+        assert fxr.check_device_error() == 0
+        assert torch.equal(h_out, d_out.cpu()), f"{kind} frame {i}: block output differs"
+        assert torch.equal(h_ck, d_ck) and torch.equal(h_cv, d_cv), f"{kind} frame {i}: cache differs"
+        assert torch.equal(h_valid, d_valid)
+        executed = dmask.cpu() != 0                       # the device mask after preprocessing
+        assert torch.equal(h_out[~executed], before[~executed])
+        assert torch.equal(hmask, torch.from_numpy(mask))
