@@ -798,7 +798,12 @@ static int32_t launch_host_rows(const void* const* src, void* const* dst, int n,
     a.n_tensors = n;
     a.n_tokens = n_tokens;
     const int grid = std::min(fxr::kHostRowsCtas, sm_count());
-    cudaError_t e = launch_pdl(fxr::host_rows_kernel, dim3(grid), dim3(fxr::kHostRowsThreads), 0, s, a);
+    // the same L1 / shared-memory split as the persistent GEMM, gather and attention kernels: an SM
+    // runs CTAs of two kernels side by side only when their carveouts agree
+    cudaError_t e = cudaFuncSetAttribute(fxr::host_rows_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         (int)cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(host_rows_kernel)");
+    e = launch_pdl(fxr::host_rows_kernel, dim3(grid), dim3(fxr::kHostRowsThreads), 0, s, a);
     if (e != cudaSuccess) return cuda_status(e, "host_rows_kernel launch");
     return FXR_OK;
 }
