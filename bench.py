@@ -342,7 +342,7 @@ def run_ours(args):
            "algorithmic_bytes_per_launch": gb, "traffic": profile_traffic(f"gather_{w.name}")}
 
     # ---- end to end through the C ABI with host buffers ----
-    e2e = e2e_measure(cfg, w, frames, wss, stream, reps=max(5, min(50, args.steps)))
+    e2e = e2e_measure(cfg, w, frames, wss, stream, reps=max(5, min(50, args.steps)), world=world)
 
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
@@ -506,13 +506,15 @@ def _raw_restore(cfg, fr, idx, cnt, save):
                                            fr["cache_k"].data_ptr(), fr["cache_v"].data_ptr(), _s()))
 
 
-def e2e_measure(cfg, w, frames, wss, stream, reps: int):
+def e2e_measure(cfg, w, frames, wss, stream, reps: int, world: int = 1):
     """Frames through the C ABI with the frame's tensors in pinned HOST memory, the way a streaming
     host feeds them: fxr_frame_forward_host reads the mask and the executed tokens' Q, K, V rows
     from host memory and writes the executed output rows back, every frame. Frames alternate between
     two CUDA streams with their own caches and workspace, so one frame's transfers overlap the
     other's kernels. For comparison, the same frames with whole-tensor copies (Q, K, V, mask in,
-    the full output back) around fxr_frame_forward."""
+    the full output back) around fxr_frame_forward. With several ranks, every rank runs its frames at
+    the same time (a barrier before each timed loop) and the line reports the whole job: the slowest
+    rank's time per frame, every rank's work and bytes."""
     import torch
 
     import fxr
@@ -555,6 +557,9 @@ def e2e_measure(cfg, w, frames, wss, stream, reps: int):
         for i in range(4):
             one(i)
         torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+            torch.cuda.synchronize()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record(stream)
         for ln in lanes:
@@ -569,17 +574,26 @@ def e2e_measure(cfg, w, frames, wss, stream, reps: int):
 
     ms = timed(rows_frame)
     ms_full = timed(full_frame)
-    value = attn_flops(w, M) / (ms * 1e-3) / 1e12
     full_h2d = sum(t.numel() * t.element_size() for t in host.values())
-    return {"value": round(value, 2), "unit": "TFLOP/s", "us_per_frame": round(ms * 1e3, 1),
-            "h2d_bytes_per_step": int(3 * M * row_bytes + 4 * w.n_tokens),
-            "d2h_bytes_per_step": int(M * row_bytes),
+    full_d2h = fr0["out"].numel() * fr0["out"].element_size()
+    tot = [attn_flops(w, M), 3 * M * row_bytes + 4 * w.n_tokens, M * row_bytes, full_h2d, full_d2h]
+    if world > 1:
+        t = torch.tensor([ms, ms_full], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, ms_full = float(t[0]), float(t[1])
+        f = torch.tensor(tot, dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(f, op=torch.distributed.ReduceOp.SUM)
+        tot = [float(x) for x in f.tolist()]
+    value = tot[0] / (ms * 1e-3) / 1e12
+    return {"value": round(value, 2), "unit": "TFLOP/s", "us_per_frame": round(ms * 1e3, 1), "ranks": world,
+            "h2d_bytes_per_step": int(tot[1]),
+            "d2h_bytes_per_step": int(tot[2]),
             "path": "fxr_frame_forward_host via ctypes: pinned host Q/K/V/mask/out, only executed rows "
                     "cross PCIe (zero-copy row kernels), frames alternating over two streams",
             "full_frame_copies": {"us_per_frame": round(ms_full * 1e3, 1),
-                                  "value": round(attn_flops(w, M) / (ms_full * 1e-3) / 1e12, 2),
-                                  "h2d_bytes_per_step": int(full_h2d),
-                                  "d2h_bytes_per_step": int(fr0["out"].numel() * fr0["out"].element_size()),
+                                  "value": round(tot[0] / (ms_full * 1e-3) / 1e12, 2),
+                                  "h2d_bytes_per_step": int(tot[3]),
+                                  "d2h_bytes_per_step": int(tot[4]),
                                   "path": "whole-tensor copies in and out around fxr_frame_forward"}}
 
 
@@ -1272,6 +1286,9 @@ def run_block(args):
         for i in range(4):
             one(i)
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize()
         reps = max(6, min(30, args.steps))
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record(stream)
@@ -1289,15 +1306,24 @@ def run_block(args):
     full_ms = timed(one_full)
     if fxr.check_device_error() != 0:
         raise RuntimeError("device error during the end-to-end frames")
-    e2e = {"value": round(1e3 / e2e_ms, 2), "unit": "frames/s", "us_per_frame": round(e2e_ms * 1e3, 1),
-           "h2d_bytes_per_step": int(M_exec * C * 2 + host_m.numel() * 4),
-           "d2h_bytes_per_step": int(M_exec * C * 2),
+    # whole job: the slowest rank's time per frame, every rank's frames and bytes
+    tot = [M_exec * C * 2 + host_m.numel() * 4, M_exec * C * 2, host_x.numel() * 2 + host_m.numel() * 4,
+           host_o[0].numel() * 2]
+    if world > 1:
+        t = torch.tensor([e2e_ms, full_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms, full_ms = float(t[0]), float(t[1])
+        f = torch.tensor(tot, dtype=torch.float64, device=device)
+        dist.all_reduce(f, op=dist.ReduceOp.SUM)
+        tot = [float(x) for x in f.tolist()]
+    e2e = {"value": round(1e3 / e2e_ms * world, 2), "unit": "frames/s", "us_per_frame": round(e2e_ms * 1e3, 1),
+           "ranks": world, "h2d_bytes_per_step": int(tot[0]), "d2h_bytes_per_step": int(tot[1]),
            "path": "fxr_double_block_forward_host via ctypes: pinned host x_in / mask / x_out, only the "
                    "executed rows cross PCIe, frames alternating over two streams",
            "full_frame_copies": {"us_per_frame": round(full_ms * 1e3, 1),
-                                 "value": round(1e3 / full_ms, 2),
-                                 "h2d_bytes_per_step": int(host_x.numel() * 2 + host_m.numel() * 4),
-                                 "d2h_bytes_per_step": int(host_o[0].numel() * 2),
+                                 "value": round(1e3 / full_ms * world, 2),
+                                 "h2d_bytes_per_step": int(tot[2]),
+                                 "d2h_bytes_per_step": int(tot[3]),
                                  "path": "whole-tensor copies around fxr_double_block_forward"}}
     out = {
         "metric": BLOCK_METRIC, "value": round(1e3 / ms * world, 2), "unit": "frames/s", "n_gpus": world,
