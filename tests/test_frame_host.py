@@ -116,15 +116,19 @@ def test_host_block_argument_checks():
     blk.mlp_hidden, blk.ln_eps = 2304, 1e-6
     args = lambda ws=16, ws_bytes=1 << 40, host=16: (ctypes.byref(d), ctypes.byref(blk), host, host, host, None,
                                                      None, None, None, ws, ws_bytes, None)
-    for fn in (L.fxr_double_block_forward_host, ):
-        assert fn(*args(ws=None)) == fxr.FXR_ERR_INVALID
-        assert fn(*args(ws=8)) == fxr.FXR_ERR_INVALID
-        assert fn(*args(ws_bytes=1 << 20)) == fxr.FXR_ERR_WORKSPACE
-        assert fn(*args(host=None)) == fxr.FXR_ERR_INVALID
-    assert L.fxr_double_block_forward_host(ctypes.byref(d), None, *([None] * 7), 16, 1 << 40, None) \
-        == fxr.FXR_ERR_INVALID                                             # null block
+    sblk = fxr.SingleBlock()
+    sblk.mlp_hidden, sblk.ln_eps = 2304, 1e-6
+    sargs = lambda ws=16, ws_bytes=1 << 40, host=16: (ctypes.byref(d), ctypes.byref(sblk), host, host, host,
+                                                      None, None, None, None, ws, ws_bytes, None)
+    for fn, a in ((L.fxr_double_block_forward_host, args), (L.fxr_single_block_forward_host, sargs)):
+        assert fn(*a(ws=None)) == fxr.FXR_ERR_INVALID
+        assert fn(*a(ws=8)) == fxr.FXR_ERR_INVALID
+        assert fn(*a(ws_bytes=1 << 20)) == fxr.FXR_ERR_WORKSPACE
+        assert fn(*a(host=None)) == fxr.FXR_ERR_INVALID
+        assert fn(ctypes.byref(d), None, *([None] * 7), 16, 1 << 40, None) == fxr.FXR_ERR_INVALID  # null block
     ws = fxr.block_host_workspace_size(cfg, 2304)
     assert ws >= fxr.double_block_workspace_size(cfg, 2304) + 1280 * 4 + 2 * 1280 * 768 * 2
+    assert fxr.block_host_workspace_size(cfg, 0) == 0                       # no MLP width: no size
 
 
 @pytest.mark.gpu
