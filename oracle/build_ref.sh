@@ -7,6 +7,10 @@ set -euo pipefail
 here="$(cd "$(dirname "$0")" && pwd)"
 ref="${FXR_REFERENCE_ROOT:-/root/reference}"
 src="$ref/src/inference"
+if [[ ! -d "$src" ]]; then
+  echo "reference sources not present ($ref): oracle/_ref not built"
+  exit 0
+fi
 out="$here/_ref"
 mkdir -p "$out"
 nvcc -gencode arch=compute_100a,code=sm_100a -O3 -std=c++17 -Xcompiler -fPIC -shared \
