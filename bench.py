@@ -1403,37 +1403,11 @@ def single_block_report(args, w, cfg, wts, sets, run, H, ms, fl, M_avg, clk, pk,
 
 
 def cpu_block_sample(w, H: int, seed: int, rows: int = 256) -> dict:
-    """The reference block's fp32 math on the host cores as the reference runs it, densely on every
-    token (flux2_double_block_plugin.cpp:330-460): LayerNorm + modulation and Q/K/V of all N
-    tokens, then QK-RMSNorm, attention, MLP and out-projection of a sample of `rows` query tokens
-    over all N keys, scaled to N rows. numpy BLAS; returns seconds per frame."""
-    rng = np.random.default_rng(seed)
-    N, C = w.n_tokens, w.n_heads * HEAD_DIM
-    f = lambda *shape, sd=1.0: (rng.standard_normal(shape, dtype=np.float32) * sd)
-    x = f(N, C)
-    wq, wo, w0, w2 = f(3 * C, C, sd=C ** -0.5), f(C, C, sd=C ** -0.5), f(H, C, sd=C ** -0.5), f(C, H, sd=H ** -0.5)
-    t0 = time.perf_counter()
-    mean = x.mean(1, keepdims=True)
-    xn = (x - mean) / np.sqrt(((x - mean) ** 2).mean(1, keepdims=True) + 1e-6)
-    qkv = xn @ wq.T
-    t_all = time.perf_counter() - t0
-    sel = rng.choice(N, size=rows, replace=False)
-    t1 = time.perf_counter()
-    q = qkv[sel, :C].reshape(rows, w.n_heads, HEAD_DIM)
-    k = qkv[:, C:2 * C].reshape(N, w.n_heads, HEAD_DIM)
-    v = qkv[:, 2 * C:].reshape(N, w.n_heads, HEAD_DIM)
-    q = q / np.sqrt((q ** 2).mean(-1, keepdims=True) + 1e-6)
-    k = k / np.sqrt((k ** 2).mean(-1, keepdims=True) + 1e-6)
-    o = np.empty((rows, w.n_heads, HEAD_DIM), np.float32)
-    for h in range(w.n_heads):
-        s = (q[:, h] @ k[:, h].T) / np.sqrt(HEAD_DIM)
-        s = np.exp(s - s.max(1, keepdims=True))
-        o[:, h] = (s / s.sum(1, keepdims=True)) @ v[:, h]
-    hh = xn[sel] @ w0.T
-    hh = 0.5 * hh * (1 + np.tanh(0.7978845608 * (hh + 0.044715 * hh ** 3)))
-    _ = x[sel] + o.reshape(rows, C) @ wo.T + hh @ w2.T
-    t_rows = time.perf_counter() - t1
-    return {"seconds_per_frame": t_all + t_rows * N / rows, "rows": rows}
+    """One dense fp32 frame of the reference block on the host cores (the oracle's
+    dense_block_sample); returns seconds per frame."""
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import oracle as O
+    return O.dense_block_sample(w.n_tokens, w.n_heads, HEAD_DIM, H, seed, rows)
 
 
 def cpu_block_baseline(w, H: int, seed: int) -> dict:
@@ -1447,7 +1421,7 @@ def cpu_block_baseline(w, H: int, seed: int) -> dict:
     return {"value": round(1.0 / spf, 4), "unit": "frames/s", "cores": cores, "kind": "port",
             "sample": f"one dense fp32 frame of {w.name}: LayerNorm + Q/K/V of all {w.n_tokens} tokens, "
                       f"attention/MLP/out-projection of {s['rows']} sampled query tokens over all keys "
-                      f"scaled to {w.n_tokens} (numpy BLAS)",
+                      f"scaled to {w.n_tokens} (numpy BLAS, oracle dense_block_sample)",
             "seconds_per_frame": round(spf, 3)}
 
 

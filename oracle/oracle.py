@@ -326,3 +326,40 @@ def ref_kernels():
     L.ref_cache_sync_kv.argtypes = [vp, vp, vp, vp, ctypes.c_int, ctypes.c_int, vp]
     _ref_lib = L
     return L
+
+
+def dense_block_sample(n_tokens: int, n_heads: int, head_dim: int, mlp_hidden: int, seed: int,
+                       rows: int = 256) -> dict:
+    """The reference double block's fp32 math timed on the host cores as the reference runs it,
+    densely on every token (flux2_double_block_plugin.cpp:330-460): LayerNorm and Q/K/V of all N
+    tokens, then QK-RMSNorm, attention, the tanh-GELU MLP and the out-projection of a sample of
+    `rows` query tokens over all N keys, scaled to N rows. numpy BLAS on seeded random data; the CPU
+    baseline of the block benchmark, not a checker. Returns seconds per frame."""
+    import time
+    rng = np.random.default_rng(seed)
+    N, C, D, H = n_tokens, n_heads * head_dim, head_dim, mlp_hidden
+    f = lambda *shape, sd=1.0: (rng.standard_normal(shape, dtype=np.float32) * sd)
+    x = f(N, C)
+    wq, wo, w0, w2 = f(3 * C, C, sd=C ** -0.5), f(C, C, sd=C ** -0.5), f(H, C, sd=C ** -0.5), f(C, H, sd=H ** -0.5)
+    t0 = time.perf_counter()
+    mean = x.mean(1, keepdims=True)
+    xn = (x - mean) / np.sqrt(((x - mean) ** 2).mean(1, keepdims=True) + 1e-6)
+    qkv = xn @ wq.T
+    t_all = time.perf_counter() - t0
+    sel = rng.choice(N, size=rows, replace=False)
+    t1 = time.perf_counter()
+    q = qkv[sel, :C].reshape(rows, n_heads, D)
+    k = qkv[:, C:2 * C].reshape(N, n_heads, D)
+    v = qkv[:, 2 * C:].reshape(N, n_heads, D)
+    q = q / np.sqrt((q ** 2).mean(-1, keepdims=True) + 1e-6)
+    k = k / np.sqrt((k ** 2).mean(-1, keepdims=True) + 1e-6)
+    o = np.empty((rows, n_heads, D), np.float32)
+    for h in range(n_heads):
+        s = (q[:, h] @ k[:, h].T) / np.sqrt(D)
+        s = np.exp(s - s.max(1, keepdims=True))
+        o[:, h] = (s / s.sum(1, keepdims=True)) @ v[:, h]
+    hh = xn[sel] @ w0.T
+    hh = 0.5 * hh * (1 + np.tanh(0.7978845608 * (hh + 0.044715 * hh ** 3)))
+    _ = x[sel] + o.reshape(rows, C) @ wo.T + hh @ w2.T
+    t_rows = time.perf_counter() - t1
+    return {"seconds_per_frame": t_all + t_rows * N / rows, "rows": rows}
