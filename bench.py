@@ -35,6 +35,21 @@ HEAD_DIM = 128
 L2_BYTES = 126 * 1024 * 1024
 
 
+def whole_job(max_vals, sum_vals, world: int, device):
+    """Whole-job figures of a multi-rank run: the max over ranks of each of `max_vals` (times) and
+    the sum over ranks of each of `sum_vals` (work, bytes), as two lists of floats. Every rank must
+    call it at the same point (two all-reduces). With one rank the inputs come back unchanged."""
+    if world <= 1:
+        return [float(x) for x in max_vals], [float(x) for x in sum_vals]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(x) for x in max_vals], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    f = torch.tensor([float(x) for x in sum_vals], dtype=torch.float64, device=device)
+    dist.all_reduce(f, op=dist.ReduceOp.SUM)
+    return [float(x) for x in t.tolist()], [float(x) for x in f.tolist()]
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -308,15 +323,7 @@ def run_ours(args):
     clk = clocks.stop()
     t_ms = e0.elapsed_time(e1)
     flops_rank = sum(attn_flops(w, frames[i % n_sets]["M"]) for i in range(args.steps))
-    if world > 1:
-        t = torch.tensor([t_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_ms = float(t.item())
-        f = torch.tensor([flops_rank], dtype=torch.float64, device=device)
-        dist.all_reduce(f, op=dist.ReduceOp.SUM)
-        flops_total = float(f.item())
-    else:
-        flops_total = flops_rank
+    (t_ms,), (flops_total,) = whole_job([t_ms], [flops_rank], world, device)
     if fxr.check_device_error() != 0:
         raise RuntimeError("device error during the timed region")
     ms_per_step = t_ms / args.steps
@@ -577,13 +584,7 @@ def e2e_measure(cfg, w, frames, wss, stream, reps: int, world: int = 1):
     full_h2d = sum(t.numel() * t.element_size() for t in host.values())
     full_d2h = fr0["out"].numel() * fr0["out"].element_size()
     tot = [attn_flops(w, M), 3 * M * row_bytes + 4 * w.n_tokens, M * row_bytes, full_h2d, full_d2h]
-    if world > 1:
-        t = torch.tensor([ms, ms_full], dtype=torch.float64, device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, ms_full = float(t[0]), float(t[1])
-        f = torch.tensor(tot, dtype=torch.float64, device="cuda")
-        torch.distributed.all_reduce(f, op=torch.distributed.ReduceOp.SUM)
-        tot = [float(x) for x in f.tolist()]
+    (ms, ms_full), tot = whole_job([ms, ms_full], tot, world, "cuda")
     value = tot[0] / (ms * 1e-3) / 1e12
     return {"value": round(value, 2), "unit": "TFLOP/s", "us_per_frame": round(ms * 1e3, 1), "ranks": world,
             "h2d_bytes_per_step": int(tot[1]),
@@ -1309,13 +1310,7 @@ def run_block(args):
     # whole job: the slowest rank's time per frame, every rank's frames and bytes
     tot = [M_exec * C * 2 + host_m.numel() * 4, M_exec * C * 2, host_x.numel() * 2 + host_m.numel() * 4,
            host_o[0].numel() * 2]
-    if world > 1:
-        t = torch.tensor([e2e_ms, full_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms, full_ms = float(t[0]), float(t[1])
-        f = torch.tensor(tot, dtype=torch.float64, device=device)
-        dist.all_reduce(f, op=dist.ReduceOp.SUM)
-        tot = [float(x) for x in f.tolist()]
+    (e2e_ms, full_ms), tot = whole_job([e2e_ms, full_ms], tot, world, device)
     e2e = {"value": round(1e3 / e2e_ms * world, 2), "unit": "frames/s", "us_per_frame": round(e2e_ms * 1e3, 1),
            "ranks": world, "h2d_bytes_per_step": int(tot[0]), "d2h_bytes_per_step": int(tot[1]),
            "path": "fxr_double_block_forward_host via ctypes: pinned host x_in / mask / x_out, only the "
