@@ -70,6 +70,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--no-ref-cuda", action="store_true",
+                    help="reference arm: skip timing the reference's own CUDA kernels")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--split", choices=["replicas", "heads", "heads_nccl"], default=None,
                     help="multi-GPU mode: independent streams per GPU (default except c5) or one "
@@ -205,6 +207,23 @@ def make_device_frame(w, seed: int, device):
         "M": int((mask != 0).sum()),
     }
     return fr
+
+
+def bench_config(w, M_avg: float, world: int, n_sets: int, use_graph: bool) -> dict:
+    """The workload description both arms print (the same keys and values for the same run)."""
+    return {"workload": w.name, "frame_px": w.grid_h * 16, "n_tokens": w.n_tokens,
+            "n_text": w.n_text, "n_image": w.n_image, "active": w.active, "pattern": w.pattern,
+            "M_avg": M_avg, "heads": w.n_heads, "head_dim": HEAD_DIM,
+            "rope_axes": list(w.rope_axes), "rope_theta": w.rope_theta,
+            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "l2": f"{n_sets} rotating input sets, {n_sets * 6 * w.n_tokens * w.n_heads * HEAD_DIM * 2 / 2**20:.0f} MiB > L2",
+            "graph": f"{n_sets} consecutive frames per CUDA graph" if use_graph else False}
+
+
+def frame_masks(w, seed: int, rank: int, n_sets: int) -> list:
+    """The change masks of the rotating input sets (make_device_frame draws the same ones)."""
+    import workloads as W
+    return [W.make_mask(w, np.random.default_rng(seed + 7919 * rank + s)) for s in range(n_sets)]
 
 
 def frame_cfg(w):
@@ -357,13 +376,7 @@ def run_ours(args):
         "us_per_frame": round(ms_per_step * 1e3, 2), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": w.dtype, "impl": "ours",
         "data": "synthetic: N(0,1) Q/K/V/cache, N(1,0.1) norm weights, Bernoulli mask (seeded)",
-        "config": {"workload": w.name, "frame_px": w.grid_h * 16, "n_tokens": w.n_tokens,
-                   "n_text": w.n_text, "n_image": w.n_image, "active": w.active, "pattern": w.pattern,
-                   "M_avg": M_avg, "heads": w.n_heads, "head_dim": HEAD_DIM,
-                   "rope_axes": list(w.rope_axes), "rope_theta": w.rope_theta,
-                   "parallelism": f"replicas{world}" if world > 1 else "single",
-                   "l2": f"{n_sets} rotating input sets, {n_sets * 6 * w.n_tokens * w.n_heads * HEAD_DIM * 2 / 2**20:.0f} MiB > L2",
-                   "graph": f"{n_sets} consecutive frames per CUDA graph" if use_graph else False},
+        "config": bench_config(w, M_avg, world, n_sets, use_graph),
         "roofline": roof,
         "kernels": {"gather": mem,
                     "in_frame_us": {k[:-3]: round(v, 2) for k, v in kern.items()},
@@ -612,10 +625,11 @@ def _cpu_oracle():
     return O, native
 
 
-def cpu_frame_sample(O, native, w, M_s: int, seed: int):
-    """One bounded sample of the plugin math on the CPU: the full gather/norm/RoPE of a frame
-    restricted to M_s executed tokens, attention of those M_s queries over all N keys, scatter,
-    cache update. Returns (seconds, attention FLOP)."""
+def cpu_frame_sample(O, native, w, M_s: int, seed: int, mask=None):
+    """One frame of the plugin math on the CPU: gather/norm/RoPE of the executed tokens, attention
+    of their queries over all N keys, scatter, cache update. The executed tokens are those of
+    `mask` when given (a whole frame of the workload), else M_s random ones (a bounded sample).
+    Returns (seconds, attention FLOP)."""
     import workloads as W
     rng = np.random.default_rng(seed)
     N, C = w.n_tokens, w.n_heads * HEAD_DIM
@@ -624,9 +638,11 @@ def cpu_frame_sample(O, native, w, M_s: int, seed: int):
         cpu_frame_sample.cache = ((w.name, N), {k: f() for k in ("q", "k", "v", "ck", "cv", "out")},
                                   W.positions(w), rng.normal(1, 0.1, 128).astype(np.float32))
     _, a, pos, nw = cpu_frame_sample.cache
-    mask = np.zeros(N, dtype=np.int32)
-    mask[rng.choice(N, size=M_s, replace=False)] = 2
-    t0 = time.perf_counter()
+    if mask is None:
+        mask = np.zeros(N, dtype=np.int32)
+        mask[rng.choice(N, size=M_s, replace=False)] = 2
+    else:
+        mask = np.array(mask, dtype=np.int32, copy=True)
     L = O.lib(native)
     fp = lambda x: x.ctypes.data_as(O._f32p)
     ip = lambda x: x.ctypes.data_as(O._i32p)
@@ -663,41 +679,142 @@ def cpu_baseline(w, budget_s: float, seed: int) -> dict:
 
 
 def run_reference(args):
+    """The reference arm: the CPU fp32 restatement of the reference math on all host cores, on the
+    same frames as our arm (the masks of the rotating input sets: the same executed tokens, all
+    heads, all N keys) when the whole run fits in about two minutes, else on a bounded number of
+    executed tokens per step. On rank 0 only; with a GPU it also times the reference's own CUDA
+    kernels on one such frame (reference_cuda)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     w = workload(args)
+    n_sets = 4
+    masks = frame_masks(w, args.seed, 0, n_sets)
+    M_avg = statistics.mean(int((m != 0).sum()) for m in masks)
     O, native = _cpu_oracle()
     cores = O.set_threads(os.cpu_count() or 1, native)
     dt, _ = cpu_frame_sample(O, native, w, 16, args.seed)
     per_row = max(dt / 16, 1e-6)
     total_steps = args.steps + args.warmup
+    whole = per_row * M_avg * total_steps <= 150.0
     budget_per_step = max(0.02, min(4.0, 120.0 / max(total_steps, 1)))   # whole run ~2 minutes
     M_s = int(max(16, min(w.n_tokens, budget_per_step / per_row)))
+    one = (lambda i: cpu_frame_sample(O, native, w, 0, args.seed + i, mask=masks[i % n_sets])) if whole \
+        else (lambda i: cpu_frame_sample(O, native, w, M_s, args.seed + 1000 + i))
     for i in range(args.warmup):
-        cpu_frame_sample(O, native, w, M_s, args.seed + i)
+        one(i)
     tot_t, tot_f = 0.0, 0.0
     for i in range(args.steps):
-        dt, fl = cpu_frame_sample(O, native, w, M_s, args.seed + 1000 + i)
+        dt, fl = one(i)
         tot_t += dt
         tot_f += fl
     value = tot_f / tot_t / 1e12
     ms_per_step = tot_t / max(args.steps, 1) * 1e3
+    sample = (f"per step: one whole oracle frame of {w.name} (the executed tokens of our arm's input "
+              f"set i % {n_sets}, M_avg {M_avg:.1f} of {w.n_tokens}, all heads and keys)") if whole else \
+        (f"per step: an oracle frame of {w.name} restricted to {M_s} executed tokens of {w.n_tokens} "
+         f"(all heads and keys), bounded so that the run ends within minutes")
     out = {
         "metric": METRIC, "value": round(value, 5), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
+        "us_per_frame": round(ms_per_step * 1e3, 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "impl": "reference", "data": "synthetic (seeded)",
-        "config": {"workload": w.name, "n_tokens": w.n_tokens, "heads": w.n_heads,
-                   "head_dim": HEAD_DIM, "active": w.active},
+        "impl": "reference", "data": "synthetic: N(0,1) Q/K/V/cache, N(1,0.1) norm weights, Bernoulli mask (seeded)",
+        "config": bench_config(w, M_avg, world, n_sets, not args.no_graph),
         "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                         "sample": f"per step: oracle frame with {M_s} executed tokens of {w.n_tokens}, all heads/keys"},
+                         "sample": sample},
         "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference has no CPU implementation of this path and its GPU attention is "
                 "numerically defective; this arm times the CPU fp32 restatement of the reference math",
     }
+    if not args.no_ref_cuda:
+        try:
+            out["reference_cuda"] = reference_cuda_leg(w, masks[0], args.seed)
+        except Exception as ex:      # reported, not required
+            out["reference_cuda"] = {"unavailable": str(ex)[:200]}
     print(json.dumps(out), flush=True)
+
+
+def reference_cuda_leg(w, mask_h, seed: int) -> dict:
+    """The reference's own CUDA kernels (oracle/_ref/libfxr_refkernels.so, compiled for sm_100a from
+    its sources) on one frame of the workload, as its plugins would run the slice in fp32:
+    gather_tokens of the Q, K, V rows (gather_scatter_kernels.cu:15-41), launch_rms_norm of the
+    gathered Q and K per head (seq_len = M*H, dim = 128; flux2_kernels.cu:58-90),
+    SpatialCache::sync_kv_cache over all N rows (spatial_kv_cache.cu:55-87,175-196), attention_fwd
+    of the M queries over the N merged keys ((batch, heads, len, dim) layout; the transposes around
+    it are not timed; attention_kernels.cu:85-173) and scatter_tokens of the outputs
+    (gather_scatter_kernels.cu:46-72). The reference has no RoPE. CUDA events on the launching
+    stream, median of repetitions, nvidia-smi clocks sampled over the leg."""
+    import torch
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import oracle as O
+    if not torch.cuda.is_available():
+        return {"unavailable": "no GPU"}
+    L = O.ref_kernels()
+    if L is None:
+        return {"unavailable": "oracle/_ref/libfxr_refkernels.so not built (reference sources absent where build() ran)"}
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    N, H, D = w.n_tokens, w.n_heads, HEAD_DIM
+    C = H * D
+    g = torch.Generator(device=dev).manual_seed(seed)
+    M = int((mask_h != 0).sum())
+    idx = torch.from_numpy(np.nonzero(mask_h)[0].astype(np.int32)).to(dev)
+    mask = torch.from_numpy(np.asarray(mask_h, dtype=np.int32)).to(dev)
+    q, k, v = (torch.randn(N, C, device=dev, generator=g) for _ in range(3))
+    qg, kg, vg = (torch.empty(M, C, device=dev) for _ in range(3))
+    wq = 1 + 0.1 * torch.randn(D, device=dev, generator=g)
+    out_full = torch.zeros(N, C, device=dev)
+    s = torch.cuda.current_stream()
+    ss = s.cuda_stream
+    cache = L.ref_cache_create(N - w.n_text, w.n_text, 64, H, D, 1, 0)
+    if not cache:
+        return {"unavailable": "reference SpatialCache construction failed"}
+
+    def timed(fn, reps):
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            fn()
+            e1.record(s)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        return statistics.median(ts[1:] if len(ts) > 2 else ts)
+
+    clocks = Clocks(0)
+    clocks.start()
+    rows = {}
+    try:
+        rows["gather_tokens x3 (Q, K, V)"] = timed(lambda: [L.ref_gather_tokens(
+            t.data_ptr(), o.data_ptr(), idx.data_ptr(), M, C, ss) for t, o in ((q, qg), (k, kg), (v, vg))], 7)
+        qn, kn = torch.empty_like(qg), torch.empty_like(kg)
+        rows["launch_rms_norm x2 (Q, K per head)"] = timed(lambda: [L.ref_rms_norm(
+            a.data_ptr(), b.data_ptr(), wq.data_ptr(), 1e-6, M * H, D, ss) for a, b in ((qg, qn), (kg, kn))], 7)
+        kk, vv = k.clone(), v.clone()
+        rows["SpatialCache::sync_kv_cache (N rows)"] = timed(lambda: L.ref_cache_sync_kv(
+            cache, kk.data_ptr(), vv.data_ptr(), mask.data_ptr(), 0, 1, ss), 7)
+        qh = qn.view(M, H, D).transpose(0, 1).contiguous()
+        kh = kk.view(N, H, D).transpose(0, 1).contiguous()
+        vh = vv.view(N, H, D).transpose(0, 1).contiguous()
+        oh = torch.empty_like(qh)
+        rows["attention_fwd (fp32, B=1)"] = timed(lambda: L.ref_attention_fwd(
+            qh.data_ptr(), kh.data_ptr(), vh.data_ptr(), oh.data_ptr(), 1, H, M, N, D, ss), 3)
+        og = oh.transpose(0, 1).reshape(M, C).contiguous()
+        rows["scatter_tokens"] = timed(lambda: L.ref_scatter_tokens(
+            og.data_ptr(), out_full.data_ptr(), idx.data_ptr(), M, C, ss), 7)
+        torch.cuda.synchronize()
+    finally:
+        clk = clocks.stop()
+        L.ref_cache_destroy(cache)
+    total = sum(rows.values())
+    return {"us_per_frame": round(total, 1), "value": round(attn_flops(w, M) / (total * 1e-6) / 1e12, 4),
+            "unit": "TFLOP/s", "M": M, "kernels_us": {k_: round(v_, 1) for k_, v_ in rows.items()},
+            "kind": "the reference's CUDA kernels compiled for sm_100a from its sources (fp32, no RoPE)",
+            "attention_fwd": "numerically defective: it normalises with one warp's partial row maximum "
+                             "and sum (attention_kernels.cu:117-139); timed, never used as an oracle",
+            "clocks": clk}
 
 
 # ---------------------------------------------------------------------------------------------

@@ -620,9 +620,11 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
                 if (prev == n_split - 1) {   // the last part to arrive combines this portion
                     if (lane == 0) p.split_cnt[u * kSplitPortions + warp] = 0;   // for the next launch
                     __threadfence();
+                    // a live row with a negative index is out of bounds (flagged there), not padding
+                    const int32_t orow = live ? (*orow_slot < 0 ? INT32_MAX : *orow_slot) : -1;
                     split_combine_store<T>(p, static_cast<T*>(stream_out(p, orow_slot[kSoftmaxThreads])),
                                            p.split_scratch + (size_t)u * n_split * kSplitSlotFloats,
-                                           n_split, r, wg, live ? *orow_slot : -1, head);
+                                           n_split, r, wg, orow, head);
                 }
                 continue;
             }

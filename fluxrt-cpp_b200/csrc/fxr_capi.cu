@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdint>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -15,6 +16,7 @@
 #include "fxr.h"
 #include "fxr_attention.cuh"
 #include "fxr_compat_kernels.cuh"
+#include "fxr_dense_kernels.cuh"
 #include "fxr_device.cuh"
 #include "fxr_gemm.cuh"
 #include "fxr_mem_kernels.cuh"
@@ -317,10 +319,12 @@ int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, con
     p.n_heads = d->n_heads;
     const float scale = d->softmax_scale > 0.f ? d->softmax_scale : 1.0f / std::sqrt((float)d->head_dim);
     p.scale_log2 = scale * 1.4426950408889634f;
-    const int grid = (int)std::min<int64_t>(attention_ctas(N, d->n_heads) * n_streams, sm_count());
     // few heads per launch (a GPU's share of a head-split frame, small models): the query tiles x
-    // heads may leave SMs idle, so launch the instantiation that can split key ranges
+    // heads may leave SMs idle, so launch the instantiation that can split key ranges, on every SM
+    // (the kernel decides on the device how many parts each unit gets; CTAs without an item exit)
     const bool split_ok = split.slots > 0 && d->n_heads <= kSplitMaxHeads;
+    const int grid = split_ok ? sm_count()
+                              : (int)std::min<int64_t>(attention_ctas(N, d->n_heads) * n_streams, sm_count());
     cudaError_t e = split_ok ? launch_pdl(fxr::attn::attention_kernel<T, true>, dim3(grid), dim3(fxr::attn::kThreads),
                                           fxr::attn::kSmemBytes, stream, maps, p)
                              : launch_pdl(fxr::attn::attention_kernel<T, false>, dim3(grid), dim3(fxr::attn::kThreads),
@@ -425,13 +429,18 @@ int32_t fxr_check_device_error(void* stream, uint32_t* word_out) {
     if (e != cudaSuccess) return cuda_status(e, "clear error word");
     if (word_out) *word_out = w;
     if (w & fxr::kErrTimeout) return fail(FXR_ERR_TIMEOUT, "device wait timed out (word 0x%x)", w);
-    if (w) return fail(FXR_ERR_INVALID, "device bounds check failed (word 0x%x)", w);
+    if (w) return fail(FXR_ERR_BOUNDS, "a kernel skipped a row index outside its buffer (word 0x%x)", w);
     return FXR_OK;
 }
 
 size_t fxr_workspace_size(const fxr_frame_desc* desc) {
     if (!desc || dtype_bytes(desc->dtype) == 0 || desc->n_heads <= 0 || desc->head_dim <= 0) return 0;
     return carve(desc, nullptr).total + split_bytes(kSplitSlotsPerSm * sm_count());
+}
+
+size_t fxr_workspace_min_size(const fxr_frame_desc* desc) {
+    if (!desc || dtype_bytes(desc->dtype) == 0 || desc->n_heads <= 0 || desc->head_dim <= 0) return 0;
+    return carve(desc, nullptr).total;
 }
 
 // Device address of g_noalloc_scratch on the current device. The first call on a device resolves
@@ -615,7 +624,8 @@ int32_t fxr_restore_rows(const fxr_frame_desc* desc, const int32_t* mask, const 
 
 static int32_t rows_copy(bool scatter, const void* src, int64_t ld_src, const int32_t* idx,
                          const int32_t* count, int32_t host_count, void* dst, int64_t ld_dst,
-                         int64_t row_bytes, void* stream) {
+                         int64_t row_bytes, int32_t n_index_rows, void* stream) {
+    const int32_t n_rows = n_index_rows > 0 ? n_index_rows : INT32_MAX;
     if (!count && host_count < 0) return fail(FXR_ERR_INVALID, "need a device count or host_count >= 0");
     if (!count && host_count == 0) return FXR_OK;
     if (!src || !dst || !idx || row_bytes <= 0) return fail(FXR_ERR_INVALID, "null pointer or row_bytes <= 0");
@@ -630,19 +640,19 @@ static int32_t rows_copy(bool scatter, const void* src, int64_t ld_src, const in
                     row_bytes % 4 == 0 && ld_src % 4 == 0 && ld_dst % 4 == 0;
     if (v16) {
         if (scatter)
-            fxr::rows_copy_kernel<uint4, true><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes / 16);
+            fxr::rows_copy_kernel<uint4, true><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes / 16, n_rows);
         else
-            fxr::rows_copy_kernel<uint4, false><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes / 16);
+            fxr::rows_copy_kernel<uint4, false><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes / 16, n_rows);
     } else if (v4) {
         if (scatter)
-            fxr::rows_copy_kernel<uint32_t, true><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes / 4);
+            fxr::rows_copy_kernel<uint32_t, true><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes / 4, n_rows);
         else
-            fxr::rows_copy_kernel<uint32_t, false><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes / 4);
+            fxr::rows_copy_kernel<uint32_t, false><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes / 4, n_rows);
     } else {
         if (scatter)
-            fxr::rows_copy_kernel<uint8_t, true><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes);
+            fxr::rows_copy_kernel<uint8_t, true><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes, n_rows);
         else
-            fxr::rows_copy_kernel<uint8_t, false><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes);
+            fxr::rows_copy_kernel<uint8_t, false><<<grid, 256, 0, s>>>(sp, ld_src, idx, count, host_count, dp, ld_dst, row_bytes, n_rows);
     }
     FXR_CHECK_LAUNCH("rows_copy_kernel launch");
     return FXR_OK;
@@ -650,14 +660,16 @@ static int32_t rows_copy(bool scatter, const void* src, int64_t ld_src, const in
 
 int32_t fxr_gather_rows(const void* src, int64_t ld_src_bytes, const int32_t* idx,
                         const int32_t* count, int32_t host_count, void* dst, int64_t ld_dst_bytes,
-                        int64_t row_bytes, void* stream) {
-    return rows_copy(false, src, ld_src_bytes, idx, count, host_count, dst, ld_dst_bytes, row_bytes, stream);
+                        int64_t row_bytes, int32_t n_index_rows, void* stream) {
+    return rows_copy(false, src, ld_src_bytes, idx, count, host_count, dst, ld_dst_bytes, row_bytes,
+                     n_index_rows, stream);
 }
 
 int32_t fxr_scatter_rows(const void* src, int64_t ld_src_bytes, const int32_t* idx,
                          const int32_t* count, int32_t host_count, void* dst, int64_t ld_dst_bytes,
-                         int64_t row_bytes, void* stream) {
-    return rows_copy(true, src, ld_src_bytes, idx, count, host_count, dst, ld_dst_bytes, row_bytes, stream);
+                         int64_t row_bytes, int32_t n_index_rows, void* stream) {
+    return rows_copy(true, src, ld_src_bytes, idx, count, host_count, dst, ld_dst_bytes, row_bytes,
+                     n_index_rows, stream);
 }
 
 int32_t fxr_kv_sync(void* keys, void* values, void* cached_keys, void* cached_values,
@@ -748,6 +760,78 @@ int32_t fxr_rms_norm(const void* x, void* y, const float* w, float eps, int64_t 
     }
     FXR_CHECK_LAUNCH("rms_norm_kernel launch");
     return FXR_OK;
+}
+
+int32_t fxr_layer_norm_f32(const float* x, float* y, const float* gamma, const float* beta, float eps,
+                           int64_t rows, int32_t dim, void* stream) {
+    if (rows < 0 || dim < 0) return fail(FXR_ERR_INVALID, "negative size");
+    if (rows == 0 || dim == 0) return FXR_OK;
+    if (!x || !y) return fail(FXR_ERR_INVALID, "null pointer argument");
+    fxr::layer_norm_f32_kernel<<<grid_rows(rows, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        x, y, gamma, beta, eps, rows, dim);
+    FXR_CHECK_LAUNCH("layer_norm_f32_kernel launch");
+    return FXR_OK;
+}
+
+int32_t fxr_modulate_f32(const float* x, const float* scale, const float* shift, float* out, int64_t rows,
+                         int32_t dim, void* stream) {
+    if (rows < 0 || dim < 0) return fail(FXR_ERR_INVALID, "negative size");
+    if (rows == 0 || dim == 0) return FXR_OK;
+    if (!x || !scale || !shift || !out) return fail(FXR_ERR_INVALID, "null pointer argument");
+    const int64_t total = rows * dim;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)sm_count() * 16));
+    fxr::modulate_f32_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, scale, shift, out, rows, dim);
+    FXR_CHECK_LAUNCH("modulate_f32_kernel launch");
+    return FXR_OK;
+}
+
+}  // extern "C"
+
+template <int kOp>
+static int32_t launch_ew(const fxr::EwArgs& a, bool vec_ok, cudaStream_t s) {
+    const bool vec = vec_ok && a.n % 4 == 0 && aligned16(a.x) && aligned16(a.out) && (!a.y || aligned16(a.y));
+    const int64_t work = vec ? a.n / 4 : a.n;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, (int64_t)sm_count() * 16));
+    if (vec)
+        fxr::ew_f32_kernel<kOp, true><<<grid, 256, 0, s>>>(a);
+    else
+        fxr::ew_f32_kernel<kOp, false><<<grid, 256, 0, s>>>(a);
+    FXR_CHECK_LAUNCH("ew_f32_kernel launch");
+    return FXR_OK;
+}
+
+extern "C" {
+
+int32_t fxr_gelu_tanh_f32(float* data, int64_t n, void* stream) {
+    if (n < 0) return fail(FXR_ERR_INVALID, "negative size");
+    if (n == 0) return FXR_OK;
+    if (!data) return fail(FXR_ERR_INVALID, "null pointer argument");
+    fxr::EwArgs a{data, nullptr, data, n, 1, 0.f};
+    return launch_ew<fxr::kEwGelu>(a, true, static_cast<cudaStream_t>(stream));
+}
+
+int32_t fxr_bias_add_f32(float* data, const float* bias, int64_t rows, int32_t dim, void* stream) {
+    if (rows < 0 || dim < 0) return fail(FXR_ERR_INVALID, "negative size");
+    if (rows == 0 || dim == 0) return FXR_OK;
+    if (!data || !bias) return fail(FXR_ERR_INVALID, "null pointer argument");
+    fxr::EwArgs a{data, bias, data, rows * dim, dim, 0.f};
+    return launch_ew<fxr::kEwBias>(a, dim % 4 == 0, static_cast<cudaStream_t>(stream));
+}
+
+int32_t fxr_add_f32(const float* x, const float* y, float* z, int64_t n, void* stream) {
+    if (n < 0) return fail(FXR_ERR_INVALID, "negative size");
+    if (n == 0) return FXR_OK;
+    if (!x || !y || !z) return fail(FXR_ERR_INVALID, "null pointer argument");
+    fxr::EwArgs a{x, y, z, n, 1, 0.f};
+    return launch_ew<fxr::kEwAdd>(a, true, static_cast<cudaStream_t>(stream));
+}
+
+int32_t fxr_scale_add_f32(const float* x, const float* y, float* out, float gate, int64_t n, void* stream) {
+    if (n < 0) return fail(FXR_ERR_INVALID, "negative size");
+    if (n == 0) return FXR_OK;
+    if (!x || !y || !out) return fail(FXR_ERR_INVALID, "null pointer argument");
+    fxr::EwArgs a{x, y, out, n, 1, gate};
+    return launch_ew<fxr::kEwScaleAdd>(a, true, static_cast<cudaStream_t>(stream));
 }
 
 int32_t fxr_attention_f32_bhsd(const float* q, const float* k, const float* v, float* out,

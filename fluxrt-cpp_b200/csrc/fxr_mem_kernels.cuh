@@ -686,11 +686,15 @@ template <typename V, bool kScatter>
 __global__ void __launch_bounds__(256)
 rows_copy_kernel(const char* __restrict__ src, int64_t ld_src, const int32_t* __restrict__ idx,
                  const int32_t* __restrict__ count, int32_t host_count, char* __restrict__ dst,
-                 int64_t ld_dst, int64_t row_vec) {
+                 int64_t ld_dst, int64_t row_vec, int32_t n_index_rows) {
     const int lane = threadIdx.x & 31;
     const int32_t M = count ? *count : host_count;
     for (int32_t m = blockIdx.x * 8 + (threadIdx.x >> 5); m < M; m += gridDim.x * 8) {
         const int32_t i = idx[m];
+        if (i < 0 || i >= n_index_rows) {          // skipped: neither the indexed nor the compact row moves
+            if (lane == 0) atomicOr(&g_error_word, kErrBounds);
+            continue;
+        }
         const V* s = reinterpret_cast<const V*>(src + (kScatter ? (int64_t)m * ld_src : (int64_t)i * ld_src));
         V* d = reinterpret_cast<V*>(dst + (kScatter ? (int64_t)i * ld_dst : (int64_t)m * ld_dst));
         for (int64_t e = lane; e < row_vec; e += 32) d[e] = s[e];

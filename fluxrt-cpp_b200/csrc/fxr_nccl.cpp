@@ -3,11 +3,10 @@
 // The library does not link NCCL: a process that already holds a libnccl.so.2 (for example through
 // PyTorch's distributed package) must drive communicators created by that same copy, so the
 // functions are looked up with dlopen(RTLD_NOLOAD) first and only then from the loader's search
-// path. The declarations below restate the public NCCL C API this file calls (types and
-// signatures from its documentation: ncclGetUniqueId, ncclCommInitRank, ncclCommDestroy,
-// ncclAllGather, ncclGetErrorString).
+// path. Types and signatures come from the installed nccl.h.
 #include <cuda_runtime.h>
 #include <dlfcn.h>
+#include <nccl.h>
 
 #include <cstdio>
 #include <cstring>
@@ -20,19 +19,15 @@ extern "C" void fxr_internal_set_error(const char* msg);
 
 namespace {
 
-struct NcclUniqueId {
-    char internal[128];
-};
-typedef void* NcclComm;
+static_assert(sizeof(ncclUniqueId) == 128, "fxr_nccl_unique_id hands out 128-byte ids");
 typedef int NcclResult;
-constexpr int kNcclInt8 = 0;   // ncclInt8: byte-wise transfers
 
 struct NcclApi {
-    NcclResult (*get_unique_id)(NcclUniqueId*) = nullptr;
-    NcclResult (*comm_init_rank)(NcclComm*, int, NcclUniqueId, int) = nullptr;
-    NcclResult (*comm_destroy)(NcclComm) = nullptr;
-    NcclResult (*all_gather)(const void*, void*, size_t, int, NcclComm, cudaStream_t) = nullptr;
-    const char* (*error_string)(NcclResult) = nullptr;
+    decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+    decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+    decltype(&ncclCommDestroy) comm_destroy = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
+    decltype(&ncclGetErrorString) error_string = nullptr;
     bool ok = false;
     std::string why;
 };
@@ -63,7 +58,7 @@ int32_t nccl_fail(const char* what, NcclResult r) {
     const NcclApi& a = api();
     char buf[256];
     std::snprintf(buf, sizeof(buf), "%s: NCCL error %d (%s)", what, r,
-                  a.error_string ? a.error_string(r) : "?");
+                  a.error_string ? a.error_string(static_cast<ncclResult_t>(r)) : "?");
     fxr_internal_set_error(buf);
     return FXR_ERR_NCCL;
 }
@@ -81,7 +76,7 @@ int32_t fxr_nccl_unique_id(unsigned char id_out[128]) {
     if (!id_out) return FXR_ERR_INVALID;
     const NcclApi& a = api();
     if (!a.ok) return no_nccl();
-    NcclUniqueId id;
+    ncclUniqueId id;
     NcclResult r = a.get_unique_id(&id);
     if (r != 0) return nccl_fail("ncclGetUniqueId", r);
     std::memcpy(id_out, id.internal, sizeof(id.internal));
@@ -92,9 +87,9 @@ int32_t fxr_nccl_comm_init(int32_t world, int32_t rank, const unsigned char id[1
     if (!id || !comm || world < 1 || rank < 0 || rank >= world) return FXR_ERR_INVALID;
     const NcclApi& a = api();
     if (!a.ok) return no_nccl();
-    NcclUniqueId uid;
+    ncclUniqueId uid;
     std::memcpy(uid.internal, id, sizeof(uid.internal));
-    NcclComm c = nullptr;
+    ncclComm_t c = nullptr;
     NcclResult r = a.comm_init_rank(&c, world, uid, rank);
     if (r != 0) return nccl_fail("ncclCommInitRank", r);
     *comm = c;
@@ -105,7 +100,7 @@ int32_t fxr_nccl_comm_destroy(void* comm) {
     if (!comm) return FXR_OK;
     const NcclApi& a = api();
     if (!a.ok) return no_nccl();
-    NcclResult r = a.comm_destroy(comm);
+    NcclResult r = a.comm_destroy(static_cast<ncclComm_t>(comm));
     return r == 0 ? FXR_OK : nccl_fail("ncclCommDestroy", r);
 }
 
@@ -114,7 +109,8 @@ int32_t fxr_internal_nccl_allgather(const void* send, void* recv, size_t bytes, 
                                     void* stream) {
     const NcclApi& a = api();
     if (!a.ok) return no_nccl();
-    NcclResult r = a.all_gather(send, recv, bytes, kNcclInt8, comm, static_cast<cudaStream_t>(stream));
+    NcclResult r = a.all_gather(send, recv, bytes, ncclInt8, static_cast<ncclComm_t>(comm),
+                                static_cast<cudaStream_t>(stream));
     return r == 0 ? FXR_OK : nccl_fail("ncclAllGather", r);
 }
 

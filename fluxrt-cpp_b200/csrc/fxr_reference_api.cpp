@@ -18,20 +18,53 @@ void gather_tokens(const float* src, float* dst, const int32_t* indices, int32_t
                    int32_t dim, cudaStream_t stream) {
     if (active_count <= 0 || dim <= 0) return;
     const int64_t row = (int64_t)dim * (int64_t)sizeof(float);
-    fxr_gather_rows(src, row, indices, nullptr, active_count, dst, row, row, stream);
+    fxr_gather_rows(src, row, indices, nullptr, active_count, dst, row, row, 0, stream);
 }
 
 void scatter_tokens(const float* src, float* dst, const int32_t* indices, int32_t active_count,
                     int32_t dim, cudaStream_t stream) {
     if (active_count <= 0 || dim <= 0) return;
     const int64_t row = (int64_t)dim * (int64_t)sizeof(float);
-    fxr_scatter_rows(src, row, indices, nullptr, active_count, dst, row, row, stream);
+    fxr_scatter_rows(src, row, indices, nullptr, active_count, dst, row, row, 0, stream);
+}
+
+void apply_modulation(const float* x, const float* scale, const float* shift, float* out,
+                      int32_t seq_len, int32_t dim, cudaStream_t stream) {
+    if (seq_len <= 0 || dim <= 0) return;
+    fxr_modulate_f32(x, scale, shift, out, seq_len, dim, stream);
+}
+
+void layer_norm_modulated(const float* x, float* y, const float* gamma, const float* beta, float eps,
+                          int32_t seq_len, int32_t dim, cudaStream_t stream) {
+    if (seq_len <= 0 || dim <= 0) return;
+    fxr_layer_norm_f32(x, y, gamma, beta, eps, seq_len, dim, stream);
+}
+
+void launch_gelu(float* data, int32_t n, cudaStream_t stream) {
+    if (n <= 0) return;
+    fxr_gelu_tanh_f32(data, n, stream);
+}
+
+void launch_bias_add(float* data, const float* bias, int32_t seq_len, int32_t dim, cudaStream_t stream) {
+    if (!bias || seq_len <= 0 || dim <= 0) return;
+    fxr_bias_add_f32(data, bias, seq_len, dim, stream);
 }
 
 void launch_rms_norm(const float* x, float* y, const float* weight, float eps, int32_t seq_len,
                      int32_t dim, cudaStream_t stream) {
     if (seq_len <= 0 || dim <= 0) return;
     fxr_rms_norm(x, y, weight, eps, seq_len, dim, FXR_F32, stream);
+}
+
+void launch_elem_add(const float* x, const float* y, float* z, int32_t n, cudaStream_t stream) {
+    if (n <= 0) return;
+    fxr_add_f32(x, y, z, n, stream);
+}
+
+void launch_scale_add(const float* x, const float* y, float* out, float gate, int32_t n,
+                      cudaStream_t stream) {
+    if (n <= 0) return;
+    fxr_scale_add_f32(x, y, out, gate, n, stream);
 }
 
 void attention_fwd(const float* Q, const float* K, const float* V, float* out, int32_t batch,

@@ -20,16 +20,18 @@ FXR_ERR_TIMEOUT = 3
 FXR_ERR_UNSUPPORTED = 4
 FXR_ERR_WORKSPACE = 5
 FXR_ERR_NCCL = 6
+FXR_ERR_BOUNDS = 7
 
 FXR_F32, FXR_F16, FXR_BF16 = 0, 1, 2
 
 # Every symbol include/fxr.h and include/fxr_plugin.h declare (checked by the CPU test suite).
 EXPORTED = [
     "fxr_abi_version", "fxr_build_info", "fxr_last_error_string", "fxr_check_device_error",
-    "fxr_workspace_size", "fxr_workspace_views", "fxr_mask_compact", "fxr_preprocess_mask",
+    "fxr_workspace_size", "fxr_workspace_min_size", "fxr_workspace_views", "fxr_mask_compact", "fxr_preprocess_mask",
     "fxr_mark_updated", "fxr_gather_norm_rope", "fxr_attention_active", "fxr_restore_rows",
     "fxr_gather_rows", "fxr_scatter_rows", "fxr_kv_sync", "fxr_output_cache_sync",
-    "fxr_rms_norm", "fxr_attention_f32_bhsd", "fxr_frame_forward", "fxr_frame_forward_noalloc",
+    "fxr_rms_norm", "fxr_layer_norm_f32", "fxr_modulate_f32", "fxr_gelu_tanh_f32", "fxr_bias_add_f32",
+    "fxr_add_f32", "fxr_scale_add_f32", "fxr_attention_f32_bhsd", "fxr_frame_forward", "fxr_frame_forward_noalloc",
     "fxr_frame_host_workspace_size", "fxr_frame_forward_host",
     "fxr_plugin_create", "fxr_plugin_clone", "fxr_plugin_destroy", "fxr_plugin_name",
     "fxr_plugin_version", "fxr_plugin_namespace", "fxr_plugin_fields", "fxr_plugin_output_desc",
@@ -173,6 +175,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
     L.fxr_check_device_error.argtypes = [_vp, ctypes.POINTER(ctypes.c_uint32)]
     L.fxr_workspace_size.argtypes = [ctypes.POINTER(FrameDesc)]
     L.fxr_workspace_size.restype = ctypes.c_size_t
+    L.fxr_workspace_min_size.argtypes = [ctypes.POINTER(FrameDesc)]
+    L.fxr_workspace_min_size.restype = ctypes.c_size_t
     L.fxr_workspace_views.argtypes = [ctypes.POINTER(FrameDesc), _vp, ctypes.POINTER(_vp),
                                       ctypes.POINTER(_vp), ctypes.POINTER(_vp),
                                       ctypes.POINTER(_i64), ctypes.POINTER(_vp)]
@@ -184,7 +188,7 @@ def load(path: str | None = None) -> ctypes.CDLL:
                                        _vp, _vp]
     L.fxr_restore_rows.argtypes = [ctypes.POINTER(FrameDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp]
     for fn in (L.fxr_gather_rows, L.fxr_scatter_rows):
-        fn.argtypes = [_vp, _i64, _vp, _vp, _i32, _vp, _i64, _i64, _vp]
+        fn.argtypes = [_vp, _i64, _vp, _vp, _i32, _vp, _i64, _i64, _i32, _vp]
     L.fxr_kv_sync.argtypes = [_vp, _vp, _vp, _vp, _vp, _i32, _i64, _i32, _vp]
     L.fxr_output_cache_sync.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp]
     L.fxr_rms_norm.argtypes = [_vp, _vp, _vp, ctypes.c_float, _i64, _i32, _i32, _vp]
@@ -322,6 +326,11 @@ def workspace_size(cfg: FrameConfig) -> int:
     return int(load().fxr_workspace_size(ctypes.byref(d)))
 
 
+def workspace_min_size(cfg: FrameConfig) -> int:
+    d = cfg.desc()
+    return int(load().fxr_workspace_min_size(ctypes.byref(d)))
+
+
 def workspace_views(cfg: FrameConfig, ws):
     """(idx_ptr, count_ptr, qc_ptr, ld_qc, save_ptr) device addresses inside a workspace tensor."""
     d = cfg.desc()
@@ -370,18 +379,24 @@ def restore_rows(cfg: FrameConfig, mask, idx, count, save, cache_k, cache_v, str
                                    _ptr(cache_k), _ptr(cache_v), _stream(stream)))
 
 
-def gather_rows(src, idx, dst, count=None, host_count: int = -1, stream=None):
+def gather_rows(src, idx, dst, count=None, host_count: int = -1, stream=None, n_index_rows=None):
+    """dst[m] = src[idx[m]]; indices outside [0, n_index_rows) (default: src's rows) are skipped
+    and reported by check_device_error as FXR_ERR_BOUNDS."""
     eb = src.element_size()
+    n = src.shape[0] if n_index_rows is None else n_index_rows
     _check(load().fxr_gather_rows(_ptr(src), src.stride(0) * eb, _ptr(idx), _ptr(count), host_count,
                                   _ptr(dst), dst.stride(0) * eb, src[0].numel() * eb if src.dim() > 1 else eb,
-                                  _stream(stream)))
+                                  n, _stream(stream)))
 
 
-def scatter_rows(src, idx, dst, count=None, host_count: int = -1, stream=None):
+def scatter_rows(src, idx, dst, count=None, host_count: int = -1, stream=None, n_index_rows=None):
+    """dst[idx[m]] = src[m]; indices outside [0, n_index_rows) (default: dst's rows) are skipped
+    and reported by check_device_error as FXR_ERR_BOUNDS."""
     eb = src.element_size()
+    n = dst.shape[0] if n_index_rows is None else n_index_rows
     _check(load().fxr_scatter_rows(_ptr(src), src.stride(0) * eb, _ptr(idx), _ptr(count), host_count,
                                    _ptr(dst), dst.stride(0) * eb, dst[0].numel() * eb if dst.dim() > 1 else eb,
-                                   _stream(stream)))
+                                   n, _stream(stream)))
 
 
 def kv_sync(keys, values, cached_keys, cached_values, mask, stream=None):

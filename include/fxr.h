@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define FXR_ABI_VERSION 1
+#define FXR_ABI_VERSION 2
 
 /* Status codes. The reference's plugin enqueue returns 0 / -1
  * (src/inference/plugins/flux2_double_block_plugin.cpp:208,230); these refine the -1. */
@@ -46,8 +46,10 @@ typedef enum fxr_status {
     FXR_ERR_CUDA = 2,         /* a CUDA runtime call or kernel launch failed */
     FXR_ERR_TIMEOUT = 3,      /* a bounded device-side wait gave up (device error word set) */
     FXR_ERR_UNSUPPORTED = 4,  /* valid request this build does not implement (e.g. head_dim != 128 on the tensor-core path) */
-    FXR_ERR_WORKSPACE = 5,    /* workspace smaller than fxr_workspace_size() */
-    FXR_ERR_NCCL = 6          /* NCCL call failed */
+    FXR_ERR_WORKSPACE = 5,    /* workspace smaller than fxr_workspace_min_size() */
+    FXR_ERR_NCCL = 6,         /* NCCL call failed */
+    FXR_ERR_BOUNDS = 7        /* a kernel met a row index outside its buffer and skipped that row
+                                 (reported by fxr_check_device_error) */
 } fxr_status;
 
 /* Storage element types (compute is fp32 throughout). */
@@ -78,8 +80,14 @@ const char* fxr_build_info(void);
 /* Last error message of the calling thread ("" if none). */
 const char* fxr_last_error_string(void);
 
-/* Reads and clears the device error word of the current device (set by bounded waits that gave
- * up and by checked-build bounds checks). Synchronises `stream`. Returns FXR_OK or FXR_ERR_TIMEOUT. */
+/* Reads and clears the device error word of the current device. Kernels set it instead of faulting:
+ * bit 0 when a bounded device wait gave up (2 s), bit 1 when an index outside [0, rows) of the
+ * indexed buffer was met (the row was skipped: nothing was read from or written to it). The checks
+ * are always compiled in. Synchronises `stream`, then returns FXR_OK, FXR_ERR_TIMEOUT (bit 0 set,
+ * whatever else is) or FXR_ERR_BOUNDS; *word_out (may be NULL) receives the raw word.
+ * There is one word per device, shared by every stream and thread that uses this library on it: a
+ * check after one stream's work can report an error raised by another stream's work that ran in
+ * the meantime. Pass stream NULL after cudaDeviceSynchronize for a check that covers all work. */
 int32_t fxr_check_device_error(void* stream, uint32_t* word_out);
 
 /* ---- workspace ------------------------------------------------------------------------------ */
@@ -87,6 +95,12 @@ int32_t fxr_check_device_error(void* stream, uint32_t* word_out);
  * of mask==1 tokens). Replaces the reference's workspace carve-up
  * (flux2_double_block_plugin.cpp:167-185, 347-366). */
 size_t fxr_workspace_size(const fxr_frame_desc* desc);
+
+/* The smallest workspace fxr_frame_forward accepts: idx, count, compact Q and saved rows, without
+ * the optional area that lets the attention split each unit's key range across CTAs. A workspace
+ * between this size and fxr_workspace_size gets as many split slots as fit in the rest; at this
+ * size the attention never splits (the split only runs for calls of at most 8 heads). */
+size_t fxr_workspace_min_size(const fxr_frame_desc* desc);
 
 /* ---- individual steps ----------------------------------------------------------------------- */
 
@@ -137,13 +151,20 @@ int32_t fxr_restore_rows(const fxr_frame_desc* desc, const int32_t* mask, const 
 
 /* Byte-exact row gather / scatter over the first *count indices (count may be a device
  * pointer, or NULL with host_count >= 0). 16-byte vectorised when row_bytes and strides allow.
- * Replace gather_tokens / scatter_tokens (gather_scatter_kernels.cu:15-72). */
+ * Replace gather_tokens / scatter_tokens (gather_scatter_kernels.cu:15-72).
+ * n_index_rows: rows of the indexed buffer (src of the gather, dst of the scatter); an index
+ * outside [0, n_index_rows) is skipped and sets the device error word (FXR_ERR_BOUNDS from
+ * fxr_check_device_error); the compact row m of a skipped index is left untouched.
+ * n_index_rows <= 0: the size is unknown (the reference signature) and only negative indices are
+ * caught. */
 int32_t fxr_gather_rows(const void* src, int64_t ld_src_bytes, const int32_t* idx,
                         const int32_t* count, int32_t host_count,
-                        void* dst, int64_t ld_dst_bytes, int64_t row_bytes, void* stream);
+                        void* dst, int64_t ld_dst_bytes, int64_t row_bytes, int32_t n_index_rows,
+                        void* stream);
 int32_t fxr_scatter_rows(const void* src, int64_t ld_src_bytes, const int32_t* idx,
                          const int32_t* count, int32_t host_count,
-                         void* dst, int64_t ld_dst_bytes, int64_t row_bytes, void* stream);
+                         void* dst, int64_t ld_dst_bytes, int64_t row_bytes, int32_t n_index_rows,
+                         void* stream);
 
 /* Full-frame K/V merge + update with the reference's exact semantics
  * (sync_kv_cache_kernel, spatial_kv_cache.cu:55-87): keys[i] = execute ? keys[i] : cached[i];
@@ -163,6 +184,28 @@ int32_t fxr_output_cache_sync(void* pred, void* cache, const int32_t* mask, uint
  * flux2_kernels.h:22-24): y = x * rsqrt(mean(x^2) + eps) * w over rows of `dim` elements. */
 int32_t fxr_rms_norm(const void* x, void* y, const float* w, float eps, int64_t rows,
                      int32_t dim, int32_t dtype, void* stream);
+
+/* The reference's dense fp32 block helpers over whole sequences (rows of `dim` floats), for the
+ * C++ mirror of its kernel layer (include/fxr_reference_api.h); off the sparse path.
+ *   fxr_layer_norm_f32   y = (x - mean) * rsqrt(var + eps) [* gamma] [+ beta], biased variance per
+ *                        row; gamma / beta may be NULL (layer_norm_modulated,
+ *                        gather_scatter_kernels.h:46-61, gather_scatter_kernels.cu:103-169)
+ *   fxr_modulate_f32     out = (1 + scale) * x + shift, scale / shift [dim] (apply_modulation,
+ *                        gather_scatter_kernels.h:38-44, gather_scatter_kernels.cu:74-99)
+ *   fxr_gelu_tanh_f32    data = data * 0.5 * (1 + tanh(0.7978845608 (data + 0.044715 data^3)))
+ *                        (launch_gelu, flux2_kernels.h:15, flux2_kernels.cu:14-29)
+ *   fxr_bias_add_f32     data[r, :] += bias (launch_bias_add, flux2_kernels.h:18-19, flux2_kernels.cu:34-53)
+ *   fxr_add_f32          z = x + y (launch_elem_add, flux2_kernels.h:27-28, flux2_kernels.cu:92-108)
+ *   fxr_scale_add_f32    out = x + gate * y (launch_scale_add, flux2_kernels.h:31-32, flux2_kernels.cu:113-135)
+ * Outputs may alias inputs element for element. */
+int32_t fxr_layer_norm_f32(const float* x, float* y, const float* gamma, const float* beta, float eps,
+                           int64_t rows, int32_t dim, void* stream);
+int32_t fxr_modulate_f32(const float* x, const float* scale, const float* shift, float* out, int64_t rows,
+                         int32_t dim, void* stream);
+int32_t fxr_gelu_tanh_f32(float* data, int64_t n, void* stream);
+int32_t fxr_bias_add_f32(float* data, const float* bias, int64_t rows, int32_t dim, void* stream);
+int32_t fxr_add_f32(const float* x, const float* y, float* z, int64_t n, void* stream);
+int32_t fxr_scale_add_f32(const float* x, const float* y, float* out, float gate, int64_t n, void* stream);
 
 /* fp32 attention in the reference's (batch, heads, len, head_dim) layout, head_dim <= 256:
  * out = softmax(Q K^T / sqrt(head_dim)) V with one softmax over all kv_len keys. Backs the
@@ -219,11 +262,15 @@ int32_t fxr_frame_forward_host(const fxr_frame_desc* desc,
  * device allocation, or a latency-critical loop that must not risk the device-wide
  * synchronisation an allocation can cause. This entry point has no counterpart in the reference.
  *   - Scratch: a fixed 96 MiB array inside this library (every GPU that loads the library holds it
- *     until the process exits). Frames whose fxr_workspace_size() exceeds 96 MiB are rejected with
- *     FXR_ERR_WORKSPACE; a 1024x1024 frame (4608 tokens, 24 heads, bf16/fp16) needs about 85 MB.
+ *     until the process exits). Frames whose fxr_workspace_min_size() exceeds 96 MiB are rejected
+ *     with FXR_ERR_WORKSPACE; a 1024x1024 frame (4608 tokens, 24 heads, bf16/fp16) needs about
+ *     85 MB. The rest of the 96 MiB serves as the attention's optional key-range split slots
+ *     (calls of at most 8 heads), exactly as a 96 MiB workspace does for fxr_frame_forward.
  *   - No cudaMalloc, cudaFree or other allocating call is made. The first call on a device looks up
- *     the scratch address for that device (once, with that device current); make that first call
- *     before any stream capture.
+ *     the scratch address for that device (once, with that device current) and keeps it for the
+ *     life of the process; make that first call before any stream capture, and do not call
+ *     cudaDeviceReset on that device afterwards (the array would move and the kept address
+ *     would be stale).
  *   - Every call on a device shares the same scratch, and each frame overwrites it completely
  *     before reading it (nothing has to start at zero). Calls whose work overlaps on the GPU (two
  *     streams, or two host threads) race on it: serialise them on one stream.

@@ -6,11 +6,16 @@
 //
 // Replaced declarations (fluxrt-cpp paths):
 //   fluxrt::plugins::gather_tokens / scatter_tokens   src/inference/plugins/gather_scatter_kernels.h:21-36
-//   fluxrt::plugins::launch_rms_norm                  src/inference/plugins/flux2_kernels.h:22-24
+//   fluxrt::plugins::apply_modulation                 src/inference/plugins/gather_scatter_kernels.h:38-49
+//   fluxrt::plugins::layer_norm_modulated             src/inference/plugins/gather_scatter_kernels.h:51-63
+//   fluxrt::plugins::launch_gelu / launch_bias_add /  src/inference/plugins/flux2_kernels.h:15-33
+//     launch_rms_norm / launch_elem_add / launch_scale_add
 //   fluxrt::plugins::attention_fwd                    src/inference/plugins/attention_kernels.h:20-24
 //   fluxrt::kernels::SpatialCache                     src/inference/kernels/spatial_kv_cache.h:12-55
-// Off-path declarations of those headers (AdaLN modulation, LayerNorm, GELU, bias/residual adds)
-// are not part of this library.
+// With these, libfxr.so takes the place of the reference's fluxrt_kernels library and of the kernel
+// sources its plugins compile (src/CMakeLists.txt:25-27; gather_scatter_kernels.cu, flux2_kernels.cu,
+// attention_kernels.cu). The forwarding headers under include/fluxrt_dropin/ carry the reference's
+// header paths, for callers that include them by those names.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -20,14 +25,22 @@
 #include <string>
 #include <vector>
 
+// fluxrt::RuntimeError, the exception type SpatialCache throws. A caller built inside the
+// reference's source tree (include root src/, src/CMakeLists.txt:10-13) already has it from
+// src/utils/error.h:18-21, which is then included here so that the class is defined once; elsewhere
+// (this library's own build) the same class is declared here.
+#if __has_include("utils/error.h")
+#include "utils/error.h"
+#else
 namespace fluxrt {
-
-// Error type thrown by SpatialCache, as the reference's RuntimeError (src/utils/error.h:18-21).
 class RuntimeError : public std::runtime_error {
 public:
     explicit RuntimeError(const std::string& msg) : std::runtime_error(msg) {}
 };
+}  // namespace fluxrt
+#endif
 
+namespace fluxrt {
 namespace plugins {
 
 // dst[m, :] = src[indices[m], :] for m < active_count; fp32 rows of `dim` values.
@@ -38,9 +51,31 @@ void gather_tokens(const float* src, float* dst, const int32_t* indices, int32_t
 void scatter_tokens(const float* src, float* dst, const int32_t* indices, int32_t active_count,
                     int32_t dim, cudaStream_t stream);
 
+// out = (1 + scale) * x + shift; x, out (seq_len, dim), scale, shift (dim).
+void apply_modulation(const float* x, const float* scale, const float* shift, float* out,
+                      int32_t seq_len, int32_t dim, cudaStream_t stream);
+
+// y = (x - mean) / sqrt(var + eps) [* gamma] [+ beta] per row of `dim` values; gamma, beta (dim)
+// or nullptr.
+void layer_norm_modulated(const float* x, float* y, const float* gamma, const float* beta, float eps,
+                          int32_t seq_len, int32_t dim, cudaStream_t stream);
+
+// In place: data = data * 0.5 * (1 + tanh(0.7978845608 * (data + 0.044715 data^3))).
+void launch_gelu(float* data, int32_t n, cudaStream_t stream);
+
+// data[r, :] += bias over (seq_len, dim); a null bias does nothing.
+void launch_bias_add(float* data, const float* bias, int32_t seq_len, int32_t dim, cudaStream_t stream);
+
 // y = x * rsqrt(mean(x^2) + eps) * weight over rows of `dim` values (seq_len rows).
 void launch_rms_norm(const float* x, float* y, const float* weight, float eps, int32_t seq_len,
                      int32_t dim, cudaStream_t stream);
+
+// z = x + y over n values.
+void launch_elem_add(const float* x, const float* y, float* z, int32_t n, cudaStream_t stream);
+
+// out = x + gate * y over n values.
+void launch_scale_add(const float* x, const float* y, float* out, float gate, int32_t n,
+                      cudaStream_t stream);
 
 // out = softmax(Q K^T / sqrt(head_dim)) V per (batch, head), layout (batch, heads, len, head_dim),
 // fp32. Computes the intended joint softmax over all kv_len keys (the reference kernel's

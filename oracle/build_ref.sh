@@ -1,8 +1,10 @@
 #!/usr/bin/env bash
-# Compiles fluxrt-cpp's own CUDA kernels for sm_100a from the reference sources, where they lie,
-# together with oracle/ref_shim.cu, into oracle/_ref/libfxr_refkernels.so (git-ignored; the .so
-# travels to the GPU box). No reference source is copied into this repository.
-# The reference's TensorRT plugin classes are not built: NvInferRuntime.h is absent here.
+# Compiles fluxrt-cpp's own CUDA kernels for sm_100a from the reference sources, where they lie
+# (FXR_REFERENCE_ROOT, by default the read-only checkout at /root/reference), together with
+# oracle/ref_shim.cu, into oracle/_ref/libfxr_refkernels.so. The .so is git-ignored and copied with
+# the working tree; machines without the reference sources skip this step and use that copy.
+# No reference source is copied into this repository. The reference's TensorRT plugin classes are
+# not built: NvInferRuntime.h is absent.
 set -euo pipefail
 here="$(cd "$(dirname "$0")" && pwd)"
 ref="${FXR_REFERENCE_ROOT:-/root/reference}"

@@ -99,6 +99,26 @@ void fxo_rope_row(float* x, int32_t head_dim, const int32_t* pos, int32_t n_axes
     rope_apply(x, head_dim, cs, sn);
 }
 
+/* RMSNorm + RoPE of the listed rows, every head: y[r] = rope(rms_norm(x[idx[r]])) per head
+ * (flux2_kernels.cu:58-82 formula, then the published FLUX rotary embedding). The per-row step of
+ * fxo_frame_forward on its own, so that a caller can round the results to a storage type. */
+void fxo_norm_rope_rows(const float* x, int64_t ld_x, const int32_t* idx, int32_t count,
+                        const int32_t* pos, int32_t n_axes, const int32_t* axes_dim, float theta,
+                        const float* w, float eps, int32_t n_heads, int32_t head_dim,
+                        float* y, int64_t ld_y) {
+    #pragma omp parallel for schedule(static)
+    for (int32_t r = 0; r < count; ++r) {
+        const int32_t i = idx[r];
+        float cs[512], sn[512];
+        rope_tables(pos + (int64_t)i * n_axes, n_axes, axes_dim, theta, head_dim, cs, sn);
+        for (int32_t h = 0; h < n_heads; ++h) {
+            float* yo = y + (int64_t)r * ld_y + (int64_t)h * head_dim;
+            rms_norm_row(x + (int64_t)i * ld_x + (int64_t)h * head_dim, yo, w, eps, head_dim);
+            rope_apply(yo, head_dim, cs, sn);
+        }
+    }
+}
+
 /* attention_kernels.cu:85-155, intended semantics: softmax over every key of one head, scale
  * 1/sqrt(D), then the weighted sum of V. Work is split over (head, 64-query block). Dot products
  * accumulate in 16 independent fp32 lanes; the softmax denominator in double. */

@@ -66,6 +66,13 @@ void fxo_rms_norm(const float* x, float* y, const float* w, float eps, int64_t r
 void fxo_rope_row(float* x, int32_t head_dim, const int32_t* pos, int32_t n_axes,
                   const int32_t* axes_dim, float theta);
 
+/* RMSNorm + RoPE of rows idx[0..count) of x, every head (the per-row step of fxo_frame_forward):
+ * y[r, h*D:(h+1)*D] = rope(rms_norm(x[idx[r], h*D:(h+1)*D], w), pos[idx[r]]). fp32. */
+void fxo_norm_rope_rows(const float* x, int64_t ld_x, const int32_t* idx, int32_t count,
+                        const int32_t* pos, int32_t n_axes, const int32_t* axes_dim, float theta,
+                        const float* w, float eps, int32_t n_heads, int32_t head_dim,
+                        float* y, int64_t ld_y);
+
 /* Joint non-causal attention of compact queries against all keys (attention_kernels.cu:85-155,
  * intended semantics: one softmax over every key, scale 1/sqrt(D) unless scale > 0).
  * q: [M, ld_q] (heads at column h*D), k, v: [N, ld_kv], o: [M, ld_o]; fp32. */

@@ -56,6 +56,9 @@ def lib(native: bool = False) -> ctypes.CDLL:
         fn.restype = None
     L.fxo_rms_norm.argtypes = [_f32p, _f32p, _f32p, ctypes.c_float, _i64, _i32]
     L.fxo_rope_row.argtypes = [_f32p, _i32, _i32p, _i32, _i32p, ctypes.c_float]
+    L.fxo_norm_rope_rows.argtypes = [_f32p, _i64, _i32p, _i32, _i32p, _i32, _i32p, ctypes.c_float,
+                                     _f32p, ctypes.c_float, _i32, _i32, _f32p, _i64]
+    L.fxo_norm_rope_rows.restype = None
     L.fxo_attention.argtypes = [_f32p, _i64, _i32, _f32p, _f32p, _i64, _i32, _i32, _i32,
                                 ctypes.c_float, _f32p, _i64]
     L.fxo_kv_sync.argtypes = [_f32p, _f32p, _f32p, _f32p, _i32p, _i32, _i64]
@@ -194,6 +197,43 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, n_heads: int, head_di
     lib().fxo_attention(_p(q, _f32p), C, M, _p(k, _f32p), _p(v, _f32p), k.shape[1], k.shape[0],
                         n_heads, head_dim, scale, _p(o, _f32p), C)
     return o
+
+
+def norm_rope_rows(x: np.ndarray, idx: np.ndarray, pos: np.ndarray, w: np.ndarray, n_heads: int,
+                   head_dim: int, axes_dim, theta: float, eps: float = 1e-6) -> np.ndarray:
+    """RMSNorm + RoPE of rows x[idx], every head -> [len(idx), n_heads * head_dim] fp32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    idx = np.ascontiguousarray(idx, dtype=np.int32)
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    ax = np.ascontiguousarray(axes_dim, dtype=np.int32)
+    C = n_heads * head_dim
+    y = np.zeros((idx.size, C), dtype=np.float32)
+    if idx.size:
+        lib().fxo_norm_rope_rows(_p(x, _f32p), x.shape[1], _p(idx, _i32p), idx.size, _p(pos, _i32p),
+                                 ax.size, _p(ax, _i32p), theta, _p(w, _f32p), eps, n_heads, head_dim,
+                                 _p(y, _f32p), C)
+    return y
+
+
+def frame_operands(q, k, v, mask, valid, pos, norm_q, norm_k, cache_k, cache_v, n_heads: int,
+                   head_dim: int, axes_dim, theta: float, operand_dtype: str = "f32",
+                   eps: float = 1e-6) -> dict:
+    """The attention operands of one frame as the CUDA path stores them: mask protocol and
+    compaction, normed + roped Q' (compact) and K' of the executed rows rounded to `operand_dtype`
+    ("f32" = unrounded), attention K/V = cache rows with the executed rows replaced by K' / V
+    (spatial_kv_cache.cu:64-67). Returns mask, idx, qc [M, C], keys, values [N, C] (fp32 arrays
+    holding the rounded values)."""
+    mask, idx = mask_compact(mask, valid)
+    qc = round_storage(norm_rope_rows(q, idx, pos, norm_q, n_heads, head_dim, axes_dim, theta, eps),
+                       operand_dtype)
+    kn = round_storage(norm_rope_rows(k, idx, pos, norm_k, n_heads, head_dim, axes_dim, theta, eps),
+                       operand_dtype)
+    keys = np.array(cache_k, dtype=np.float32, copy=True)
+    values = np.array(cache_v, dtype=np.float32, copy=True)
+    keys[idx] = kn
+    values[idx] = np.asarray(v, dtype=np.float32)[idx]
+    return {"mask": mask, "idx": idx, "qc": qc, "keys": keys, "values": values}
 
 
 def _f32(a):

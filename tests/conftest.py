@@ -21,3 +21,14 @@ def cuda():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda:0")
+
+
+def pytest_terminal_summary(terminalreporter):
+    """Achieved max-abs / mean-abs of each tolerance check next to its bar."""
+    import parity_stats
+    if not parity_stats.RECORDS:
+        return
+    tr = terminalreporter
+    tr.section("measured errors (max-abs / mean-abs against the bar)")
+    for test, what, mx, mn, bmx, bmn in parity_stats.RECORDS:
+        tr.write_line(f"{test[:58]:58s} {what[:30]:30s} {mx:9.2e} / {mn:9.2e}   bar {bmx:.0e} / {bmn:.0e}")

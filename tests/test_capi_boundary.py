@@ -45,7 +45,7 @@ def test_library_is_sm100a_only_and_self_contained(lib):
     out = subprocess.run(["ldd", fxr.LIB_PATH], capture_output=True, text=True).stdout
     assert "libcudart" not in out      # static runtime: nothing to resolve against torch's copy
     assert "libtorch" not in out and "libpython" not in out
-    assert lib.fxr_abi_version() == 1
+    assert lib.fxr_abi_version() == 2
 
 
 def test_frame_desc_layout_matches_header():
@@ -60,6 +60,20 @@ def test_workspace_size_and_views(lib):
     C = 24 * 128
     assert n >= 4608 * 4 + 4608 * C * 2 * 3
     assert n % 256 == 0
+    # the minimum leaves out only the optional key-range split area
+    lo = fxr.workspace_min_size(cfg)
+    assert 4608 * 4 + 4608 * C * 2 * 3 <= lo < n and lo % 256 == 0
+    assert fxr.workspace_min_size(fxr.FrameConfig(n_tokens=16, n_text=4, dtype="f32", head_dim=0)) == 0
+
+
+def test_status_codes_match_the_header():
+    """Every FXR_ERR_* value of include/fxr.h is the binding's constant of the same name."""
+    text = open(HEADERS[0]).read()
+    body = text[text.index("typedef enum fxr_status"):text.index("} fxr_status;")]
+    codes = dict((k, int(v)) for k, v in re.findall(r"\b(FXR_(?:OK|ERR_[A-Z_]+))\s*=\s*(\d+)", body))
+    assert codes["FXR_ERR_BOUNDS"] == 7 and len(codes) == 8
+    for name, value in codes.items():
+        assert getattr(fxr, name) == value, name
 
 
 def test_invalid_arguments_rejected_without_gpu(lib):

@@ -2,9 +2,10 @@
 when they run a frame (it uses a fixed scratch array inside the library instead of a workspace).
 
 Checked through the C ABI against fxr_frame_forward (caller workspace) on the same inputs, for two
-calls in a row, with the tolerance the parity tests use (the two paths run the same kernels, so the
-results are in fact identical). This file is collected last so that a stopping run has already run
-every other test; it also passes on its own in a fresh process.
+calls in a row, with the tolerance the parity tests use and bit for bit: the two paths run the same
+kernels with the same schedule (the 6-head case also gets the same key-range split slots from the
+built-in scratch as from fxr_workspace_size's workspace). This file is collected last so that a
+stopping run has already run every other test; it also passes on its own in a fresh process.
 """
 import ctypes
 
@@ -45,7 +46,10 @@ def _close(a, b, what):
     assert err.max() <= TOL["max_abs"] and err.mean() <= TOL["mean_abs"], (what, err.max(), err.mean())
 
 
-@pytest.mark.parametrize("wl", [W.C2, W.C1])
+C2_6HEADS = W.Workload("c2_1024px_p25_bf16_h6", 64, 64, 512, n_heads=6)
+
+
+@pytest.mark.parametrize("wl", [W.C2, W.C1, C2_6HEADS])
 def test_noalloc_matches_workspace_entry_point(cuda, wl):
     L = _lib()
     tdt = torch.bfloat16 if wl.dtype == "bf16" else torch.float16
@@ -72,6 +76,7 @@ def test_noalloc_matches_workspace_entry_point(cuda, wl):
         assert torch.equal(a["mask"], b["mask"])
         for k in ("out", "cache_k", "cache_v"):
             _close(b[k], a[k], f"call {call}: {k}")
+            assert torch.equal(b[k], a[k]), f"call {call}: {k} differs from the workspace entry point"
 
 
 def test_noalloc_rejects_frames_beyond_its_scratch(cuda):
