@@ -70,6 +70,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="default run: skip the c4 streams / c5 head-split sub-records")
     ap.add_argument("--no-ref-cuda", action="store_true",
                     help="reference arm: skip timing the reference's own CUDA kernels")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
@@ -394,15 +396,46 @@ def run_ours(args):
             out["cpu_baseline"] = cpu_baseline(w, args.cpu_seconds, args.seed)
         except Exception as ex:  # the baseline is reported, not required
             out["cpu_baseline"] = {"value": None, "error": str(ex)[:200]}
+    for g_ in graphs:
+        del g_
+    graphs.clear()
+    del run_graph
+    del frames, wss
+    torch.cuda.empty_cache()
+    if not args.no_sub and args.config == "c2" and args.active is None and args.heads is None:
+        out["sub"] = sub_records(args, world)
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:
-        for g_ in graphs:
-            del g_
-        graphs.clear()
-        del run_graph
         dist.barrier()
         dist.destroy_process_group()
+
+
+def sub_records(args, world: int) -> dict:
+    """The two configurations that shard over GPUs, measured on the same ranks after the main
+    figure (every rank takes the same steps): 8 independent 768^2 edit streams spread over the
+    GPUs (aggregate frames/s, no collective) and one 2048^2 frame split by heads (us per frame,
+    exchange of O over NVLink peer stores). Each keeps the keys its own runner prints."""
+    import copy
+    import torch
+    keep = ("value", "unit", "ms_per_step", "frames_per_s", "us_per_frame", "us_per_frame_per_gpu",
+            "scaling", "config", "roofline", "clocks", "steps", "warmup")
+    recs = {}
+    for name, cfg_, extra in (("c4_streams8", "c4", {"streams": 8, "split": None}),
+                              ("c5_heads", "c5", {"streams": None, "split": "heads"})):
+        a = copy.copy(args)
+        a.config, a.active, a.heads = cfg_, None, None
+        a.streams, a.split = extra["streams"], extra["split"]
+        a.steps = max(20, min(args.steps, 200 if cfg_ == "c4" else 100))
+        a.warmup = 3
+        try:
+            line = run_streams(a, embedded=True) if cfg_ == "c4" else run_heads(a, embedded=True)
+            recs[name] = {k: line[k] for k in keep if k in line}
+        except Exception as ex:   # reported, not required
+            recs[name] = {"error": str(ex)[:200]}
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return recs
 
 
 def per_kernel_times(cfg, w, frames, wss, stream, reps: int):
@@ -820,10 +853,12 @@ def reference_cuda_leg(w, mask_h, seed: int) -> dict:
 # ---------------------------------------------------------------------------------------------
 # one frame split by heads over the GPUs (peer stores + arrival wait)
 # ---------------------------------------------------------------------------------------------
-def run_heads(args):
-    """A step is one frame of all heads, split across the ranks by heads; every rank's attention
-    epilogue stores its heads' O rows into every rank's output over NVLink, then each rank waits
-    for all arrivals. value = whole-frame attention FLOP / max-over-ranks time (strong scaling)."""
+def run_heads(args, embedded: bool = False):
+    """A step is one frame of all heads, split across the ranks by heads; each rank's exchange
+    kernel stores its heads' O rows into every rank's output over NVLink, then each rank waits
+    for all arrivals. value = whole-frame attention FLOP / max-over-ranks time (strong scaling).
+    embedded: run inside an initialised process group and return the JSON object instead of
+    printing it (the multi-GPU sub-records of the default run)."""
     import datetime
     import torch
     import torch.distributed as dist
@@ -832,7 +867,7 @@ def run_heads(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
+    if world > 1 and not embedded:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
@@ -997,7 +1032,7 @@ def run_heads(args):
         "gpu_launches": (6 if nccl else 5) * args.steps,   # + NCCL's own kernel per frame when nccl
         "clocks": clk,
     }
-    if rank == 0:
+    if rank == 0 and not embedded:
         print(json.dumps(out_line), flush=True)
     torch.cuda.synchronize()
     if world > 1:
@@ -1013,16 +1048,19 @@ def run_heads(args):
         fxr.nccl_comm_destroy(comm)
     if world > 1:
         dist.barrier()
-        dist.destroy_process_group()
+        if not embedded:
+            dist.destroy_process_group()
+    return out_line
 
 
 # ---------------------------------------------------------------------------------------------
 # independent edit streams, batched (config 4: 8 streams of 768^2 spread over the GPUs)
 # ---------------------------------------------------------------------------------------------
-def run_streams(args):
+def run_streams(args, embedded: bool = False):
     """A step is one frame of every stream: each GPU runs its streams' frames as one batched set
     of launches (fxr_frame_forward_batch). value = attention FLOP of all streams / max-over-ranks
-    time; frames_per_s = streams / step time. Strong scaling: the total of streams is fixed."""
+    time; frames_per_s = streams / step time. Strong scaling: the total of streams is fixed.
+    embedded: as for run_heads."""
     import datetime
     import torch
     import torch.distributed as dist
@@ -1031,7 +1069,7 @@ def run_streams(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
+    if world > 1 and not embedded:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
@@ -1113,14 +1151,16 @@ def run_streams(args):
                    "l2": f"{n_sets} rotating sets of every stream's inputs", "graph": bool(graphs)},
         "e2e": None, "gpu_launches": 4 * args.steps, "clocks": clk,
     }
-    if rank == 0:
+    if rank == 0 and not embedded:
         print(json.dumps(out_line), flush=True)
     for g in graphs:
         del g
     graphs.clear()
     if world > 1:
         dist.barrier()
-        dist.destroy_process_group()
+        if not embedded:
+            dist.destroy_process_group()
+    return out_line
 
 
 # ---------------------------------------------------------------------------------------------

@@ -9,12 +9,14 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
 
 #include "fxr.h"
 #include "fxr_attention.cuh"
+#include "fxr_attention2.cuh"
 #include "fxr_compat_kernels.cuh"
 #include "fxr_dense_kernels.cuh"
 #include "fxr_device.cuh"
@@ -262,6 +264,16 @@ struct OutSet {
     SplitArea split;   // key-range split scratch (none: never split)
 };
 
+// Attention kernel for launches that need no key-range split: two query tiles per CTA unless
+// FXR_ATTENTION_TILES=1 selects the one-tile kernel (read once per process).
+static bool attention_pairs() {
+    static const bool pairs = [] {
+        const char* v = std::getenv("FXR_ATTENTION_TILES");
+        return !(v && v[0] == '1');
+    }();
+    return pairs;
+}
+
 int64_t attention_ctas(int64_t n_tokens, int64_t n_heads) {
     if (n_tokens <= 0 || n_heads <= 0) return 0;
     const int64_t max_tiles = (n_tokens + fxr::attn::kBM - 1) / fxr::attn::kBM * n_heads;
@@ -284,6 +296,7 @@ int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, con
                                  const SplitArea& split, cudaStream_t stream) {
     if (n_streams < 1 || n_streams > fxr::kMaxBatch) return fail(FXR_ERR_INVALID, "1..%d streams per launch", fxr::kMaxBatch);
     static bool configured[kMaxDevices] = {false};
+    static bool pairs_ok[kMaxDevices] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < kMaxDevices && !configured[dev]) {
@@ -293,7 +306,15 @@ int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, con
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(fxr::attn::attention_kernel<T, true>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fxr::attn::kSmemBytes);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(fxr::attn2::attention_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)fxr::attn2::kSmemBytes);
+        // the two-tile kernel redistributes its launch registers between warpgroups (setmaxnreg):
+        // it only runs when the compiled register count gives the CTA enough of them
+        cudaFuncAttributes fa{};
+        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, fxr::attn2::attention_kernel<T>);
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
+        pairs_ok[dev] = (uint32_t)fa.numRegs * (uint32_t)fxr::attn2::kThreads >= fxr::attn2::kRegPool;
         configured[dev] = true;
     }
     const int64_t C = (int64_t)d->n_heads * d->head_dim;
@@ -323,12 +344,21 @@ int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, con
     // heads may leave SMs idle, so launch the instantiation that can split key ranges, on every SM
     // (the kernel decides on the device how many parts each unit gets; CTAs without an item exit)
     const bool split_ok = split.slots > 0 && d->n_heads <= kSplitMaxHeads;
-    const int grid = split_ok ? sm_count()
-                              : (int)std::min<int64_t>(attention_ctas(N, d->n_heads) * n_streams, sm_count());
-    cudaError_t e = split_ok ? launch_pdl(fxr::attn::attention_kernel<T, true>, dim3(grid), dim3(fxr::attn::kThreads),
-                                          fxr::attn::kSmemBytes, stream, maps, p)
-                             : launch_pdl(fxr::attn::attention_kernel<T, false>, dim3(grid), dim3(fxr::attn::kThreads),
-                                          fxr::attn::kSmemBytes, stream, maps, p);
+    cudaError_t e;
+    if (!split_ok && attention_pairs() && dev >= 0 && dev < kMaxDevices && pairs_ok[dev]) {
+        // two query tiles per CTA (fxr_attention2.cuh)
+        const int64_t units = (N + fxr::attn2::kRows - 1) / fxr::attn2::kRows * d->n_heads * n_streams;
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(units, sm_count()));
+        e = launch_pdl(fxr::attn2::attention_kernel<T>, dim3(grid), dim3(fxr::attn2::kThreads),
+                       fxr::attn2::kSmemBytes, stream, maps, p);
+    } else {
+        const int grid = split_ok ? sm_count()
+                                  : (int)std::min<int64_t>(attention_ctas(N, d->n_heads) * n_streams, sm_count());
+        e = split_ok ? launch_pdl(fxr::attn::attention_kernel<T, true>, dim3(grid), dim3(fxr::attn::kThreads),
+                                  fxr::attn::kSmemBytes, stream, maps, p)
+                     : launch_pdl(fxr::attn::attention_kernel<T, false>, dim3(grid), dim3(fxr::attn::kThreads),
+                                  fxr::attn::kSmemBytes, stream, maps, p);
+    }
     if (e != cudaSuccess) return cuda_status(e, "attention_kernel launch");
     return FXR_OK;
 }

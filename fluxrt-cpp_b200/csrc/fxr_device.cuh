@@ -130,6 +130,37 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     return false;
 }
 
+// Non-blocking probe of an mbarrier phase: never suspends the thread.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// As mbar_wait, spinning on test_wait: for a single latency-critical thread (an MMA issuer) that
+// must react within tens of cycles of a phase completing; try_wait may keep a thread suspended for
+// hundreds of cycles after the phase completes. Bounded like every other wait.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, volatile int* abort) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1; i < kWaitLimitPolls; ++i) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if ((i & 255u) == 0u) {
+            if (*abort) return false;
+            if (global_timer_ns() - t0 > kWaitLimitNs) break;
+        }
+    }
+    atomicOr(&g_error_word, kErrTimeout);
+    *abort = 1;
+    return false;
+}
+
 // As mbar_wait, for waits that may last microseconds (a whole DRAM round trip or more): each
 // try_wait may suspend the thread until the phase completes (suspend-time hint 20 us) instead of
 // spinning, which keeps waiting warps off the issue slots of the working ones.
