@@ -372,13 +372,29 @@ int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
 }
 
 // Gather of n_streams frames of the same geometry (one launch; rows stream after stream).
+// Whether a gather launch over n_streams frames of n_tokens can do the compaction itself (every
+// CTA's share of the rows fits its shared-memory list; token and row indices fit the list entries).
+static bool gather_can_compact(int32_t n_streams, int32_t n_tokens) {
+    const int64_t rows = (int64_t)n_streams * n_tokens;
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(sm_count(), n_tokens));
+    return n_tokens < (1 << 24) && (rows + grid - 1) / grid <= fxr::kBulkListCap;
+}
+
 template <typename T>
 int32_t launch_gather_streams(const fxr_frame_desc* d, int32_t n_streams, const fxr::GatherStream* gs,
                               const int32_t* pos, const float* nq, const float* nk, int64_t ld_qc,
                               cudaStream_t stream, const float* nq_txt = nullptr,
-                              const float* nk_txt = nullptr, int32_t n_text_norm = 0) {
+                              const float* nk_txt = nullptr, int32_t n_text_norm = 0,
+                              const SplitArea* compact_split = nullptr) {
     if (n_streams < 1 || n_streams > fxr::kMaxBatch) return fail(FXR_ERR_INVALID, "1..%d streams per launch", fxr::kMaxBatch);
     fxr::GatherArgs a{};
+    // compact_split != nullptr: the gather compacts the masks itself (gs[b].valid) and zeroes these
+    // key-split counters; the caller launched no compaction kernel
+    if (compact_split) {
+        a.compact = 1;
+        a.zero = reinterpret_cast<uint4*>(compact_split->cnt);
+        a.zero_vec = (int32_t)((size_t)compact_split->slots * kSplitCntBytes / 16);
+    }
     for (int32_t b = 0; b < n_streams; ++b) a.s[b] = gs[b];
     a.n_streams = n_streams;
     a.pos = pos;
@@ -402,7 +418,7 @@ int32_t launch_gather_streams(const fxr_frame_desc* d, int32_t n_streams, const 
     const size_t budget = 190 * 1024;
     lay.stages = (uint32_t)std::max<size_t>(2, std::min<size_t>(fxr::kBulkMaxStages, budget / lay.stage_bytes));
     const size_t smem = (size_t)lay.stages * lay.stage_bytes + (size_t)lay.stages * fxr::kBulkInfoWords * 4 +
-                        (size_t)lay.stages * 16;
+                        (size_t)lay.stages * 16 + (compact_split ? fxr::kBulkListCap * sizeof(uint2) : 0);
     if (smem > 220 * 1024)
         return fail(FXR_ERR_UNSUPPORTED, "gather rows of %zu bytes do not fit the bulk pipeline", row_bytes);
     static bool configured[kMaxDevices] = {false};
@@ -431,6 +447,19 @@ int32_t launch_gather(const fxr_frame_desc* d, const void* q, const void* k, con
 }
 
 }  // namespace
+
+static int32_t check_gather_args(const fxr_frame_desc* desc, const void* q, const void* k, const void* v,
+                                 const int32_t* mask, const int32_t* idx, const int32_t* count,
+                                 const int32_t* pos, const float* norm_q, const float* norm_k, void* qc,
+                                 int64_t ld_qc, void* cache_k, void* cache_v, void* save) {
+    if (!q || !k || !v || !mask || !idx || !count || !norm_q || !norm_k || !qc || !cache_k ||
+        !cache_v || (desc->rope_n_axes > 0 && !pos))
+        return fail(FXR_ERR_INVALID, "null pointer argument");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(qc) || !aligned16(cache_k) ||
+        !aligned16(cache_v) || (save && !aligned16(save)) || (ld_qc % 8))
+        return fail(FXR_ERR_INVALID, "Q/K/V/qc/cache/save must be 16-byte aligned");
+    return FXR_OK;
+}
 
 // =============================================================================================
 extern "C" {
@@ -589,12 +618,9 @@ int32_t fxr_gather_norm_rope(const fxr_frame_desc* desc, const void* q, const vo
     int32_t st = check_desc(desc, false);
     if (st != FXR_OK) return st;
     if (desc->n_tokens == 0) return FXR_OK;
-    if (!q || !k || !v || !mask || !idx || !count || !norm_q || !norm_k || !qc || !cache_k ||
-        !cache_v || (desc->rope_n_axes > 0 && !pos))
-        return fail(FXR_ERR_INVALID, "null pointer argument");
-    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(qc) || !aligned16(cache_k) ||
-        !aligned16(cache_v) || (save && !aligned16(save)) || (ld_qc % 8))
-        return fail(FXR_ERR_INVALID, "Q/K/V/qc/cache/save must be 16-byte aligned");
+    if ((st = check_gather_args(desc, q, k, v, mask, idx, count, pos, norm_q, norm_k, qc, ld_qc, cache_k,
+                                cache_v, save)) != FXR_OK)
+        return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (desc->dtype == FXR_BF16)
         return launch_gather<__nv_bfloat16>(desc, q, k, v, mask, idx, count, pos, norm_q, norm_k, qc,
@@ -936,7 +962,11 @@ static int32_t frame_forward_impl(const fxr_frame_desc* desc, const void* q, con
         return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, w.total);
     if (!aligned16(workspace)) return fail(FXR_ERR_INVALID, "workspace must be 16-byte aligned");
     const SplitArea split = split_area(w.total, workspace, workspace_bytes, desc->n_heads);
-    if ((st = launch_compact(mask, valid, desc->n_tokens, w.idx, w.count, split, stream)) != FXR_OK) return st;
+    // device-resident frames: the gather compacts the mask itself (one launch fewer); host-resident
+    // ones need the index list before the gather, for the row upload
+    const bool fused = !host && gather_can_compact(1, desc->n_tokens);
+    if (!fused && (st = launch_compact(mask, valid, desc->n_tokens, w.idx, w.count, split, stream)) != FXR_OK)
+        return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const size_t eb = dtype_bytes(desc->dtype);
     const int64_t row_bytes = (int64_t)desc->n_heads * desc->head_dim * (int64_t)eb;
@@ -947,11 +977,23 @@ static int32_t frame_forward_impl(const fxr_frame_desc* desc, const void* q, con
                                    s)) != FXR_OK)
             return st;
     }
-    if ((st = fxr_gather_norm_rope(desc, q, k, v, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc,
-                                   w.ld_qc, cache_k, cache_v, w.save, stream)) != FXR_OK)
-        return st;
     if (!cache_k || !cache_v || !out || !aligned16(cache_k) || !aligned16(cache_v) || !aligned16(out))
         return fail(FXR_ERR_INVALID, "cache/out must be non-null and 16-byte aligned");
+    if (fused) {
+        if ((st = check_gather_args(desc, q, k, v, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc, w.ld_qc,
+                                    cache_k, cache_v, w.save)) != FXR_OK)
+            return st;
+        fxr::GatherStream gs{q, k, v, mask, w.idx, w.count, w.qc, cache_k, cache_v, w.save, valid};
+        st = desc->dtype == FXR_BF16
+                 ? launch_gather_streams<__nv_bfloat16>(desc, 1, &gs, pos, norm_q, norm_k, w.ld_qc, s, nullptr,
+                                                        nullptr, 0, &split)
+                 : launch_gather_streams<__half>(desc, 1, &gs, pos, norm_q, norm_k, w.ld_qc, s, nullptr, nullptr, 0,
+                                                 &split);
+    } else {
+        st = fxr_gather_norm_rope(desc, q, k, v, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc, w.ld_qc,
+                                  cache_k, cache_v, w.save, stream);
+    }
+    if (st != FXR_OK) return st;
     OutSet os;
     os.out = out;
     os.split = split;
@@ -1697,15 +1739,21 @@ static int32_t batch_group(const fxr_frame_desc* desc, int32_t nb, const fxr_str
             !aligned16(x.cache_v) || !aligned16(x.out))
             return fail(FXR_ERR_INVALID, "stream %d: buffers must be 16-byte aligned", b);
         ca.s[b] = fxr::CompactStream{x.mask, x.valid, w.idx, w.count};
-        gs[b] = fxr::GatherStream{x.q, x.k, x.v, x.mask, w.idx, w.count, w.qc, x.cache_k, x.cache_v, w.save};
+        gs[b] = fxr::GatherStream{x.q, x.k, x.v, x.mask, w.idx, w.count, w.qc, x.cache_k, x.cache_v, w.save,
+                                  x.valid};
         as[b] = AttnStreamArgs{w.qc, w.ld_qc, w.count, x.cache_k, x.cache_v, w.idx, x.out};
         ra.s[b] = fxr::RestoreStream{x.mask, w.idx, w.count, static_cast<const uint4*>(w.save),
                                      static_cast<char*>(x.cache_k), static_cast<char*>(x.cache_v)};
         ld_qc = w.ld_qc;
     }
     int32_t st;
-    if ((st = launch_compact_streams(ca, nb, desc->n_tokens, SplitArea{}, s)) != FXR_OK) return st;
-    if ((st = launch_gather_streams<T>(desc, nb, gs, pos, nq, nk, ld_qc, s)) != FXR_OK) return st;
+    // the gather compacts every stream's mask itself when its rows fit (one launch fewer)
+    const SplitArea none{};
+    const bool fused = gather_can_compact(nb, desc->n_tokens);
+    if (!fused && (st = launch_compact_streams(ca, nb, desc->n_tokens, SplitArea{}, s)) != FXR_OK) return st;
+    if ((st = launch_gather_streams<T>(desc, nb, gs, pos, nq, nk, ld_qc, s, nullptr, nullptr, 0,
+                                       fused ? &none : nullptr)) != FXR_OK)
+        return st;
     if ((st = launch_attention_streams<T>(desc, nb, as, SplitArea{}, s)) != FXR_OK) return st;
     return launch_restore_streams(desc, ra, nb, s);
 }

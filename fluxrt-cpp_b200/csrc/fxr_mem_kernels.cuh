@@ -151,11 +151,19 @@ struct GatherStream {           // one stream's buffers
     void* cache_k;
     void* cache_v;
     void* save;
+    const uint8_t* valid;       // compacting launches: cache-row validity (NULL: every row valid)
 };
 
 struct GatherArgs {
     GatherStream s[kMaxBatch];
     int32_t n_streams;
+    // compact != 0: the launch also does the mask protocol and compaction of every stream (the
+    // work of compact_kernel): each CTA scans the masks itself and keeps the list of its own rows
+    // in shared memory; CTA 0 writes the preprocessed masks, idx and count for the later kernels
+    // and zeroes the attention's key-split arrival counters (zero, zero_vec 16-byte words).
+    int32_t compact;
+    uint4* zero;
+    int32_t zero_vec;
     const int32_t* pos;
     const float* norm_q;
     const float* norm_k;
@@ -238,11 +246,104 @@ constexpr int kBulkProducerWarp = kBulkGroupWarps * kBulkGroups;
 constexpr int kBulkThreads = (kBulkProducerWarp + 1) * 32;
 constexpr int kBulkMaxStages = 32;
 constexpr int kBulkInfoWords = 8;   // per stage: token, mode, position ids[4], stream, compact row
+constexpr int kBulkListCap = 1024;  // rows per CTA of a compacting launch (token|mode, stream|row)
+constexpr int kScanPer = 8;         // tokens per thread and pass of the in-kernel compaction
+constexpr int kScanWarps = kBulkThreads / 32;
 
 struct BulkLayout {
     uint32_t stage_bytes;   // 3 rows (Q, K, V) of C elements, 128-byte aligned
     uint32_t stages;
 };
+
+// In-kernel mask protocol + compaction of every stream of a gather launch (compact_kernel's work,
+// done redundantly by every CTA so that no CTA waits for another). Tokens are scanned in passes of
+// kScanPer x kBulkThreads: thread t holds tokens pass0 + k*kBulkThreads + t (coalesced loads), a
+// ballot per (k, warp) and an exclusive scan of the kScanPer x kScanWarps counts give each executed
+// token its rank R in ascending token order. Launch row g = (earlier streams' rows) + R belongs to
+// CTA g % grid, slot g / grid of its list: (token | mode << 28, stream << 24 | R), mode 1 for mask 1
+// (execute, keep the cache row) and 2 for any other executed value. CTA 0 also writes the
+// preprocessed mask (valid == 0 -> 2), idx[R] and count, and zeroes the key-split counters.
+// Returns the executed rows of all streams.
+__device__ __forceinline__ int32_t compact_into_list(const GatherArgs& a, uint2* list) {
+    __shared__ int32_t cnt[kScanPer * kScanWarps];
+    __shared__ int32_t off[kScanPer * kScanWarps + 1];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t lt = (1u << lane) - 1u;
+    const bool writer = blockIdx.x == 0;
+    if (writer)
+        for (int32_t e = threadIdx.x; e < a.zero_vec; e += kBulkThreads) a.zero[e] = make_uint4(0, 0, 0, 0);
+    const int32_t n = a.n_tokens;
+    int32_t pre = 0;
+    for (int b = 0; b < a.n_streams; ++b) {
+        int32_t* mask = const_cast<int32_t*>(a.s[b].mask);
+        const uint8_t* valid = a.s[b].valid;
+        int32_t* idx = const_cast<int32_t*>(a.s[b].idx);
+        int32_t base = 0;
+        for (int32_t c0 = 0; c0 < n; c0 += kScanPer * kBulkThreads) {
+            int32_t mv[kScanPer];
+            uint32_t bal[kScanPer];
+#pragma unroll
+            for (int k = 0; k < kScanPer; ++k) {
+                const int32_t tok = c0 + k * kBulkThreads + (int32_t)threadIdx.x;
+                mv[k] = tok < n ? mask[tok] : 0;
+                if (valid != nullptr && tok < n && valid[tok] == 0) {
+                    if (writer && mv[k] != 2) mask[tok] = 2;
+                    mv[k] = 2;
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kScanPer; ++k) {
+                bal[k] = __ballot_sync(0xffffffffu, mv[k] != 0);
+                if (lane == 0) cnt[k * kScanWarps + warp] = __popc(bal[k]);
+            }
+            __syncthreads();
+            if (warp == 0) {
+                // exclusive scan of the counts in (k, warp) order: lane l sums a run of entries
+                constexpr int kRun = (kScanPer * kScanWarps + 31) / 32;
+                int32_t v[kRun], sum = 0;
+#pragma unroll
+                for (int q = 0; q < kRun; ++q) {
+                    const int e = lane * kRun + q;
+                    v[q] = e < kScanPer * kScanWarps ? cnt[e] : 0;
+                    sum += v[q];
+                }
+                int32_t incl = sum;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                int32_t run = incl - sum;
+#pragma unroll
+                for (int q = 0; q < kRun; ++q) {
+                    const int e = lane * kRun + q;
+                    if (e < kScanPer * kScanWarps) off[e] = run;
+                    run += v[q];
+                }
+                if (lane == 31) off[kScanPer * kScanWarps] = incl;
+            }
+            __syncthreads();
+#pragma unroll
+            for (int k = 0; k < kScanPer; ++k) {
+                if ((bal[k] >> lane) & 1u) {
+                    const int32_t tok = c0 + k * kBulkThreads + (int32_t)threadIdx.x;
+                    const int32_t R = base + off[k * kScanWarps + warp] + __popc(bal[k] & lt);
+                    if (writer) idx[R] = tok;
+                    const int32_t g = pre + R;
+                    if (g % (int32_t)gridDim.x == (int32_t)blockIdx.x)
+                        list[g / (int32_t)gridDim.x] = make_uint2((uint32_t)tok | ((mv[k] == 1 ? 1u : 2u) << 28),
+                                                                  ((uint32_t)b << 24) | (uint32_t)R);
+                }
+            }
+            base += off[kScanPer * kScanWarps];
+            __syncthreads();   // cnt / off are rewritten by the next pass
+        }
+        if (writer && threadIdx.x == 0) *const_cast<int32_t*>(a.s[b].count) = base;
+        pre += base;
+    }
+    __syncthreads();       // the list is complete
+    return pre;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kBulkThreads, 1)
@@ -271,8 +372,13 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
 
     // executed rows of all streams, stream after stream: row r of the launch is row r - pre[b] of
     // stream b (pre = exclusive prefix of the streams' counts)
+    uint2* list = reinterpret_cast<uint2*>(bsm + S * lay.stage_bytes + S * (kBulkInfoWords * 4 + 16));
     int32_t M = 0;
-    for (int b = 0; b < a.n_streams; ++b) M += *a.s[b].count;
+    if (a.compact) {
+        M = compact_into_list(a, list);
+    } else {
+        for (int b = 0; b < a.n_streams; ++b) M += *a.s[b].count;
+    }
     const int64_t C = (int64_t)a.n_heads * kHeadDim;
     const uint32_t row_bytes = (uint32_t)(C * (int64_t)sizeof(T));
     const int32_t rows_here =
@@ -284,17 +390,25 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
         int32_t issued = 0;
         for (int32_t kb = 0; ok && kb < rows_here; kb += 32) {
             const int32_t kl = kb + lane;
-            int32_t i = -1, sb = 0, m = 0;
+            int32_t i = -1, sb = 0, m = 0, mode = 0;
             if (kl < rows_here) {
-                m = (int32_t)blockIdx.x + kl * (int32_t)gridDim.x;
-                while (sb + 1 < a.n_streams && m >= *a.s[sb].count) m -= *a.s[sb++].count;
-                i = __ldg(a.s[sb].idx + m);
+                if (a.compact) {
+                    const uint2 e = list[kl];
+                    i = (int32_t)(e.x & 0x0FFFFFFFu);
+                    mode = (int32_t)(e.x >> 28);
+                    sb = (int32_t)(e.y >> 24);
+                    m = (int32_t)(e.y & 0x00FFFFFFu);
+                } else {
+                    m = (int32_t)blockIdx.x + kl * (int32_t)gridDim.x;
+                    while (sb + 1 < a.n_streams && m >= *a.s[sb].count) m -= *a.s[sb++].count;
+                    i = __ldg(a.s[sb].idx + m);
+                }
                 if (i < 0 || i >= a.n_tokens) i = -1;
             }
             // bookkeeping loads of the 32 rows, in flight while the row copies are issued
-            int32_t mode = 0, p[4] = {0, 0, 0, 0};
+            int32_t p[4] = {0, 0, 0, 0};
             if (i >= 0) {
-                mode = __ldg(a.s[sb].mask + i);
+                if (!a.compact) mode = __ldg(a.s[sb].mask + i);
 #pragma unroll
                 for (int ax = 0; ax < 4; ++ax)
                     if (ax < a.n_axes) p[ax] = __ldg(a.pos + (int64_t)i * a.n_axes + ax);

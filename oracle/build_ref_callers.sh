@@ -34,7 +34,7 @@ inc=(-I"$tree/src" -I"$repo/include")
 link=(-L"$lib" -lfxr -Xlinker -rpath -Xlinker '$ORIGIN/../../fluxrt-cpp_b200/lib' -Xlinker -rpath -Xlinker "$lib")
 nvcc -gencode arch=compute_100a,code=sm_100a -O2 -std=c++17 "${inc[@]}" \
   "$tree/src/spike/test_spatial_cache.cu" "${link[@]}" -o "$out/ref_test_spatial_cache"
-nvcc -O2 -std=c++17 "${inc[@]}" -x c++ "$tree/src/spike/test_gather_scatter.cpp" "${link[@]}" \
+nvcc -Wno-deprecated-gpu-targets -O2 -std=c++17 "${inc[@]}" -x c++ "$tree/src/spike/test_gather_scatter.cpp" "${link[@]}" \
   -lcudart -o "$out/ref_test_gather_scatter"
 echo "$out/ref_test_spatial_cache"
 echo "$out/ref_test_gather_scatter"
