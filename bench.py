@@ -383,12 +383,14 @@ def run_ours(args):
         "kernels": {"gather": mem,
                     "in_frame_us": {k[:-3]: round(v, 2) for k, v in kern.items()},
                     "isolated_us": {k[:-3]: round(v, 2) for k, v in iso.items()},
-                    "timing": "in_frame: event records between the four launches of each frame in "
-                              "a CUDA graph (each interval also holds one launch gap); isolated: 40 "
-                              "back-to-back launches of one kernel per graph; the attention roofline "
-                              "uses in_frame, the gather roofline isolated"},
+                    "timing": "the frame itself is 3 launches (the gather compacts the mask); in_frame: "
+                              "the frame's four steps through their own entry points (compaction, gather, "
+                              "attention, restore) with event records between them in a CUDA graph (each "
+                              "interval also holds one launch gap); isolated: 40 back-to-back launches of "
+                              "one step per graph; the attention roofline uses in_frame, the gather "
+                              "roofline isolated"},
         "e2e": e2e,
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": 3 * args.steps,
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -1149,7 +1151,7 @@ def run_streams(args, embedded: bool = False):
                    "n_tokens": w.n_tokens, "active": w.active, "heads": w.n_heads,
                    "parallelism": f"streams{total}-over-{world}",
                    "l2": f"{n_sets} rotating sets of every stream's inputs", "graph": bool(graphs)},
-        "e2e": None, "gpu_launches": 4 * args.steps, "clocks": clk,
+        "e2e": None, "gpu_launches": 3 * args.steps, "clocks": clk,
     }
     if rank == 0 and not embedded:
         print(json.dumps(out_line), flush=True)

@@ -65,8 +65,9 @@ constexpr uint32_t kRegsSoftmax = 200;
 constexpr uint32_t kRegsOther = 96;
 constexpr uint32_t kRegPool = 2 * 128 * kRegsSoftmax + 128 * kRegsOther;   // 63488 <= 384 x 166
 constexpr float kRescaleThreshold = 8.0f;       // log2 units
-constexpr int kPolyPeriod = 8;                  // of every 8 score pairs ...
-constexpr int kPolyCount = 2;                   // ... this many use ex2_poly2
+constexpr int kPolyPeriod = 4;                  // the last of every 4 score pairs uses ex2_poly2
+                                                // (spread evenly: measured 3 % shorter steps than
+                                                // two adjacent pairs of every 8)
 
 enum Bar : uint32_t {
     kQFull = 0,
@@ -413,7 +414,7 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
                         const float2 x = attn::ffma2(make_float2(__uint_as_float(s[2 * k]), __uint_as_float(s[2 * k + 1])),
                                                      c2, nm2);
                         float2 e;
-                        if ((k % kPolyPeriod) < kPolyCount) {
+                        if ((k % kPolyPeriod) == kPolyPeriod - 1) {
                             e = attn::ex2_poly2(x);
                         } else {
                             e = make_float2(ex2_approx(x.x), ex2_approx(x.y));

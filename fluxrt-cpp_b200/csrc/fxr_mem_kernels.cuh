@@ -368,6 +368,19 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
     __syncthreads();
     volatile int* abort = &abort_flag;
     pdl_launch_dependents();
+    // Warm L2 with the bookkeeping inputs while the preceding kernel finishes: the masks (compacting
+    // launches) or index lists, and the position ids. A prefetch brings nothing into the CTA, so it
+    // is safe before the dependency wait even for data the preceding kernel writes.
+    {
+        const int64_t t = (int64_t)blockIdx.x * kBulkThreads + threadIdx.x, stride = (int64_t)gridDim.x * kBulkThreads;
+        const int64_t mask_lines = ((int64_t)a.n_tokens * 4 + 127) / 128;
+        for (int b = 0; b < a.n_streams; ++b) {
+            const char* src = reinterpret_cast<const char*>(a.compact ? a.s[b].mask : a.s[b].idx);
+            for (int64_t l = t; l < mask_lines; l += stride) prefetch_l2(src + l * 128);
+        }
+        const int64_t pos_lines = ((int64_t)a.n_tokens * a.n_axes * 4 + 127) / 128;
+        for (int64_t l = t; l < pos_lines; l += stride) prefetch_l2(reinterpret_cast<const char*>(a.pos) + l * 128);
+    }
     pdl_wait();  // count / idx / mask come from the compaction
 
     // executed rows of all streams, stream after stream: row r of the launch is row r - pre[b] of
