@@ -240,17 +240,27 @@ def run_frame(cfg, fr, ws):
                       fr["norm_k"], fr["cache_k"], fr["cache_v"], fr["out"], ws)
 
 
+def attention_kernel_name(heads_per_launch: int) -> str:
+    """The attention kernel the library launches (launch_attention_streams in csrc/fxr_capi.cu):
+    the two-tile kernel, in its stream-K capable form when the workspace holds the scratch slots
+    (every bench workspace does; the kernel picks whole units or stream-K from M on the device);
+    FXR_ATTENTION_TILES=1 selects the one-tile kernel, which splits key ranges for at most 8 heads."""
+    if os.environ.get("FXR_ATTENTION_TILES", "") == "1":
+        return "fxr::attn::attention_kernel" + (" (key-range split)" if heads_per_launch <= 8 else "")
+    return "fxr::attn2::attention_kernel (stream-K capable)"
+
+
 def attn_flops(w, M: int) -> float:
     return 4.0 * M * w.n_tokens * HEAD_DIM * w.n_heads
 
 
 def gather_bytes(w, M: int) -> float:
-    """Algorithmic bytes of the gather/norm/RoPE/cache-write kernel: read Q,K,V rows, write
-    compact Q' and the K', V cache rows (6 rows of C elements per executed token), plus the index,
-    mask and position-id reads."""
+    """Algorithmic bytes of the compacting gather/norm/RoPE/cache-write kernel: read Q,K,V rows,
+    write compact Q' and the K', V cache rows (6 rows of C elements per executed token), the
+    executed tokens' position ids, and the mask scan (read the mask, write the index list)."""
     eb = 2
     C = w.n_heads * HEAD_DIM
-    return 6.0 * M * C * eb + M * (4 + 4 + 4 * len(w.rope_axes))
+    return 6.0 * M * C * eb + M * (4 + 4 * len(w.rope_axes)) + 4.0 * w.n_tokens
 
 
 def run_ours(args):
@@ -357,14 +367,14 @@ def run_ours(args):
     attn_us = kern["attention_us"]
     achieved = attn_flops(w, M_avg) / (attn_us * 1e-6) / 1e12
     traffic = profile_traffic(f"attention_{w.name}")
-    roof = {"bound": "tensor", "kernel": "fxr::attn::attention_kernel", "achieved": round(achieved, 1),
+    roof = {"bound": "tensor", "kernel": attention_kernel_name(w.n_heads), "achieved": round(achieved, 1),
             "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
             "peak_kind": f"{pk['source']} burst bf16 (cuBLAS)",
             "frac_of_nominal_2250": round(achieved / 2250.0, 4),
             "traffic": traffic, "algorithmic_flop_per_launch": attn_flops(w, M_avg)}
     g_us = iso["gather_us"]      # back-to-back launches: no event-record gap around the launch
     gb = gather_bytes(w, M_avg)
-    mem = {"kernel": "fxr::gather_bulk_kernel", "bound": "hbm", "us": round(g_us, 2),
+    mem = {"kernel": "fxr::gather_bulk_kernel (compacting)", "bound": "hbm", "us": round(g_us, 2),
            "achieved": round(gb / (g_us * 1e-6) / 1e9, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
            "frac": round(gb / (g_us * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
            "algorithmic_bytes_per_launch": gb, "traffic": profile_traffic(f"gather_{w.name}")}
@@ -383,12 +393,11 @@ def run_ours(args):
         "kernels": {"gather": mem,
                     "in_frame_us": {k[:-3]: round(v, 2) for k, v in kern.items()},
                     "isolated_us": {k[:-3]: round(v, 2) for k, v in iso.items()},
-                    "timing": "the frame itself is 3 launches (the gather compacts the mask); in_frame: "
-                              "the frame's four steps through their own entry points (compaction, gather, "
-                              "attention, restore) with event records between them in a CUDA graph (each "
-                              "interval also holds one launch gap); isolated: 40 back-to-back launches of "
-                              "one step per graph; the attention roofline uses in_frame, the gather "
-                              "roofline isolated"},
+                    "timing": "the frame's 3 launches (compacting gather, attention, restore) through "
+                              "fxr_frame_step on the frame's workspace; in_frame: event records between "
+                              "them in a CUDA graph, mean over frames (each interval also holds one "
+                              "launch gap); isolated: 40 back-to-back launches of one step per graph; the "
+                              "attention roofline uses in_frame, the gather roofline isolated"},
         "e2e": e2e,
         "gpu_launches": 3 * args.steps,
         "clocks": clk,
@@ -440,30 +449,38 @@ def sub_records(args, world: int) -> dict:
     return recs
 
 
+def run_step(cfg, fr, ws, step):
+    import fxr
+    fxr.frame_step(step, cfg, fr["q"], fr["k"], fr["v"], fr["mask"], None, fr["pos"], fr["norm_q"],
+                   fr["norm_k"], fr["cache_k"], fr["cache_v"], fr["out"], ws)
+
+
+# The frame's three launches as fxr_frame_step runs them (same workspace, same schedule).
+FRAME_STEPS = (("gather_us", 2), ("attention_us", 3), ("restore_us", 4))
+
+
 def per_kernel_times(cfg, w, frames, wss, stream, reps: int):
-    """Per-kernel device time: the four launches of `reps` frames are captured in one CUDA graph
-    with event records between them (on the launching stream), so host launch overhead does not
-    leak into the intervals; median over frames."""
+    """Per-kernel device time inside a stream of frames: the frame's three launches (compacting
+    gather, attention, restore; fxr_frame_step on the frame's own workspace) of `reps` frames are
+    captured in one CUDA graph with event records between them (on the launching stream), so host
+    launch overhead does not leak into the intervals. Mean over frames: event timestamps inside a
+    graph advance in steps of about 2 us on this GPU, so a median would land on a tick; the mean
+    over frames (whose phase against the tick varies) does not, and it pairs with the mean
+    executed-row count."""
     import torch
     ev = lambda: torch.cuda.Event(enable_timing=True, external=True)
-    names = ["compact_us", "gather_us", "attention_us", "restore_us"]
-    events = [[ev() for _ in range(5)] for _ in range(reps)]
+    names = [n for n, _ in FRAME_STEPS]
+    events = [[ev() for _ in range(len(names) + 1)] for _ in range(reps)]
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         s = torch.cuda.current_stream()
         for i in range(reps):
             fr, ws = frames[i % len(frames)], wss[i % len(wss)]
-            idx, cnt, qc, ld_qc, save = __import__("fxr").workspace_views(cfg, ws)
             e = events[i]
             e[0].record(s)
-            _raw_compact(fr, idx, cnt)
-            e[1].record(s)
-            _raw_gather(cfg, fr, idx, cnt, qc, ld_qc, save)
-            e[2].record(s)
-            _raw_attention(cfg, fr, qc, ld_qc, cnt, idx)
-            e[3].record(s)
-            _raw_restore(cfg, fr, idx, cnt, save)
-            e[4].record(s)
+            for k, (_, step) in enumerate(FRAME_STEPS):
+                run_step(cfg, fr, ws, step)
+                e[k + 1].record(s)
     g.replay()
     torch.cuda.synchronize()
     g.replay()
@@ -474,42 +491,22 @@ def per_kernel_times(cfg, w, frames, wss, stream, reps: int):
         for k, name in enumerate(names):
             acc[name].append(e[k].elapsed_time(e[k + 1]) * 1e3)
     del g
-    return {k: statistics.median(v) for k, v in acc.items()}
+    return {k: statistics.mean(v) for k, v in acc.items()}
 
 
 def isolated_kernel_times(cfg, frames, wss, reps: int):
-    """Per-kernel device time of `reps` back-to-back launches of one step kernel alone (rotating
-    input sets, one CUDA graph, CUDA events around its replay on the launching stream), after the
-    frames have run once so that the compaction results exist. Every step is idempotent on its
+    """Per-kernel device time of `reps` back-to-back launches of one of the frame's steps alone
+    (rotating input sets, one CUDA graph, CUDA events around its replay on the launching stream),
+    after the frames have run once so that the index lists exist. Every step is idempotent on its
     inputs. Mean per launch, median of 5 replays."""
     import torch
-    import fxr
-    views = [fxr.workspace_views(cfg, ws) for ws in wss]
     n = len(frames)
-
-    def k_compact(i):
-        idx, cnt, qc, ld_qc, save = views[i % n]
-        _raw_compact(frames[i % n], idx, cnt)
-
-    def k_gather(i):
-        idx, cnt, qc, ld_qc, save = views[i % n]
-        _raw_gather(cfg, frames[i % n], idx, cnt, qc, ld_qc, save)
-
-    def k_attention(i):
-        idx, cnt, qc, ld_qc, save = views[i % n]
-        _raw_attention(cfg, frames[i % n], qc, ld_qc, cnt, idx)
-
-    def k_restore(i):
-        idx, cnt, qc, ld_qc, save = views[i % n]
-        _raw_restore(cfg, frames[i % n], idx, cnt, save)
-
     out = {}
-    for name, fn in (("compact_us", k_compact), ("gather_us", k_gather),
-                     ("attention_us", k_attention), ("restore_us", k_restore)):
+    for name, step in FRAME_STEPS:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             for i in range(reps):
-                fn(i)
+                run_step(cfg, frames[i % n], wss[i % n], step)
         g.replay()
         torch.cuda.synchronize()
         ts = []
@@ -523,42 +520,6 @@ def isolated_kernel_times(cfg, frames, wss, reps: int):
         out[name] = statistics.median(ts)
         del g
     return out
-
-
-def _s():
-    import torch
-    return torch.cuda.current_stream().cuda_stream
-
-
-def _raw_compact(fr, idx, cnt):
-    import fxr
-    fxr._check(fxr.load().fxr_mask_compact(fr["mask"].data_ptr(), None, fr["mask"].numel(), idx, cnt, _s()))
-
-
-def _raw_gather(cfg, fr, idx, cnt, qc, ld_qc, save):
-    import ctypes
-    import fxr
-    d = cfg.desc()
-    fxr._check(fxr.load().fxr_gather_norm_rope(
-        ctypes.byref(d), fr["q"].data_ptr(), fr["k"].data_ptr(), fr["v"].data_ptr(),
-        fr["mask"].data_ptr(), idx, cnt, fr["pos"].data_ptr(), fr["norm_q"].data_ptr(),
-        fr["norm_k"].data_ptr(), qc, ld_qc, fr["cache_k"].data_ptr(), fr["cache_v"].data_ptr(), save, _s()))
-
-
-def _raw_attention(cfg, fr, qc, ld_qc, cnt, idx):
-    import ctypes
-    import fxr
-    d = cfg.desc()
-    fxr._check(fxr.load().fxr_attention_active(ctypes.byref(d), qc, ld_qc, cnt, fr["cache_k"].data_ptr(),
-                                               fr["cache_v"].data_ptr(), idx, fr["out"].data_ptr(), _s()))
-
-
-def _raw_restore(cfg, fr, idx, cnt, save):
-    import ctypes
-    import fxr
-    d = cfg.desc()
-    fxr._check(fxr.load().fxr_restore_rows(ctypes.byref(d), fr["mask"].data_ptr(), idx, cnt, save,
-                                           fr["cache_k"].data_ptr(), fr["cache_v"].data_ptr(), _s()))
 
 
 def e2e_measure(cfg, w, frames, wss, stream, reps: int, world: int = 1):
@@ -1023,15 +984,18 @@ def run_heads(args, embedded: bool = False):
                    "l2": f"{n_sets} rotating input sets, cache shards {n_sets * shard_bytes / 2**20:.0f} MiB > L2",
                    "graph": use_graph},
         "roofline": {"bound": "tensor" if t_tensor >= t_link else "nvlink",
-                     "kernel": ("fxr::attn::attention_kernel + NCCL all-gather + heads_scatter_kernel"
-                                if nccl else "fxr::attn::attention_kernel (epilogue stores to every rank)"),
+                     "kernel": (attention_kernel_name(max(_heads_split(w.n_heads, world)))
+                                + ("" if world == 1 else " + NCCL all-gather + heads_scatter_kernel" if nccl
+                                   else " + heads_push_kernel (peer stores to every rank)")),
                      "target_us": round(max(t_tensor, t_link) * 1e6, 2),
                      "achieved_frac": round(max(t_tensor, t_link) * 1e3 / ms_per_step, 4),
                      "peak_tensor": pk["bf16_tflops"], "peak_nvlink_gbs": 770.0,
                      "nvlink_bytes_per_rank": nvlink_bytes,
                      "note": "frac = roofline time of one frame / measured frame time (whole frame, 5 kernels)"},
         "e2e": None,
-        "gpu_launches": (6 if nccl else 5) * args.steps,   # + NCCL's own kernel per frame when nccl
+        # compaction, gather, attention, restore; with peers also the row numbering and the exchange
+        # (heads_push_kernel, or heads_scatter_kernel after NCCL's own all-gather kernel)
+        "gpu_launches": (4 if world == 1 else 6) * args.steps,
         "clocks": clk,
     }
     if rank == 0 and not embedded:

@@ -2,13 +2,16 @@
 //
 // Work unit: two 128-row tiles of compact queries of one head (256 rows) against all N keys of
 // that head, in steps of 128 keys. Persistent CTAs walk the units round-robin; M is read on the
-// device. The two tiles run as two dependency chains that the tensor core interleaves, so that the
-// softmax of one tile overlaps the products of the other:
+// device. When whole units would leave SMs idle (fewer units than SMs, or a last wave that is
+// mostly empty), the kSplit instantiation runs a stream-K schedule instead: the (unit, key step)
+// iterations are cut into one contiguous range per CTA, and units cut between CTAs are combined
+// through L2 (choose_schedule below). The two tiles run as two dependency chains that the tensor
+// core interleaves, so that the softmax of one tile overlaps the products of the other:
 //   tile i, step j:  S_i = Q_i K_j^T  ->  softmax_i(j): P_i  ->  O_i += P_i V_j  ->  S_i(j+1) ...
 // Warp roles (384 threads, three warpgroups):
 //   warps 0-3   softmax of tile 0: one thread per query row (TMEM lane), all 128 scores of a step
 //   warps 4-7   softmax of tile 1
-//   warp 8      TMA producer: Q_0, Q_1 and a 4-slot ring of 128-key K and V tiles in the tensor
+//   warp 8      TMA producer: Q_0, Q_1 and a 5-slot ring of 128-key K and V tiles in the tensor
 //               core's consumption order K_0 V_0 K_1 V_1 ... (128-byte swizzle)
 //   warp 9      TMEM allocator and the single MMA-issuing thread
 //   warps 10-11 idle (they complete the third warpgroup)
@@ -28,7 +31,7 @@
 // Every mbarrier wait is bounded (2 s); on timeout the kernel sets the device error word, drains its
 // outstanding copies and products, frees its tensor memory and returns.
 // Replaces attention_fwd (attention_kernels.cu:85-173) and scatter_tokens
-// (gather_scatter_kernels.cu:46-72) on this path, for launches that need no key-range split.
+// (gather_scatter_kernels.cu:46-72) on this path.
 #pragma once
 
 #include "fxr_attention.cuh"
@@ -62,8 +65,8 @@ constexpr uint32_t kColS = 0, kColO = 256;      // + tile * 128
 // less (setmaxnreg). The launch gives the CTA kThreads x (registers per thread) registers; the two
 // shares must fit in it, which the host checks against the compiled register count before launch.
 constexpr uint32_t kRegsSoftmax = 200;
-constexpr uint32_t kRegsOther = 96;
-constexpr uint32_t kRegPool = 2 * 128 * kRegsSoftmax + 128 * kRegsOther;   // 63488 <= 384 x 166
+constexpr uint32_t kRegsOther = 104;            // the producer / MMA loops compile without spills
+constexpr uint32_t kRegPool = 2 * 128 * kRegsSoftmax + 128 * kRegsOther;   // 64512 = 384 x 168
 constexpr float kRescaleThreshold = 8.0f;       // log2 units
 constexpr int kPolyPeriod = 4;                  // the last of every 4 score pairs uses ex2_poly2
                                                 // (spread evenly: measured 3 % shorter steps than
@@ -84,8 +87,170 @@ enum Bar : uint32_t {
 };
 constexpr uint32_t kSlotTmem = kNumBars * 8;
 constexpr uint32_t kSlotAbort = kSlotTmem + 4;
-static_assert(kSlotAbort + 8 <= 256, "barrier area overflow");
+constexpr uint32_t kSlotCursor = kSlotAbort + 4;   // [softmax warp] {next, end} of its item walk
+static_assert(kSlotCursor % 8 == 0 && kSlotCursor + 8 * kSoftmaxWarps <= 256, "barrier area overflow");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
+
+// Stream-K schedule (the kSplit instantiation): CTA c takes the iterations [c * per, (c+1) * per)
+// of the (unit, key step) space, unit-major. Its first and last items may cover part of a unit
+// only; such a part writes its tiles' unnormalised O rows with their running maxima and sums to
+// scratch slots (per CTA two items x two tiles, column chunk-major so that a warp's stores are
+// contiguous). Per (unit, softmax warp) an arrival counter elects the part that arrives last; its
+// warp combines every part of its 32 rows in key order (the result does not depend on which CTA
+// came last) and stores them. A unit cut between CTAs has its last part in the CTA c_last that
+// holds its final step; no other cut unit ends there, so c_last indexes its counters.
+// Costs in 128-key steps of both tiles (~1.7-2 us each): the fixed cost of an item (Q tiles,
+// pipeline ramp, epilogue) and the extra cost of each cut end of a CTA's range (partial write,
+// counter, combine through L2). Fitted to measured frames: a 2048^2 frame's 288 units of 132 steps
+// run faster as two rounds of whole units (585.6 us) than as stream-K (627.8 us), a 1024^2 frame's
+// 96 units of 36 steps faster as stream-K (84.7 -> 79.9 us per frame).
+constexpr float kItemOverheadSteps = 2.0f;
+constexpr float kCutOverheadSteps = 4.5f;
+constexpr int kSlotsPerCta = 4;    // scratch slots (one tile's partial each) a stream-K CTA may use
+
+struct Sched {
+    int32_t n_units;
+    int32_t n_steps;
+    int32_t per;                   // stream-K iterations per CTA; 0: whole units round-robin
+};
+
+// The schedule of a launch, the same on every thread of every CTA (a function of M, the grid and
+// the scratch only): stream-K when its estimated time (iterations per CTA + item overheads) beats
+// whole units (CTA rounds x steps per unit).
+__device__ __forceinline__ Sched choose_schedule(int32_t n_units, int32_t n_steps, int32_t grid,
+                                                 int32_t slots, bool allow) {
+    Sched sc{n_units, n_steps, 0};
+    if (!allow || slots < kSlotsPerCta * grid || n_units <= 0) return sc;
+    const float whole = (float)((n_units + grid - 1) / grid) * ((float)n_steps + kItemOverheadSteps);
+    const int32_t per = (int32_t)(((int64_t)n_units * n_steps + grid - 1) / grid);
+    const int32_t items = (per + n_steps - 1) / n_steps + 1;      // at most, counting both cut ends
+    const float sk = (float)per + kItemOverheadSteps * (float)items + 2.0f * kCutOverheadSteps;
+    if (sk < whole) sc.per = per;
+    return sc;
+}
+
+// A CTA's walk over its items. Whole units: cur is the unit (stride: the grid). Stream-K: cur is
+// the next iteration, end the CTA's last + 1.
+struct Cursor {
+    int32_t cur, end;
+};
+
+__device__ __forceinline__ Cursor first_cursor(const Sched& sc) {
+    if (sc.per == 0) return Cursor{(int32_t)blockIdx.x, sc.n_units};
+    const int32_t a = (int32_t)blockIdx.x * sc.per;
+    return Cursor{a, min(sc.n_units * sc.n_steps, a + sc.per)};
+}
+
+// The next item of the walk: unit u and its key steps [s0, s1). False when the CTA is done.
+__device__ __forceinline__ bool next_item(const Sched& sc, Cursor& c, int32_t& u, int32_t& s0, int32_t& s1) {
+    if (c.cur >= c.end) return false;
+    if (sc.per == 0) {
+        u = c.cur;
+        s0 = 0;
+        s1 = sc.n_steps;
+        c.cur += gridDim.x;
+        return true;
+    }
+    u = c.cur / sc.n_steps;
+    s0 = c.cur - u * sc.n_steps;
+    s1 = min(sc.n_steps, s0 + (c.end - c.cur));
+    c.cur += s1 - s0;
+    return true;
+}
+
+// Scratch slot of the part of unit u that CTA c runs, tile t: its first item (slot pair 0) unless
+// the unit starts inside the CTA's range after other items (pair 1).
+__device__ __forceinline__ size_t part_slot(const Sched& sc, int32_t u, int32_t c, int t) {
+    const int32_t c_first = (int32_t)((int64_t)u * sc.n_steps / sc.per);
+    const int k = (c == c_first && u * sc.n_steps > c * sc.per) ? 1 : 0;
+    return ((size_t)c * 2 + k) * 2 + t;
+}
+
+// The last part of unit u combines row r of tile t over every part (CTAs c_first..c_last, in key
+// order) and stores it to out_row (nullptr: padding row, or a bad index already flagged).
+template <typename T>
+__device__ __forceinline__ void combine_store(const float* scratch, const Sched& sc, int32_t u, int t, int r,
+                                              T* out_row) {
+    const int32_t c0 = (int32_t)((int64_t)u * sc.n_steps / sc.per);
+    const int32_t c1 = (int32_t)(((int64_t)(u + 1) * sc.n_steps - 1) / sc.per);
+    float m_all = -INFINITY;
+    for (int32_t c = c0; c <= c1; ++c)
+        m_all = fmaxf(m_all, __ldcg(scratch + part_slot(sc, u, c, t) * attn::kSplitSlotFloats + kBM * kD + r));
+    float acc[kD];
+#pragma unroll
+    for (int k = 0; k < kD; ++k) acc[k] = 0.f;
+    float l_tot = 0.f;
+    for (int32_t c = c0; c <= c1; ++c) {
+        const float* sq = scratch + part_slot(sc, u, c, t) * attn::kSplitSlotFloats;
+        const float a = ex2_approx(__ldcg(sq + kBM * kD + r) - m_all);
+        l_tot += a * __ldcg(sq + kBM * kD + kBM + r);
+        const float4* oq = reinterpret_cast<const float4*>(sq);
+#pragma unroll
+        for (int q = 0; q < kD / 4; ++q) {
+            const float4 x = __ldcg(oq + q * kBM + r);
+            acc[4 * q] += a * x.x;
+            acc[4 * q + 1] += a * x.y;
+            acc[4 * q + 2] += a * x.z;
+            acc[4 * q + 3] += a * x.w;
+        }
+    }
+    if (out_row == nullptr) return;
+    const float inv = 1.0f / l_tot;
+    uint4* dst = reinterpret_cast<uint4*>(out_row);
+#pragma unroll
+    for (int k = 0; k < kD / 8; ++k) {
+        uint4 v;
+        v.x = StoreT<T>::pack2(acc[8 * k + 0] * inv, acc[8 * k + 1] * inv);
+        v.y = StoreT<T>::pack2(acc[8 * k + 2] * inv, acc[8 * k + 3] * inv);
+        v.z = StoreT<T>::pack2(acc[8 * k + 4] * inv, acc[8 * k + 5] * inv);
+        v.w = StoreT<T>::pack2(acc[8 * k + 6] * inv, acc[8 * k + 7] * inv);
+        dst[k] = v;
+    }
+}
+
+// End of an item that covers part of a cut unit (stream-K schedule): the part's O rows, maxima and
+// sums go to its scratch slot, then O is released to the MMA thread (kOFree); the warp whose arrival
+// completes the unit combines every part of its 32 rows and stores them. Kept out of line: inlined,
+// this rarely run code changed the code of the step loop around it enough to slow whole-unit
+// schedules of the same kernel by up to 20 % (measured), which a call does not.
+template <typename T>
+__device__ __noinline__ void cut_unit_epilogue(float* scratch, int32_t* split_cnt, int32_t n_tokens,
+                                               int64_t ld_out, T* out, const Sched sc, int32_t u,
+                                               int32_t head, int t, int r, int warp, uint32_t tO,
+                                               float m_run, float l_run, uint32_t ofree_bar, bool live,
+                                               int32_t orow) {
+    const uint32_t lane = lane_id();
+    float* slot = scratch + part_slot(sc, u, (int32_t)blockIdx.x, t) * attn::kSplitSlotFloats;
+    float4* od = reinterpret_cast<float4*>(slot);
+#pragma unroll 1
+    for (int h = 0; h < 4; ++h) {
+        uint32_t o[32];
+        FXR_TMEM_LD32(tO + h * 32u, o);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            od[(h * 8 + k) * kBM + r] = make_float4(__uint_as_float(o[4 * k]), __uint_as_float(o[4 * k + 1]),
+                                                    __uint_as_float(o[4 * k + 2]), __uint_as_float(o[4 * k + 3]));
+    }
+    slot[kBM * kD + r] = m_run;
+    slot[kBM * kD + kBM + r] = l_run;
+    tc_fence_before();
+    mbar_arrive(ofree_bar);
+    __threadfence();
+    __syncwarp();
+    const int32_t c_first = (int32_t)((int64_t)u * sc.n_steps / sc.per);
+    const int32_t c_last = (int32_t)(((int64_t)(u + 1) * sc.n_steps - 1) / sc.per);
+    int32_t* cnt = split_cnt + c_last * attn::kSplitPortions + warp;
+    int32_t prev = 0;
+    if (lane == 0) prev = atomicAdd(cnt, 1);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != c_last - c_first) return;
+    // the last part to arrive combines these 32 rows
+    if (lane == 0) *cnt = 0;      // for the next launch
+    __threadfence();
+    const bool store = live && orow >= 0 && orow < n_tokens;
+    if (live && !store) atomicOr(&g_error_word, kErrBounds);
+    combine_store<T>(scratch, sc, u, t, r, store ? out + (int64_t)orow * ld_out + (int64_t)head * kD : nullptr);
+}
 
 // Work unit u of the launch -> stream b, head and first compact row of tile 0. Units are numbered
 // stream after stream, (row pair, head) within a stream as pair + head * pairs, so that the CTAs
@@ -111,7 +276,7 @@ __device__ __forceinline__ void decode_pair_unit(const Params& p, int32_t u, int
     row0 = (u - head * pairs) * kRows;
 }
 
-template <typename T>
+template <typename T, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
 attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
@@ -168,6 +333,7 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
     for (int b = 0; b < kMaxBatch; ++b)
         if (b < p.n_streams) n_units += (*p.s[b].count + kRows - 1) / kRows * p.n_heads;
     const int32_t n_steps = (p.n_tokens + kBN - 1) / kBN;
+    const Sched sc = choose_schedule(n_units, n_steps, (int32_t)gridDim.x, p.split_slots, kSplit);
 
     if (warp >= kSoftmaxWarps) {
       // warpgroup 2: producer, MMA issuer and two idle warps
@@ -187,9 +353,11 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
                 ++it;
                 return true;
             };
-            for (int32_t w = blockIdx.x; ok && w < n_units; w += gridDim.x) {
+            Cursor cur = first_cursor(sc);
+            int32_t u, s0, s1;
+            while (ok && next_item(sc, cur, u, s0, s1)) {
                 int32_t b, head, row0, m_b;
-                decode_pair_unit(p, w, b, head, row0, m_b);
+                decode_pair_unit(p, u, b, head, row0, m_b);
                 const CUtensorMap* tmQ = &maps.q[0];
                 const CUtensorMap* tmK = &maps.k[0];
                 const CUtensorMap* tmV = &maps.v[0];
@@ -208,10 +376,10 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
                     tma_load_2d(dq + kHalfBytes, tmQ, bar(kQFull), head * kD + 64, row0 + t * kBM);
                 }
                 ++q_it;
-                ok = load(tmK, head, 0);
-                for (int32_t j = 0; ok && j < n_steps; ++j) {
+                ok = load(tmK, head, s0 * kBN);
+                for (int32_t j = s0; ok && j < s1; ++j) {
                     ok = load(tmV, head, j * kBN);
-                    if (ok && j + 1 < n_steps) ok = load(tmK, head, (j + 1) * kBN);
+                    if (ok && j + 1 < s1) ok = load(tmK, head, (j + 1) * kBN);
                 }
             }
             if (*abort) {
@@ -270,7 +438,10 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
             // Per step the tensor core alternates between the tiles: O_0 += P_0 V_j (in two halves of
             // keys, the first as soon as its probabilities are stored), S_0(j+1), O_1 += P_1 V_j,
             // S_1(j+1); the softmax of one tile runs while the other tile's products execute.
-            for (int32_t w = blockIdx.x; ok && w < n_units; w += gridDim.x) {
+            Cursor cur = first_cursor(sc);
+            int32_t u, s0, s1;
+            while (ok && next_item(sc, cur, u, s0, s1)) {
+                const int32_t nst = s1 - s0;
                 if (!wait(bar(kQFull), q_it & 1)) { ok = false; break; }
                 ++q_it;
                 // the previous unit's last products read P_t from S_t: S_t may be rewritten once
@@ -286,11 +457,11 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
                 qk(0, sK);
                 qk(1, sK);
                 release();
-                if (n_steps == 1) umma_commit(bar(kQEmpty));
-                for (int32_t j = 0; j < n_steps; ++j, ++g) {
+                if (nst == 1) umma_commit(bar(kQEmpty));
+                for (int32_t j = 0; j < nst; ++j, ++g) {
                     const uint32_t sV = acquire();
                     if (!sV) { ok = false; break; }
-                    const bool more = j + 1 < n_steps;
+                    const bool more = j + 1 < nst;
                     for (int t = 0; t < 2; ++t) {
                         if (!wait(bar(kPHalf0 + t), g & 1)) { ok = false; break; }
                         if (j == 0 && units_done > 0 && !wait(bar(kOFree + t), (units_done - 1) & 1)) {
@@ -315,7 +486,7 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
                             qk(t, sK);
                             if (t == 1) {
                                 release();                            // K_{j+1}
-                                if (j + 2 == n_steps) umma_commit(bar(kQEmpty));
+                                if (j + 2 == nst) umma_commit(bar(kQEmpty));
                             }
                         }
                     }
@@ -348,16 +519,30 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
         uint32_t s_it = 0, units_done = 0;
         bool ok = true;
         int32_t* orow_slot = reinterpret_cast<int32_t*>(gbase + kSmemRowIdx) + threadIdx.x;
-        for (int32_t w = blockIdx.x; ok && w < n_units; w += gridDim.x) {
+        // The walk's cursor is kept in shared memory (a slot per warp, written by every lane with
+        // the same value): across the step loop only its countdown stays in registers.
+        volatile int32_t* wcur = reinterpret_cast<volatile int32_t*>(gbase + kSmemBar + kSlotCursor) + 2 * warp;
+        {
+            const Cursor c0 = first_cursor(sc);
+            wcur[0] = c0.cur;
+            wcur[1] = c0.end;
+        }
+        while (ok) {
+            int32_t u, s0, s1;
+            {
+                Cursor cc{wcur[0], wcur[1]};
+                if (!next_item(sc, cc, u, s0, s1)) break;
+                wcur[0] = cc.cur;
+            }
             int32_t b, head, row0, m_b;
-            decode_pair_unit(p, w, b, head, row0, m_b);
+            decode_pair_unit(p, u, b, head, row0, m_b);
             const int32_t row = row0 + t * kBM + r;
             const bool live = row < m_b;
             // the output row and stream of this thread, loaded now (kept in shared memory: the step
             // loop has no register to spare) so that the epilogue does not wait on a global load
             orow_slot[0] = live ? __ldg(p.s[b].idx + row) : -1;
             float m_run = -INFINITY, l_run = 0.f;
-            for (int32_t j = 0; j < n_steps; ++j, ++s_it) {
+            for (int32_t j = s0; j < s1; ++j, ++s_it) {
                 if (!wwait(bar(kSFull + t), s_it & 1)) { ok = false; break; }
                 tc_fence_after();
                 uint32_t s[128];
@@ -381,7 +566,7 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
                                              fmaxf(mp[6], mp[7])) * c;
                 float alpha = 1.f;
                 bool rescale = false;
-                if (j == 0) {
+                if (j == s0) {
                     m_run = mx;
                 } else if (__any_sync(0xffffffffu, live && mx > m_run + kRescaleThreshold)) {
                     const float m_new = fmaxf(m_run, mx);
@@ -433,6 +618,20 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
             // epilogue: O is final once the last product of the tile has completed
             if (!wwait(bar(kPVDone + t), (s_it - 1) & 1)) { ok = false; break; }
             tc_fence_after();
+            if (kSplit && sc.per > 0) {
+                // the item again, from the cursor (its end iteration), not kept across the loop
+                const int32_t it_end = wcur[0];
+                u = (it_end - 1) / n_steps;
+                s1 = it_end - u * n_steps;
+                s0 = max(0, (int32_t)blockIdx.x * sc.per - u * n_steps);
+            }
+            if (kSplit && sc.per > 0 && (s0 > 0 || s1 < n_steps)) {
+                cut_unit_epilogue<T>(p.split_scratch, p.split_cnt, p.n_tokens, p.ld_out,
+                                     static_cast<T*>(attn::stream_out(p, b)), sc, u, head, t, r, warp, tO,
+                                     m_run, l_run, bar(kOFree + t), live, *orow_slot);
+                ++units_done;
+                continue;
+            }
             const int32_t i = *orow_slot;
             const bool store = live && i >= 0 && i < p.n_tokens;
             if (live && !store) atomicOr(&g_error_word, kErrBounds);

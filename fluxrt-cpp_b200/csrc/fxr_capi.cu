@@ -23,13 +23,26 @@
 #include "fxr_gemm.cuh"
 #include "fxr_mem_kernels.cuh"
 
-// Built-in frame scratch of fxr_frame_forward_noalloc (see that function). 96 MiB holds the
-// workspace of a 1024x1024 frame (4608 tokens, 24 heads, 16-bit storage: ~85 MB). Every GPU that
-// loads this library keeps this array for the life of the process.
-constexpr size_t kNoAllocScratchBytes = size_t(96) << 20;
+#include <nvtx3/nvToolsExt.h>
+
+// Built-in frame scratch of fxr_frame_forward_noalloc (see that function). 128 MiB holds the
+// workspace of a 1024x1024 frame (4608 tokens, 24 heads, 16-bit storage: ~85 MB) with the scratch
+// slots of the attention's stream-K schedule (~39 MB on 148 SMs). Every GPU that loads this
+// library keeps this array for the life of the process.
+constexpr size_t kNoAllocScratchBytes = size_t(128) << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
+
+// NVTX range over a host-side scope (an entry point, one step's launch), named "fxr:<step>":
+// profilers that record NVTX (ncu --nvtx, Nsight Systems) attribute the kernels launched inside it.
+// Without a tool attached a push / pop is a check of a function pointer.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 thread_local std::string t_last_error;
 
@@ -221,7 +234,7 @@ Views carve(const fxr_frame_desc* d, void* ws) {
 // partial-result slot of the attention. A workspace of at least the base size works without it;
 // fxr_workspace_size includes room for kSplitSlotsPerSm slots per SM.
 constexpr int kSplitSlotsPerSm = 4;
-constexpr int kSplitMaxHeads = 8;   // launches with at most this many heads may split key ranges
+constexpr int kSplitMaxHeads = 8;   // one-tile kernel: launches with at most this many heads may split key ranges
 constexpr size_t kSplitSlotBytes = (size_t)fxr::attn::kSplitSlotFloats * sizeof(float);
 constexpr size_t kSplitCntBytes = (size_t)fxr::attn::kSplitPortions * sizeof(int32_t);
 
@@ -235,11 +248,12 @@ size_t split_bytes(int32_t slots) {
     return align_up((size_t)slots * kSplitCntBytes, 256) + (size_t)slots * kSplitSlotBytes;
 }
 
-// Launches with more than kSplitMaxHeads heads never split: no area, so the compaction zeroes no
-// arrival counters for them.
+// The scratch slots and arrival counters that a workspace leaves after its base part (none when it
+// ends there): key-range split of the one-tile kernel, stream-K schedule of the two-tile kernel.
 SplitArea split_area(size_t base, void* ws, size_t ws_bytes, int32_t n_heads) {
     SplitArea a;
-    if (!ws || ws_bytes <= base || n_heads > kSplitMaxHeads) return a;
+    (void)n_heads;
+    if (!ws || ws_bytes <= base) return a;
     const int32_t max_slots = kSplitSlotsPerSm * sm_count();
     int32_t slots = (int32_t)std::min<size_t>(max_slots, (ws_bytes - base) / (kSplitSlotBytes + kSplitCntBytes));
     while (slots > 0 && split_bytes(slots) > ws_bytes - base) --slots;
@@ -294,6 +308,7 @@ struct AttnStreamArgs {
 template <typename T>
 int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, const AttnStreamArgs* st,
                                  const SplitArea& split, cudaStream_t stream) {
+    NvtxRange nvtx_("fxr:attention");
     if (n_streams < 1 || n_streams > fxr::kMaxBatch) return fail(FXR_ERR_INVALID, "1..%d streams per launch", fxr::kMaxBatch);
     static bool configured[kMaxDevices] = {false};
     static bool pairs_ok[kMaxDevices] = {false};
@@ -307,14 +322,19 @@ int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, con
             e = cudaFuncSetAttribute(fxr::attn::attention_kernel<T, true>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fxr::attn::kSmemBytes);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(fxr::attn2::attention_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)fxr::attn2::kSmemBytes);
+            e = cudaFuncSetAttribute(fxr::attn2::attention_kernel<T, false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fxr::attn2::kSmemBytes);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(fxr::attn2::attention_kernel<T, true>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fxr::attn2::kSmemBytes);
         // the two-tile kernel redistributes its launch registers between warpgroups (setmaxnreg):
         // it only runs when the compiled register count gives the CTA enough of them
-        cudaFuncAttributes fa{};
-        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, fxr::attn2::attention_kernel<T>);
+        cudaFuncAttributes fa{}, fs{};
+        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, fxr::attn2::attention_kernel<T, false>);
+        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fs, fxr::attn2::attention_kernel<T, true>);
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
-        pairs_ok[dev] = (uint32_t)fa.numRegs * (uint32_t)fxr::attn2::kThreads >= fxr::attn2::kRegPool;
+        pairs_ok[dev] = (uint32_t)fa.numRegs * (uint32_t)fxr::attn2::kThreads >= fxr::attn2::kRegPool &&
+                        (uint32_t)fs.numRegs * (uint32_t)fxr::attn2::kThreads >= fxr::attn2::kRegPool;
         configured[dev] = true;
     }
     const int64_t C = (int64_t)d->n_heads * d->head_dim;
@@ -340,18 +360,22 @@ int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, con
     p.n_heads = d->n_heads;
     const float scale = d->softmax_scale > 0.f ? d->softmax_scale : 1.0f / std::sqrt((float)d->head_dim);
     p.scale_log2 = scale * 1.4426950408889634f;
-    // few heads per launch (a GPU's share of a head-split frame, small models): the query tiles x
-    // heads may leave SMs idle, so launch the instantiation that can split key ranges, on every SM
-    // (the kernel decides on the device how many parts each unit gets; CTAs without an item exit)
-    const bool split_ok = split.slots > 0 && d->n_heads <= kSplitMaxHeads;
     cudaError_t e;
-    if (!split_ok && attention_pairs() && dev >= 0 && dev < kMaxDevices && pairs_ok[dev]) {
-        // two query tiles per CTA (fxr_attention2.cuh)
+    if (attention_pairs() && dev >= 0 && dev < kMaxDevices && pairs_ok[dev]) {
+        // two query tiles per CTA (fxr_attention2.cuh). With scratch slots for a stream-K schedule,
+        // the instantiation that can run it, on every SM (the kernel chooses on the device, from M;
+        // CTAs without an item exit)
+        const bool sk = split.slots >= fxr::attn2::kSlotsPerCta * sm_count();
         const int64_t units = (N + fxr::attn2::kRows - 1) / fxr::attn2::kRows * d->n_heads * n_streams;
-        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(units, sm_count()));
-        e = launch_pdl(fxr::attn2::attention_kernel<T>, dim3(grid), dim3(fxr::attn2::kThreads),
-                       fxr::attn2::kSmemBytes, stream, maps, p);
+        const int grid = sk ? sm_count() : (int)std::max<int64_t>(1, std::min<int64_t>(units, sm_count()));
+        e = sk ? launch_pdl(fxr::attn2::attention_kernel<T, true>, dim3(grid), dim3(fxr::attn2::kThreads),
+                            fxr::attn2::kSmemBytes, stream, maps, p)
+               : launch_pdl(fxr::attn2::attention_kernel<T, false>, dim3(grid), dim3(fxr::attn2::kThreads),
+                            fxr::attn2::kSmemBytes, stream, maps, p);
     } else {
+        // few heads per launch (a GPU's share of a head-split frame, small models): the query tiles
+        // x heads may leave SMs idle, so launch the instantiation that can split key ranges
+        const bool split_ok = split.slots > 0 && d->n_heads <= kSplitMaxHeads;
         const int grid = split_ok ? sm_count()
                                   : (int)std::min<int64_t>(attention_ctas(N, d->n_heads) * n_streams, sm_count());
         e = split_ok ? launch_pdl(fxr::attn::attention_kernel<T, true>, dim3(grid), dim3(fxr::attn::kThreads),
@@ -386,6 +410,7 @@ int32_t launch_gather_streams(const fxr_frame_desc* d, int32_t n_streams, const 
                               cudaStream_t stream, const float* nq_txt = nullptr,
                               const float* nk_txt = nullptr, int32_t n_text_norm = 0,
                               const SplitArea* compact_split = nullptr) {
+    NvtxRange nvtx_("fxr:gather");
     if (n_streams < 1 || n_streams > fxr::kMaxBatch) return fail(FXR_ERR_INVALID, "1..%d streams per launch", fxr::kMaxBatch);
     fxr::GatherArgs a{};
     // compact_split != nullptr: the gather compacts the masks itself (gs[b].valid) and zeroes these
@@ -560,6 +585,7 @@ int32_t fxr_workspace_views(const fxr_frame_desc* desc, void* workspace, int32_t
 static int32_t launch_compact_streams(fxr::CompactArgs a, int32_t n_streams, int32_t n_tokens,
                                       const SplitArea& split, void* stream, void* zero2 = nullptr,
                                       size_t zero2_bytes = 0, int32_t n_force = 0) {
+    NvtxRange nvtx_("fxr:compact");
     a.n = n_tokens;
     a.zero2 = reinterpret_cast<uint4*>(zero2);
     a.zero2_vec = (int32_t)(zero2_bytes / 16);
@@ -665,6 +691,7 @@ static int32_t launch_restore_streams(const fxr_frame_desc* desc, fxr::RestoreAr
 int32_t fxr_restore_rows(const fxr_frame_desc* desc, const int32_t* mask, const int32_t* idx,
                          const int32_t* count, const void* save, void* cache_k, void* cache_v,
                          void* stream) {
+    NvtxRange nvtx_("fxr:restore");
     int32_t st = check_desc(desc, false);
     if (st != FXR_OK) return st;
     if (desc->n_tokens == 0) return FXR_OK;
@@ -953,6 +980,7 @@ static int32_t frame_forward_impl(const fxr_frame_desc* desc, const void* q, con
                                   const float* norm_q, const float* norm_k, void* cache_k, void* cache_v,
                                   void* out, void* workspace, size_t workspace_bytes, void* stream,
                                   const HostIo* host) {
+    NvtxRange nvtx_("fxr:frame");
     int32_t st = check_desc(desc, true);
     if (st != FXR_OK) return st;
     if (desc->n_tokens == 0) return FXR_OK;
@@ -1019,6 +1047,61 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc, const void* q, const void*
                               workspace, workspace_bytes, stream, nullptr);
 }
 
+// One step of fxr_frame_forward on its workspace layout (same index list, compact queries, save rows
+// and split scratch), so that a step run on its own launches what the frame launches.
+int32_t fxr_frame_step(int32_t step, const fxr_frame_desc* desc, const void* q, const void* k, const void* v,
+                       int32_t* mask, const uint8_t* valid, const int32_t* pos, const float* norm_q,
+                       const float* norm_k, void* cache_k, void* cache_v, void* out, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+    NvtxRange nvtx_("fxr:frame_step");
+    int32_t st = check_desc(desc, true);
+    if (st != FXR_OK) return st;
+    if (step < FXR_STEP_COMPACT || step > FXR_STEP_RESTORE) return fail(FXR_ERR_INVALID, "unknown frame step %d", step);
+    if (desc->n_tokens == 0) return FXR_OK;
+    if (!workspace) return fail(FXR_ERR_INVALID, "null workspace");
+    const Views w = carve(desc, workspace);
+    if (workspace_bytes < w.total)
+        return fail(FXR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, w.total);
+    if (!aligned16(workspace)) return fail(FXR_ERR_INVALID, "workspace must be 16-byte aligned");
+    const SplitArea split = split_area(w.total, workspace, workspace_bytes, desc->n_heads);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (step) {
+    case FXR_STEP_COMPACT:
+        return launch_compact(mask, valid, desc->n_tokens, w.idx, w.count, split, stream);
+    case FXR_STEP_GATHER:
+    case FXR_STEP_GATHER_COMPACT: {
+        if (!cache_k || !cache_v || !aligned16(cache_k) || !aligned16(cache_v))
+            return fail(FXR_ERR_INVALID, "cache must be non-null and 16-byte aligned");
+        if (step == FXR_STEP_GATHER)
+            return fxr_gather_norm_rope(desc, q, k, v, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc, w.ld_qc,
+                                        cache_k, cache_v, w.save, stream);
+        if (!gather_can_compact(1, desc->n_tokens))
+            return fail(FXR_ERR_UNSUPPORTED, "frame too large for the compacting gather");
+        if ((st = check_gather_args(desc, q, k, v, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc, w.ld_qc,
+                                    cache_k, cache_v, w.save)) != FXR_OK)
+            return st;
+        fxr::GatherStream gs{q, k, v, mask, w.idx, w.count, w.qc, cache_k, cache_v, w.save, valid};
+        return desc->dtype == FXR_BF16
+                   ? launch_gather_streams<__nv_bfloat16>(desc, 1, &gs, pos, norm_q, norm_k, w.ld_qc, s, nullptr,
+                                                          nullptr, 0, &split)
+                   : launch_gather_streams<__half>(desc, 1, &gs, pos, norm_q, norm_k, w.ld_qc, s, nullptr, nullptr, 0,
+                                                   &split);
+    }
+    case FXR_STEP_ATTENTION: {
+        if (!cache_k || !cache_v || !out || !aligned16(cache_k) || !aligned16(cache_v) || !aligned16(out))
+            return fail(FXR_ERR_INVALID, "cache/out must be non-null and 16-byte aligned");
+        OutSet os;
+        os.out = out;
+        os.split = split;
+        return desc->dtype == FXR_BF16
+                   ? launch_attention<__nv_bfloat16>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s)
+                   : launch_attention<__half>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s);
+    }
+    default:
+        return fxr_restore_rows(desc, mask, w.idx, w.count, w.save, cache_k, cache_v, stream);
+    }
+}
+
 // Staging rows of a host-buffer frame at the start of its workspace: the mask copy, then Q, K, V
 // (row stride ld_qkv) and the output (ld_out); the frame's own workspace follows.
 struct HostStage {
@@ -1076,6 +1159,7 @@ int32_t fxr_frame_forward_host(const fxr_frame_desc* desc, const void* host_q, c
                                const int32_t* pos, const float* norm_q, const float* norm_k, void* cache_k,
                                void* cache_v, void* host_out, void* workspace, size_t workspace_bytes,
                                void* stream) {
+    NvtxRange nvtx_("fxr:frame_host");
     int32_t st = check_desc(desc, true);
     if (st != FXR_OK) return st;
     if (desc->n_tokens == 0) return FXR_OK;
@@ -1145,6 +1229,7 @@ int32_t fxr_ln_modulate_rows(int32_t dtype, const void* x, int64_t ld_x, int32_t
 
 int32_t fxr_rows_gemm(const fxr_rows_gemm_desc* d, const int32_t* idx, const int32_t* count, void* scratch,
                       size_t scratch_bytes, void* stream) {
+    NvtxRange nvtx_("fxr:rows_gemm");
     namespace G = fxr::gemm;
     if (!d) return fail(FXR_ERR_INVALID, "null desc");
     if (d->dtype != FXR_BF16 && d->dtype != FXR_F16) return fail(FXR_ERR_UNSUPPORTED, "dtype must be bf16 or fp16");
@@ -1505,6 +1590,7 @@ int32_t fxr_double_block_forward(const fxr_frame_desc* desc, const fxr_double_bl
                                  void* x_out, int32_t* mask, uint8_t* valid, const int32_t* pos,
                                  void* cache_k, void* cache_v, void* workspace, size_t workspace_bytes,
                                  void* stream) {
+    NvtxRange nvtx_("fxr:double_block");
     return double_block_impl(desc, blk, x_in, x_out, mask, valid, pos, cache_k, cache_v, workspace,
                              workspace_bytes, stream, nullptr);
 }
@@ -1614,6 +1700,7 @@ int32_t fxr_single_block_forward(const fxr_frame_desc* desc, const fxr_single_bl
                                  void* x_out, int32_t* mask, uint8_t* valid, const int32_t* pos,
                                  void* cache_k, void* cache_v, void* workspace, size_t workspace_bytes,
                                  void* stream) {
+    NvtxRange nvtx_("fxr:single_block");
     return single_block_impl(desc, blk, x_in, x_out, mask, valid, pos, cache_k, cache_v, workspace,
                              workspace_bytes, stream, nullptr);
 }
@@ -1763,6 +1850,7 @@ extern "C" {
 int32_t fxr_frame_forward_batch(const fxr_frame_desc* desc, int32_t n_streams, const fxr_stream_frame* frames,
                                 const int32_t* pos, const float* norm_q, const float* norm_k, void* workspace,
                                 size_t workspace_bytes, void* stream) {
+    NvtxRange nvtx_("fxr:frame_batch");
     int32_t st = check_desc(desc, true);
     if (st != FXR_OK) return st;
     if (n_streams < 0) return fail(FXR_ERR_INVALID, "n_streams < 0");
@@ -1841,6 +1929,7 @@ int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g, c
                                 const int32_t* pos, const float* norm_q, const float* norm_k,
                                 void* cache_k, void* cache_v, void* workspace,
                                 size_t workspace_bytes, void* stream) {
+    NvtxRange nvtx_("fxr:frame_heads");
     int32_t st = check_desc(desc, true);
     if (st != FXR_OK) return st;
     if (!g || g->world < 1 || g->world > FXR_MAX_RANKS || g->rank < 0 || g->rank >= g->world)
@@ -1915,6 +2004,7 @@ int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g, c
         a.out[r] = reinterpret_cast<uint4*>(static_cast<char*>(g->out[r]) + col);
         a.arrive[r] = g->arrive[r];
     }
+    NvtxRange nvtx_push("fxr:exchange");
     cudaError_t e = launch_pdl(fxr::heads_push_kernel, dim3(push_ctas()), dim3(fxr::kPushThreads), 0, s, a);
     if (e != cudaSuccess) return cuda_status(e, "heads_push_kernel launch");
     g->epoch += 1;
@@ -1922,6 +2012,7 @@ int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g, c
 }
 
 int32_t fxr_head_group_wait(const fxr_head_group* g, void* stream) {
+    NvtxRange nvtx_("fxr:head_group_wait");
     if (!g || g->world < 1 || g->world > FXR_MAX_RANKS || g->rank < 0 || g->rank >= g->world)
         return fail(FXR_ERR_INVALID, "head group not initialised");
     if (g->world == 1) return FXR_OK;   // a single GPU stored its rows itself
@@ -1988,6 +2079,7 @@ size_t fxr_heads_nccl_workspace_size(const fxr_frame_desc* desc, const fxr_head_
 int32_t fxr_allgather_heads(const fxr_frame_desc* desc, const fxr_head_group* g, void* nccl_comm,
                             const void* o_local, int32_t m_cap, void* gathered, const int32_t* idx,
                             const int32_t* count, void* out, void* stream) {
+    NvtxRange nvtx_("fxr:allgather_heads");
     int32_t st = check_desc(desc, false);
     if (st != FXR_OK) return st;
     if (!group_ok(g)) return fail(FXR_ERR_INVALID, "head group not initialised");
@@ -2032,6 +2124,7 @@ int32_t fxr_frame_forward_heads_nccl(const fxr_frame_desc* desc, const fxr_head_
                                      const int32_t* pos, const float* norm_q, const float* norm_k,
                                      void* cache_k, void* cache_v, void* out, void* workspace,
                                      size_t workspace_bytes, void* stream) {
+    NvtxRange nvtx_("fxr:frame_heads_nccl");
     int32_t st = check_desc(desc, true);
     if (st != FXR_OK) return st;
     if (!group_ok(g)) return fail(FXR_ERR_INVALID, "head group not initialised");

@@ -31,7 +31,7 @@ EXPORTED = [
     "fxr_mark_updated", "fxr_gather_norm_rope", "fxr_attention_active", "fxr_restore_rows",
     "fxr_gather_rows", "fxr_scatter_rows", "fxr_kv_sync", "fxr_output_cache_sync",
     "fxr_rms_norm", "fxr_layer_norm_f32", "fxr_modulate_f32", "fxr_gelu_tanh_f32", "fxr_bias_add_f32",
-    "fxr_add_f32", "fxr_scale_add_f32", "fxr_attention_f32_bhsd", "fxr_frame_forward", "fxr_frame_forward_noalloc",
+    "fxr_add_f32", "fxr_scale_add_f32", "fxr_attention_f32_bhsd", "fxr_frame_forward", "fxr_frame_step", "fxr_frame_forward_noalloc",
     "fxr_frame_host_workspace_size", "fxr_frame_forward_host",
     "fxr_plugin_create", "fxr_plugin_clone", "fxr_plugin_destroy", "fxr_plugin_name",
     "fxr_plugin_version", "fxr_plugin_namespace", "fxr_plugin_fields", "fxr_plugin_output_desc",
@@ -194,6 +194,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
     L.fxr_rms_norm.argtypes = [_vp, _vp, _vp, ctypes.c_float, _i64, _i32, _i32, _vp]
     L.fxr_frame_forward.argtypes = [ctypes.POINTER(FrameDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]
+    L.fxr_frame_step.argtypes = [_i32, ctypes.POINTER(FrameDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                 _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]
     L.fxr_frame_forward_noalloc.argtypes = [ctypes.POINTER(FrameDesc)] + [_vp] * 12
     L.fxr_frame_host_workspace_size.argtypes = [ctypes.POINTER(FrameDesc)]
     L.fxr_frame_host_workspace_size.restype = ctypes.c_size_t
@@ -442,6 +444,20 @@ def frame_forward(cfg: FrameConfig, q, k, v, mask, valid, pos, norm_q, norm_k, c
                                     _ptr(valid), _ptr(pos), _ptr(norm_q), _ptr(norm_k),
                                     _ptr(cache_k), _ptr(cache_v), _ptr(out), _ptr(workspace),
                                     workspace.numel() * workspace.element_size(), _stream(stream)))
+
+
+# fxr_frame_step steps
+STEP_COMPACT, STEP_GATHER, STEP_GATHER_COMPACT, STEP_ATTENTION, STEP_RESTORE = 0, 1, 2, 3, 4
+
+
+def frame_step(step: int, cfg: FrameConfig, q, k, v, mask, valid, pos, norm_q, norm_k, cache_k, cache_v,
+               out, workspace, stream=None):
+    """One step of frame_forward on its workspace layout (fxr_frame_step)."""
+    d = cfg.desc()
+    _check(load().fxr_frame_step(step, ctypes.byref(d), _ptr(q), _ptr(k), _ptr(v), _ptr(mask),
+                                 _ptr(valid), _ptr(pos), _ptr(norm_q), _ptr(norm_k),
+                                 _ptr(cache_k), _ptr(cache_v), _ptr(out), _ptr(workspace),
+                                 workspace.numel() * workspace.element_size(), _stream(stream)))
 
 
 def frame_forward_noalloc(cfg: FrameConfig, q, k, v, mask, valid, pos, norm_q, norm_k, cache_k,

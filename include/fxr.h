@@ -97,9 +97,11 @@ int32_t fxr_check_device_error(void* stream, uint32_t* word_out);
 size_t fxr_workspace_size(const fxr_frame_desc* desc);
 
 /* The smallest workspace fxr_frame_forward accepts: idx, count, compact Q and saved rows, without
- * the optional area that lets the attention split each unit's key range across CTAs. A workspace
- * between this size and fxr_workspace_size gets as many split slots as fit in the rest; at this
- * size the attention never splits (the split only runs for calls of at most 8 heads). */
+ * the optional area of scratch slots that lets the attention cut work units between CTAs (the
+ * two-tile kernel's stream-K schedule, which needs 4 slots per SM; the one-tile kernel's key-range
+ * split, calls of at most 8 heads). A workspace between this size and fxr_workspace_size gets as
+ * many slots as fit in the rest; at this size the attention never cuts a unit. The outputs of a
+ * frame can differ in the last bits between workspaces that allow different schedules. */
 size_t fxr_workspace_min_size(const fxr_frame_desc* desc);
 
 /* ---- individual steps ----------------------------------------------------------------------- */
@@ -218,13 +220,39 @@ int32_t fxr_attention_f32_bhsd(const float* q, const float* k, const float* v, f
 /* ---- composite ------------------------------------------------------------------------------ */
 /* One frame: compact -> gather/norm/RoPE/cache write -> attention + scatter -> restore of
  * mask==1 rows. The body of the sparse attention plugin's enqueue. Workspace: see
- * fxr_workspace_size. Four kernel launches, no host synchronisation. */
+ * fxr_workspace_size. Three kernel launches (the gather compacts the mask itself), no host
+ * synchronisation. */
 int32_t fxr_frame_forward(const fxr_frame_desc* desc,
                           const void* q, const void* k, const void* v,
                           int32_t* mask, const uint8_t* valid, const int32_t* pos,
                           const float* norm_q, const float* norm_k,
                           void* cache_k, void* cache_v, void* out,
                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* One step of fxr_frame_forward, on the same arguments and workspace layout, for callers that run
+ * their own work between the steps or time them one by one:
+ *   FXR_STEP_COMPACT          mask preprocessing + index list of executed tokens (also zeroes the
+ *                             workspace's split counters)
+ *   FXR_STEP_GATHER           gather + QK-RMSNorm + RoPE + cache write of the listed rows
+ *   FXR_STEP_GATHER_COMPACT   the two above in one launch, as fxr_frame_forward runs them
+ *   FXR_STEP_ATTENTION        attention + scatter, with the workspace's split / stream-K scratch,
+ *                             so that its schedule is the frame's
+ *   FXR_STEP_RESTORE          restore of the cache rows of mask==1 tokens
+ * COMPACT, GATHER, ATTENTION, RESTORE in order (or GATHER_COMPACT, ATTENTION, RESTORE) give the
+ * result of fxr_frame_forward bit for bit. Unused pointer arguments of a step may be null. */
+enum {
+    FXR_STEP_COMPACT = 0,
+    FXR_STEP_GATHER = 1,
+    FXR_STEP_GATHER_COMPACT = 2,
+    FXR_STEP_ATTENTION = 3,
+    FXR_STEP_RESTORE = 4
+};
+int32_t fxr_frame_step(int32_t step, const fxr_frame_desc* desc,
+                       const void* q, const void* k, const void* v,
+                       int32_t* mask, const uint8_t* valid, const int32_t* pos,
+                       const float* norm_q, const float* norm_k,
+                       void* cache_k, void* cache_v, void* out,
+                       void* workspace, size_t workspace_bytes, void* stream);
 
 /* One frame whose per-frame tensors live in page-locked host memory, for a streaming host that
  * produces each frame's projections on the CPU side and wants the output back. The reference moves
@@ -261,11 +289,12 @@ int32_t fxr_frame_forward_host(const fxr_frame_desc* desc,
  * when they run a frame: for example a plugin enqueue inside an inference engine that owns every
  * device allocation, or a latency-critical loop that must not risk the device-wide
  * synchronisation an allocation can cause. This entry point has no counterpart in the reference.
- *   - Scratch: a fixed 96 MiB array inside this library (every GPU that loads the library holds it
- *     until the process exits). Frames whose fxr_workspace_min_size() exceeds 96 MiB are rejected
- *     with FXR_ERR_WORKSPACE; a 1024x1024 frame (4608 tokens, 24 heads, bf16/fp16) needs about
- *     85 MB. The rest of the 96 MiB serves as the attention's optional key-range split slots
- *     (calls of at most 8 heads), exactly as a 96 MiB workspace does for fxr_frame_forward.
+ *   - Scratch: a fixed 128 MiB array inside this library (every GPU that loads the library holds
+ *     it until the process exits). Frames whose fxr_workspace_min_size() exceeds 128 MiB are
+ *     rejected with FXR_ERR_WORKSPACE; a 1024x1024 frame (4608 tokens, 24 heads, bf16/fp16) needs
+ *     about 85 MB. The rest of the 128 MiB serves as the attention's optional split slots (its
+ *     stream-K schedule and key-range split), exactly as a 128 MiB workspace does for
+ *     fxr_frame_forward; for a 1024x1024 frame that is the full fxr_workspace_size().
  *   - No cudaMalloc, cudaFree or other allocating call is made. The first call on a device looks up
  *     the scratch address for that device (once, with that device current) and keeps it for the
  *     life of the process; make that first call before any stream capture, and do not call

@@ -60,7 +60,7 @@ def test_workspace_size_and_views(lib):
     C = 24 * 128
     assert n >= 4608 * 4 + 4608 * C * 2 * 3
     assert n % 256 == 0
-    # the minimum leaves out only the optional key-range split area
+    # the minimum leaves out only the optional split / stream-K slot area
     lo = fxr.workspace_min_size(cfg)
     assert 4608 * 4 + 4608 * C * 2 * 3 <= lo < n and lo % 256 == 0
     assert fxr.workspace_min_size(fxr.FrameConfig(n_tokens=16, n_text=4, dtype="f32", head_dim=0)) == 0
@@ -90,6 +90,19 @@ def test_invalid_arguments_rejected_without_gpu(lib):
     st = lib.fxr_frame_forward(ctypes.byref(d), *([None] * 11), None, 0, None)
     assert st == fxr.FXR_ERR_INVALID
     assert lib.fxr_kv_sync(None, None, None, None, None, 4, 4, 7, None) == fxr.FXR_ERR_INVALID
+    d = fxr.FrameConfig(n_tokens=16, n_text=4).desc()
+    assert lib.fxr_frame_step(9, ctypes.byref(d), *([None] * 11), None, 0, None) == fxr.FXR_ERR_INVALID
+    assert b"step" in lib.fxr_last_error_string()
+    assert lib.fxr_frame_step(fxr.STEP_ATTENTION, ctypes.byref(d), *([None] * 11), None, 0, None) == fxr.FXR_ERR_INVALID
+
+
+def test_frame_steps_match_the_header():
+    """The FXR_STEP_* values of include/fxr.h are the binding's STEP_* constants."""
+    text = open(HEADERS[0]).read()
+    steps = dict((k, int(v)) for k, v in re.findall(r"\bFXR_STEP_([A-Z_]+)\s*=\s*(\d+)", text))
+    assert steps == {"COMPACT": 0, "GATHER": 1, "GATHER_COMPACT": 2, "ATTENTION": 3, "RESTORE": 4}
+    for name, value in steps.items():
+        assert getattr(fxr, "STEP_" + name) == value, name
 
 
 def test_product_path_has_no_cpu_fallback():

@@ -10,6 +10,8 @@ significant bits, so storing a value of magnitude 2-4 alone moves it by up to 2^
 are held to at most 1 bf16 ulp from the oracle rounded to bf16, with mean-abs <= 2e-4. Every
 tolerance check records its measured max-abs / mean-abs (printed in pytest's summary).
 """
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -201,6 +203,29 @@ def _run_frame(w: W.Workload, fr: dict, valid=None, cfg=None):
     return {k: host(v) for k, v in t.items()}
 
 
+@pytest.mark.parametrize("split_gather", [False, True])
+@pytest.mark.parametrize("active", [0.25, 0.27])
+def test_frame_steps_equal_frame_forward(cuda, split_gather, active):
+    """fxr_frame_step run step by step (compacting gather, attention, restore; or compaction and
+    gather as two steps) on the frame's workspace gives fxr_frame_forward's outputs, cache rows and
+    mask bit for bit (at 27 % active the attention runs its stream-K schedule), with a frame of
+    execute-only rows so that the restore has work."""
+    w = W.with_active(W.C2, active)
+    fr = _with_exec_only(W.make_frame(w, seed=61), seed=62)
+    cfg = cfg_of(w)
+    a = _run_frame(w, fr)
+    t = _frame_tensors(w, fr)
+    ws = torch.empty(fxr.workspace_size(cfg), dtype=torch.uint8, device="cuda")
+    steps = ([fxr.STEP_COMPACT, fxr.STEP_GATHER] if split_gather else [fxr.STEP_GATHER_COMPACT]) + \
+        [fxr.STEP_ATTENTION, fxr.STEP_RESTORE]
+    for st in steps:
+        fxr.frame_step(st, cfg, t["q"], t["k"], t["v"], t["mask"], None, t["pos"], t["norm_q"], t["norm_k"],
+                       t["cache_k"], t["cache_v"], t["out"], ws)
+    sync_ok()
+    for k in ("out", "cache_k", "cache_v", "mask"):
+        assert np.array_equal(host(t[k]), a[k]), k
+
+
 @pytest.mark.parametrize("wl,heads", [(W.C1, 24), (W.KLEIN, 24), (W.C3, 4), (W.C2, 6)])
 def test_frame_forward_parity(cuda, wl, heads):
     w = small(wl, heads)
@@ -244,20 +269,31 @@ def _oracle_rows(w: W.Workload, fr: dict, valid, operand_dtype: str, n_sample=No
     return op["idx"][sel], ref
 
 
-def _split_parts(M: int, n_heads: int, n_tokens: int, grid: int = 148, slots: int = 4 * 148) -> int:
-    """Parts per (query tile, head) unit that the split-capable attention chooses: the kernel's
-    cost model (choose_splits in fxr_attention.cuh: CTA rounds x (steps per item + 2), + 4 steps per
-    split item, at most 4 parts) restated on the host, with the persistent grid of one CTA per SM
-    and the split slots that fxr_workspace_size provides."""
-    units, steps = -(-M // 128) * n_heads, -(-n_tokens // 256)
-    best, best_cost = 1, -(-units // grid) * (steps + 2.0)
-    for sp in range(2, 5):
-        if sp > steps or units * sp > slots:
-            break
-        cost = -(-(units * sp) // grid) * (steps / sp + 2.0 + 4.0)
-        if cost < best_cost:
-            best, best_cost = sp, cost
-    return best
+def _cuts_units(M: int, n_heads: int, n_tokens: int, grid: int = 148, slots: int = 4 * 148) -> bool:
+    """Whether the attention of a frame cuts work units between CTAs, from the kernels' own cost
+    models restated on the host (persistent grid of one CTA per SM, the split slots that
+    fxr_workspace_size provides):
+      two-tile kernel (fxr_attention2.cuh, choose_schedule): units of 256 query rows x all keys in
+        128-key steps; stream-K (per = ceil(units x steps / grid) iterations per CTA) when
+        per + 2 x items + 2 x 4.5 < ceil(units / grid) x (steps + 2), items = ceil(per / steps) + 1,
+        and the workspace holds 4 slots per CTA;
+      one-tile kernel (fxr_attention.cuh, choose_splits; FXR_ATTENTION_TILES=1, at most 8 heads):
+        units of 128 rows, 256-key steps, 2 to 4 equal parts when
+        ceil(units x parts / grid) x (steps / parts + 6) < ceil(units / grid) x (steps + 2)."""
+    if os.environ.get("FXR_ATTENTION_TILES", "") == "1":
+        if n_heads > 8:
+            return False
+        units, steps = -(-M // 128) * n_heads, -(-n_tokens // 256)
+        whole = -(-units // grid) * (steps + 2.0)
+        return any(sp <= steps and units * sp <= slots and -(-(units * sp) // grid) * (steps / sp + 6.0) < whole
+                   for sp in range(2, 5))
+    if slots < 4 * grid:
+        return False
+    units, steps = -(-M // 256) * n_heads, -(-n_tokens // 128)
+    whole = -(-units // grid) * (steps + 2.0)
+    per = -(-(units * steps) // grid)
+    items = -(-per // steps) + 1
+    return per + 2.0 * items + 9.0 < whole
 
 
 def test_frame_forward_deterministic_and_noop(cuda):
@@ -294,28 +330,33 @@ def test_full_size_c2_properties(cuda):
     assert_close(g["out"][rows], ref32, what="O (256 rows) vs fp32 oracle", **TOL_O)
 
 
-@pytest.mark.parametrize("wl,heads,active,n_sample", [(W.C5, 3, None, 128), (W.C2, 2, 1.0, 256),
-                                                      (W.C5, 24, None, 96)])
-def test_high_resolution_and_split_attention_vs_oracle(cuda, wl, heads, active, n_sample):
-    """Frames whose attention splits each unit's key range across CTAs (a GPU's 3 heads of an 8-way
-    split 2048^2 frame; 2 heads of a fully active 1024^2 frame) and the full 2048^2 frame (24
-    heads, N = 16896, no split), sampled executed rows against the oracle on the stored operands
-    and against the fp32 oracle. The split frames also equal, within the bar, the same frame run
-    with a workspace that leaves no split slots (the unsplit schedule)."""
+@pytest.mark.parametrize("wl,heads,active,n_sample,cut", [(W.C5, 3, None, 128, True), (W.C2, 2, 1.0, 256, True),
+                                                          (W.C5, 24, None, 96, False), (W.C2, 24, 0.27, 128, True),
+                                                          (W.C2, 24, 0.10, 128, True), (W.C2, 24, 1.0, 64, False)])
+def test_high_resolution_and_split_attention_vs_oracle(cuda, wl, heads, active, n_sample, cut):
+    """Frames whose attention cuts work units between CTAs (a GPU's 3 heads of an 8-way split
+    2048^2 frame; 2 heads of a fully active 1024^2 frame; 1024^2 frames with 24 heads whose units
+    fill one wave and a few SMs of a second, or fewer than the SMs) and frames that run whole units
+    (the full 2048^2 frame, N = 16896, in two rounds; a fully active 1024^2 frame), sampled executed
+    rows against the oracle on the stored operands and against the fp32 oracle.
+    The cut frames also equal, within the bar, the same frame run with a workspace that leaves no
+    split slots (whole units)."""
     w = small(wl if active is None else W.with_active(wl, active), heads)
     fr = W.make_frame(w, seed=57)
     M = int((fr["mask"] != 0).sum())
-    split = _split_parts(M, heads, w.n_tokens)
-    assert (split > 1) == (heads <= 8), (M, split)
+    split = _cuts_units(M, heads, w.n_tokens)
+    if os.environ.get("FXR_ATTENTION_TILES", "") == "1":
+        cut = cut and heads <= 8          # the one-tile kernel splits only launches of few heads
+    assert split == cut, (M, split)
     g = _run_frame(w, fr)
     mask = fr["mask"]
     assert np.array_equal(g["out"][mask == 0], fr["out"][mask == 0])
     assert np.array_equal(g["cache_v"][mask == 2], fr["v"][mask == 2])
     rows, ref = _oracle_rows(w, fr, None, w.dtype, n_sample=n_sample, seed=58)
-    assert_close(g["out"][rows], ref, what=f"O split={split} vs oracle on stored operands", **TOL_O)
+    assert_close(g["out"][rows], ref, what=f"O cut={split} vs oracle on stored operands", **TOL_O)
     _, ref32 = _oracle_rows(w, fr, None, "f32", n_sample=n_sample, seed=58)
-    assert_close(g["out"][rows], ref32, what=f"O split={split} vs fp32 oracle", **TOL_O)
-    if split > 1:
+    assert_close(g["out"][rows], ref32, what=f"O cut={split} vs fp32 oracle", **TOL_O)
+    if split:
         cfg = cfg_of(w)
         t = _frame_tensors(w, fr)
         ws = torch.empty(fxr.workspace_min_size(cfg), dtype=torch.uint8, device="cuda")
@@ -323,8 +364,8 @@ def test_high_resolution_and_split_attention_vs_oracle(cuda, wl, heads, active, 
                           t["norm_k"], t["cache_k"], t["cache_v"], t["out"], ws)
         sync_ok()
         u = host(t["out"])
-        assert not np.array_equal(u[rows], g["out"][rows])        # the split schedule did run
-        assert_close(g["out"][rows], u[rows], what="O split vs unsplit", **TOL_O)
+        assert not np.array_equal(u[rows], g["out"][rows])        # the cut schedule did run
+        assert_close(g["out"][rows], u[rows], what="O cut vs whole units", **TOL_O)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -484,7 +525,8 @@ def test_frame_output_independent_of_stale_workspace(cuda, fill):
 def test_frame_forward_batch_matches_per_stream_frames(cuda, n_streams, wl, heads):
     """Streams in one set of launches equal per-stream frames bit for bit (each (query tile, head)
     unit is computed the same way whichever launch holds it); 9 streams run as groups of 8 + 1.
-    More than 8 heads per launch, so that neither path splits key ranges."""
+    The per-stream frames get a workspace without split slots, so that both paths run whole units
+    (a lone small frame would otherwise take the stream-K schedule)."""
     w = small(wl, heads)
     cfg = cfg_of(w)
     pos = dev(W.positions(w), "i32")
@@ -497,7 +539,7 @@ def test_frame_forward_batch_matches_per_stream_frames(cuda, n_streams, wl, head
     b = [_frame_tensors(w, fr) for fr in frs]
     ws = torch.empty(fxr.batch_workspace_size(cfg, n_streams), dtype=torch.uint8, device="cuda")
     fxr.frame_forward_batch(cfg, [dict(t, valid=valids[i]) for i, t in enumerate(a)], pos, nq, nk, ws)
-    wsf = torch.empty(fxr.workspace_size(cfg), dtype=torch.uint8, device="cuda")
+    wsf = torch.empty(fxr.workspace_min_size(cfg), dtype=torch.uint8, device="cuda")
     for i, t in enumerate(b):
         fxr.frame_forward(cfg, t["q"], t["k"], t["v"], t["mask"], valids[i], pos, nq, nk,
                           t["cache_k"], t["cache_v"], t["out"], wsf)
