@@ -192,6 +192,38 @@ def test_attention_parity(cuda, M, N, H, dtype):
     assert np.array_equal(got[untouched], out0[untouched])
 
 
+@pytest.mark.parametrize("jump,dtype", [(10.0, "bf16"), (10.0, "f16"), (40.0, "bf16"), (150.0, "bf16")])
+def test_attention_row_maximum_jumps(cuda, jump, dtype):
+    """Rows whose score maximum jumps by `jump` (log2 units) at a key of the third 128-key step, so
+    that the lazy rescale of the softmax (only when a row maximum grows by more than 2^8) runs, from
+    a small jump up to one that would overflow fp32 without it, against the oracle. One key then
+    carries most of each row's weight, and the rounding of its probability to the 16-bit PV operand
+    (up to 2^-9 relative in bf16) goes straight into the output, so V is scaled to keep that inside
+    the bar."""
+    rng = np.random.default_rng(int(jump) + (1 if dtype == "f16" else 0))
+    H, N, M = 1, 640, 96
+    C = 128 * H
+    scale_log2 = 1.4426950408889634 / np.sqrt(128.0)
+    qdir = rng.normal(size=C).astype(np.float32)
+    qdir /= np.linalg.norm(qdir)
+    a = np.sqrt(jump / scale_log2)
+    qc = (qdir[None, :] * a + rng.normal(scale=0.05, size=(N, C))).astype(np.float32)
+    k = rng.normal(scale=0.3, size=(N, C)).astype(np.float32)
+    k[300] = qdir * a                                   # the key that every row's maximum jumps to
+    k[:128] -= (qc[:1] * 0.5 / a)                       # the first step's scores a little lower still
+    v = rng.normal(scale=0.25, size=(N, C)).astype(np.float32)
+    qc, k, v = (W.round_storage(x, dtype) for x in (qc, k, v))
+    idx = np.sort(rng.choice(N, size=M, replace=False)).astype(np.int32)
+    cfg = fxr.FrameConfig(n_tokens=N, n_text=0, n_heads=H, dtype=dtype)
+    d_out = dev(np.zeros((N, C), np.float32), dtype)
+    cnt = torch.tensor([M], dtype=torch.int32, device="cuda")
+    fxr.attention_active(cfg, dev(qc, dtype), cnt, dev(k, dtype), dev(v, dtype), dev(idx, "i32"), d_out)
+    sync_ok()
+    ref = O.attention(qc[:M], k, v, H, 128)
+    got = host(d_out)[idx]
+    assert_close(got, ref, what=f"O jump 2^{jump:g}", **TOL_O)
+
+
 def _run_frame(w: W.Workload, fr: dict, valid=None, cfg=None):
     cfg = cfg or cfg_of(w)
     t = _frame_tensors(w, fr)
