@@ -393,13 +393,14 @@ def run_ours(args):
         "kernels": {"gather": mem,
                     "in_frame_us": {k[:-3]: round(v, 2) for k, v in kern.items()},
                     "isolated_us": {k[:-3]: round(v, 2) for k, v in iso.items()},
-                    "timing": "the frame's 3 launches (compacting gather, attention, restore) through "
+                    "timing": "the frame's launches (compacting gather, attention; the restore step "
+                              "launches nothing when the attention restores mask==1 rows itself) through "
                               "fxr_frame_step on the frame's workspace; in_frame: event records between "
                               "them in a CUDA graph, mean over frames (each interval also holds one "
                               "launch gap); isolated: 40 back-to-back launches of one step per graph; the "
                               "attention roofline uses in_frame, the gather roofline isolated"},
         "e2e": e2e,
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": 2 * args.steps,   # compacting gather + attention (which restores mask==1 rows)
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -455,7 +456,8 @@ def run_step(cfg, fr, ws, step):
                    fr["norm_k"], fr["cache_k"], fr["cache_v"], fr["out"], ws)
 
 
-# The frame's three launches as fxr_frame_step runs them (same workspace, same schedule).
+# The frame's steps as fxr_frame_step runs them (same workspace, same schedule; the restore step
+# launches nothing when the two-tile attention restored the mask==1 rows itself).
 FRAME_STEPS = (("gather_us", 2), ("attention_us", 3), ("restore_us", 4))
 
 
@@ -993,9 +995,10 @@ def run_heads(args, embedded: bool = False):
                      "nvlink_bytes_per_rank": nvlink_bytes,
                      "note": "frac = roofline time of one frame / measured frame time (whole frame, 5 kernels)"},
         "e2e": None,
-        # compaction, gather, attention, restore; with peers also the row numbering and the exchange
-        # (heads_push_kernel, or heads_scatter_kernel after NCCL's own all-gather kernel)
-        "gpu_launches": (4 if world == 1 else 6) * args.steps,
+        # compaction, gather, attention (which restores mask==1 rows); with peers also the row
+        # numbering and the exchange (heads_push_kernel, or heads_scatter_kernel after NCCL's own
+        # all-gather kernel)
+        "gpu_launches": (3 if world == 1 else 5) * args.steps,
         "clocks": clk,
     }
     if rank == 0 and not embedded:
@@ -1115,7 +1118,7 @@ def run_streams(args, embedded: bool = False):
                    "n_tokens": w.n_tokens, "active": w.active, "heads": w.n_heads,
                    "parallelism": f"streams{total}-over-{world}",
                    "l2": f"{n_sets} rotating sets of every stream's inputs", "graph": bool(graphs)},
-        "e2e": None, "gpu_launches": 3 * args.steps, "clocks": clk,
+        "e2e": None, "gpu_launches": 2 * args.steps, "clocks": clk,
     }
     if rank == 0 and not embedded:
         print(json.dumps(out_line), flush=True)
@@ -1457,7 +1460,7 @@ def run_block(args):
         "kernels_isolated_us": {k: round(v, 2) for k, v in kern.items()},
         "dense_torch_same_gpu_us": round(dense_us, 1),
         "e2e": e2e,
-        "gpu_launches": 13 * args.steps,
+        "gpu_launches": 12 * args.steps,
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -1515,7 +1518,7 @@ def single_block_report(args, w, cfg, wts, sets, run, H, ms, fl, M_avg, clk, pk,
         "config": {"workload": w.name + "_single_block", "n_tokens": N, "active": w.active, "M_avg": M_avg,
                    "heads": w.n_heads, "hidden": C, "mlp_hidden": H, "graph": True},
         "roofline": roof, "kernels_isolated_us": {k: round(v, 2) for k, v in kern.items()},
-        "gpu_launches": 8 * args.steps, "clocks": clk,
+        "gpu_launches": 7 * args.steps, "clocks": clk,
         "e2e": None, "note": "e2e and the CPU arm are reported by --path block",
     }
 

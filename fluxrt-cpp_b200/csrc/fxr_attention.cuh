@@ -103,6 +103,17 @@ struct Stream {                  // one edit stream of the launch
     const int32_t* count;        // executed rows (compaction output, device)
     const int32_t* idx;          // their token indices
     void* out;                   // O row base
+    // Restore of the cache rows of mask==1 tokens at the end of the attention (two-tile kernel;
+    // restore_rows == nullptr: the caller restores them with a separate launch). Lists written by
+    // the compaction: compact rows, their number, and per head kRestoreSlots arrival counters that
+    // start at zero.
+    const int32_t* restore_rows;
+    const int32_t* restore_count;
+    const int32_t* restore_idx;  // compact row -> token (the attention's own idx may be a row numbering)
+    int32_t* head_done;
+    const uint4* save;           // [M][2 * row_vec] the saved K and V rows of each compact row
+    char* cache_k;
+    char* cache_v;
 };
 
 // Tensor maps of every stream: compact Q' and the K / V caches.
@@ -122,6 +133,8 @@ struct Params {
     float* split_scratch;        // [split_slots][kSplitSlotFloats]
     int32_t* split_cnt;          // [split_slots][kSplitPortions], zero at launch
     int32_t split_slots;         // 0: never split
+    int64_t ld_cache_bytes;      // fused restore: cache row pitch
+    int32_t row_vec;             // fused restore: 16-byte vectors per K (or V) row of the launch's heads
 };
 
 // Parts per unit: the shortest estimated kernel time (CTA rounds x steps per item + overheads);
@@ -225,6 +238,28 @@ __device__ __forceinline__ void* stream_out(const Params& p, int32_t b) {
     for (int k = 1; k < kMaxBatch; ++k)
         if (k == b) o = p.s[k].out;
     return o;
+}
+
+// The fused-restore fields of stream b (static-index selection, see above).
+struct RestoreRef {
+    const int32_t* rows;
+    const int32_t* count;
+    int32_t* head_done;
+    const uint4* save;
+    char* cache_k;
+    char* cache_v;
+    const int32_t* idx;
+    const int32_t* m;
+};
+__device__ __forceinline__ RestoreRef stream_restore(const Params& p, int32_t b) {
+    RestoreRef r{p.s[0].restore_rows, p.s[0].restore_count, p.s[0].head_done, p.s[0].save,
+                 p.s[0].cache_k, p.s[0].cache_v, p.s[0].restore_idx, p.s[0].count};
+#pragma unroll
+    for (int k = 1; k < kMaxBatch; ++k)
+        if (k == b)
+            r = RestoreRef{p.s[k].restore_rows, p.s[k].restore_count, p.s[k].head_done, p.s[k].save,
+                           p.s[k].cache_k, p.s[k].cache_v, p.s[k].restore_idx, p.s[k].count};
+    return r;
 }
 
 template <typename T>

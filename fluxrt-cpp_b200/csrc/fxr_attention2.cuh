@@ -14,7 +14,9 @@
 //   warp 8      TMA producer: Q_0, Q_1 and a 5-slot ring of 128-key K and V tiles in the tensor
 //               core's consumption order K_0 V_0 K_1 V_1 ... (128-byte swizzle)
 //   warp 9      TMEM allocator and the single MMA-issuing thread
-//   warps 10-11 idle (they complete the third warpgroup)
+//   warp 10     after the CTA's last item: restore of the cache rows of mask==1 tokens, head by
+//               head, once no CTA reads that head any more
+//   warp 11     idle (it completes the third warpgroup)
 // Tensor memory (512 columns): S_0 [0,128), S_1 [128,256) fp32 scores; O_0 [256,384), O_1 [384,512)
 // fp32 outputs. The 16-bit probabilities P_i of a step are written over the first 64 columns of
 // S_i (key pairs packed per column) and read from there by the PV product (A operand in tensor
@@ -50,6 +52,7 @@ constexpr int kSlots = 5;                       // K/V tile ring
 constexpr int kSoftmaxWarps = 8;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
+constexpr int kRestoreWarp = 10;
 constexpr int kThreads = 32 * 12;
 constexpr uint32_t kSoftmaxThreads = 32 * kSoftmaxWarps;
 constexpr uint32_t kHalfBytes = 128 * 128;      // 128 rows x 64 16-bit values (one swizzle span)
@@ -276,6 +279,63 @@ __device__ __forceinline__ void decode_pair_unit(const Params& p, int32_t u, int
     row0 = (u - head * pairs) * kRows;
 }
 
+// Fused restore of the cache rows of mask==1 tokens, head by head: the saved K and V slices of head
+// `head` of every listed row are copied back into the cache by one warp (lanes 0-15 the K slice,
+// 16-31 the V slice of a row), 32 rows' indices fetched at a time.
+__device__ __forceinline__ void restore_head_rows(const attn::RestoreRef rr, int64_t ld_cache_bytes, int32_t row_vec,
+                                                  int32_t n_tokens, int32_t head) {
+    const uint32_t lane = lane_id();
+    const int32_t n1 = __ldcg(rr.count);
+    const int32_t half = (int32_t)(lane >> 4), l = (int32_t)(lane & 15);
+    for (int32_t e0 = 0; e0 < n1; e0 += 32) {
+        const int32_t e = e0 + (int32_t)lane;
+        int32_t m = -1, i = -1;
+        if (e < n1) {
+            m = __ldcg(rr.rows + e);
+            i = __ldcg(rr.idx + m);
+        }
+        for (int q = 0; q < 32; ++q) {
+            const int32_t mq = __shfl_sync(0xffffffffu, m, q), iq = __shfl_sync(0xffffffffu, i, q);
+            if (mq < 0) break;
+            if (iq < 0 || iq >= n_tokens) continue;   // flagged by the gather, which skipped the row
+            const uint4 v = rr.save[(int64_t)mq * 2 * row_vec + half * row_vec + head * (kD / 8) + l];
+            char* dst = (half ? rr.cache_v : rr.cache_k) + (int64_t)iq * ld_cache_bytes + (int64_t)head * kD * 2 + l * 16;
+            *reinterpret_cast<uint4*>(dst) = v;
+        }
+    }
+}
+
+// Whether any stream of the launch lists mask==1 rows to restore (read once the compaction is over).
+__device__ __forceinline__ bool restore_pending(const attn::Params& p) {
+    if (p.s[0].restore_rows == nullptr) return false;
+    bool any = false;
+#pragma unroll
+    for (int k = 0; k < kMaxBatch; ++k)
+        if (k < p.n_streams) any = any || __ldcg(attn::stream_restore(p, k).count) > 0;
+    return any;
+}
+
+// Restore of mask==1 cache rows by warp 10 after its CTA has finished all its items: it adds the key
+// steps of each of the CTA's items to that head's counter; the arrival that completes a head (every
+// item of the head done in every CTA, so no CTA reads its K / V any more) restores that head's rows.
+// Runs only for launches that list such rows. Out of line: the other roles' code is the same with
+// and without it.
+__device__ __noinline__ void restore_tail(const attn::Params& p, const Sched sc, int32_t n_steps) {
+    const uint32_t lane = lane_id();
+    Cursor cur = first_cursor(sc);
+    int32_t u, s0, s1;
+    while (next_item(sc, cur, u, s0, s1)) {
+        int32_t b, head, row0, m_b;
+        decode_pair_unit(p, u, b, head, row0, m_b);
+        const attn::RestoreRef rr = attn::stream_restore(p, b);
+        int32_t prev = 0;
+        if (lane == 0) prev = atom_add_acq_rel_gpu(rr.head_done + head, s1 - s0);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev + (s1 - s0) == (m_b + kRows - 1) / kRows * n_steps)
+            restore_head_rows(rr, p.ld_cache_bytes, p.row_vec, p.n_tokens, head);
+    }
+}
+
 template <typename T, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
 attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Params p) {
@@ -334,6 +394,7 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
         if (b < p.n_streams) n_units += (*p.s[b].count + kRows - 1) / kRows * p.n_heads;
     const int32_t n_steps = (p.n_tokens + kBN - 1) / kBN;
     const Sched sc = choose_schedule(n_units, n_steps, (int32_t)gridDim.x, p.split_slots, kSplit);
+    bool restore = false;   // warp 10: this launch restores mask==1 rows at the end
 
     if (warp >= kSoftmaxWarps) {
       // warpgroup 2: producer, MMA issuer and two idle warps
@@ -500,6 +561,8 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
                 attn::mbar_wait_drain(bar(kDrain), 0);
             }
         }
+      } else if (warp == kRestoreWarp) {
+        restore = restore_pending(p);   // after the compaction (pdl_wait above); used at the end
       }
     } else {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
@@ -618,18 +681,21 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
             // epilogue: O is final once the last product of the tile has completed
             if (!wwait(bar(kPVDone + t), (s_it - 1) & 1)) { ok = false; break; }
             tc_fence_after();
+            int32_t steps_done = n_steps;
             if (kSplit && sc.per > 0) {
                 // the item again, from the cursor (its end iteration), not kept across the loop
                 const int32_t it_end = wcur[0];
                 u = (it_end - 1) / n_steps;
                 s1 = it_end - u * n_steps;
                 s0 = max(0, (int32_t)blockIdx.x * sc.per - u * n_steps);
+                steps_done = s1 - s0;
             }
             if (kSplit && sc.per > 0 && (s0 > 0 || s1 < n_steps)) {
                 cut_unit_epilogue<T>(p.split_scratch, p.split_cnt, p.n_tokens, p.ld_out,
                                      static_cast<T*>(attn::stream_out(p, b)), sc, u, head, t, r, warp, tO,
                                      m_run, l_run, bar(kOFree + t), live, *orow_slot);
                 ++units_done;
+                (void)steps_done;
                 continue;
             }
             const int32_t i = *orow_slot;
@@ -659,6 +725,7 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
             tc_fence_before();
             mbar_arrive(bar(kOFree + t));
             ++units_done;
+            (void)steps_done;
         }
     }
 
@@ -669,6 +736,8 @@ attention_kernel(const __grid_constant__ Maps maps, const __grid_constant__ Para
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+    // ---------------- restore of mask==1 cache rows (whole warp, after every item of the CTA) ----
+    if (warp == kRestoreWarp && restore && !*abort) restore_tail(p, sc, n_steps);
 }
 
 }  // namespace attn2

@@ -12,6 +12,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 #include <string>
 
 #include "fxr.h"
@@ -207,6 +208,7 @@ struct Views {
     void* qc;
     int64_t ld_qc;
     void* save;
+    fxr::RestoreList restore;   // mask==1 rows for the restore (written by the compaction)
     size_t total;
 };
 
@@ -226,6 +228,11 @@ Views carve(const fxr_frame_desc* d, void* ws) {
     off = align_up(off + N * C * eb, 256);
     v.save = b ? b + off : nullptr;
     off = align_up(off + N * 2 * C * eb, 256);
+    v.restore.count = reinterpret_cast<int32_t*>(b ? b + off : nullptr);
+    v.restore.head_done = reinterpret_cast<int32_t*>(b ? b + off + 16 : nullptr);
+    off = align_up(off + 16 + (size_t)d->n_heads * fxr::kRestoreSlots * sizeof(int32_t), 256);
+    v.restore.rows = reinterpret_cast<int32_t*>(b ? b + off : nullptr);
+    off = align_up(off + N * sizeof(int32_t), 256);
     v.total = off;
     return v;
 }
@@ -303,11 +310,23 @@ struct AttnStreamArgs {
     const void* cv;
     const int32_t* idx;
     void* out;
+    // the frame whose mask==1 cache rows the attention may restore itself (nullptr: it does not)
+    const Views* frame = nullptr;
 };
+
+// Whether the two-tile kernel serves attention launches of this dtype on the current device (it
+// then also restores the frame's mask==1 cache rows, so the frame needs no restore launch).
+static bool g_pairs_ready[2][kMaxDevices] = {{false}};
+static bool attention_restores(int32_t dtype) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
+    return attention_pairs() && g_pairs_ready[dtype == FXR_BF16 ? 1 : 0][dev];
+}
 
 template <typename T>
 int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, const AttnStreamArgs* st,
-                                 const SplitArea& split, cudaStream_t stream) {
+                                 const SplitArea& split, cudaStream_t stream, bool* restored = nullptr) {
+    if (restored) *restored = false;
     NvtxRange nvtx_("fxr:attention");
     if (n_streams < 1 || n_streams > fxr::kMaxBatch) return fail(FXR_ERR_INVALID, "1..%d streams per launch", fxr::kMaxBatch);
     static bool configured[kMaxDevices] = {false};
@@ -335,6 +354,7 @@ int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, con
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
         pairs_ok[dev] = (uint32_t)fa.numRegs * (uint32_t)fxr::attn2::kThreads >= fxr::attn2::kRegPool &&
                         (uint32_t)fs.numRegs * (uint32_t)fxr::attn2::kThreads >= fxr::attn2::kRegPool;
+        g_pairs_ready[std::is_same<T, __nv_bfloat16>::value ? 1 : 0][dev] = pairs_ok[dev];
         configured[dev] = true;
     }
     const int64_t C = (int64_t)d->n_heads * d->head_dim;
@@ -366,6 +386,25 @@ int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, con
         // the instantiation that can run it, on every SM (the kernel chooses on the device, from M;
         // CTAs without an item exit)
         const bool sk = split.slots >= fxr::attn2::kSlotsPerCta * sm_count();
+        // the mask==1 rows of every stream's frame are restored by the kernel's tail
+        bool fuse = restored != nullptr;
+        for (int32_t b = 0; b < n_streams; ++b) fuse = fuse && st[b].frame != nullptr;
+        if (fuse) {
+            const size_t eb = dtype_bytes(d->dtype);
+            for (int32_t b = 0; b < n_streams; ++b) {
+                const Views& w = *st[b].frame;
+                p.s[b].restore_rows = w.restore.rows;
+                p.s[b].restore_count = w.restore.count;
+                p.s[b].head_done = w.restore.head_done;
+                p.s[b].restore_idx = w.idx;
+                p.s[b].save = static_cast<const uint4*>(w.save);
+                p.s[b].cache_k = static_cast<char*>(const_cast<void*>(st[b].ck));
+                p.s[b].cache_v = static_cast<char*>(const_cast<void*>(st[b].cv));
+            }
+            p.ld_cache_bytes = d->ld_cache * (int64_t)eb;
+            p.row_vec = (int32_t)((int64_t)d->n_heads * d->head_dim * (int64_t)eb / 16);
+            *restored = true;
+        }
         const int64_t units = (N + fxr::attn2::kRows - 1) / fxr::attn2::kRows * d->n_heads * n_streams;
         const int grid = sk ? sm_count() : (int)std::max<int64_t>(1, std::min<int64_t>(units, sm_count()));
         e = sk ? launch_pdl(fxr::attn2::attention_kernel<T, true>, dim3(grid), dim3(fxr::attn2::kThreads),
@@ -387,12 +426,14 @@ int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, con
     return FXR_OK;
 }
 
+// frame / restored: as for launch_attention_streams (the frame's views, whose mask==1 rows the
+// kernel restores when it can; *restored tells whether it will)
 template <typename T>
 int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc, const int32_t* count,
                          const void* ck, const void* cv, const int32_t* idx, const OutSet& os,
-                         cudaStream_t stream) {
-    const AttnStreamArgs st{qc, ld_qc, count, ck, cv, idx, os.out};
-    return launch_attention_streams<T>(d, 1, &st, os.split, stream);
+                         cudaStream_t stream, const Views* frame = nullptr, bool* restored = nullptr) {
+    const AttnStreamArgs st{qc, ld_qc, count, ck, cv, idx, os.out, frame};
+    return launch_attention_streams<T>(d, 1, &st, os.split, stream, restored);
 }
 
 // Gather of n_streams frames of the same geometry (one launch; rows stream after stream).
@@ -584,9 +625,10 @@ int32_t fxr_workspace_views(const fxr_frame_desc* desc, void* workspace, int32_t
 // start at zero.
 static int32_t launch_compact_streams(fxr::CompactArgs a, int32_t n_streams, int32_t n_tokens,
                                       const SplitArea& split, void* stream, void* zero2 = nullptr,
-                                      size_t zero2_bytes = 0, int32_t n_force = 0) {
+                                      size_t zero2_bytes = 0, int32_t n_force = 0, int32_t n_heads = 0) {
     NvtxRange nvtx_("fxr:compact");
     a.n = n_tokens;
+    a.n_heads = n_heads;
     a.zero2 = reinterpret_cast<uint4*>(zero2);
     a.zero2_vec = (int32_t)(zero2_bytes / 16);
     a.n_force = n_force;
@@ -598,13 +640,15 @@ static int32_t launch_compact_streams(fxr::CompactArgs a, int32_t n_streams, int
     return FXR_OK;
 }
 
+// restore: the mask==1 list of a frame's workspace (and its heads' counters), or nullptr
 static int32_t launch_compact(int32_t* mask, const uint8_t* valid, int32_t n_tokens, int32_t* idx,
-                              int32_t* count, const SplitArea& split, void* stream) {
+                              int32_t* count, const SplitArea& split, void* stream,
+                              const fxr::RestoreList* restore = nullptr, int32_t n_heads = 0) {
     if (n_tokens < 0) return fail(FXR_ERR_INVALID, "n_tokens < 0");
     if (!count || (n_tokens > 0 && (!mask || !idx))) return fail(FXR_ERR_INVALID, "null pointer");
     fxr::CompactArgs a{};
-    a.s[0] = fxr::CompactStream{mask, valid, idx, count};
-    return launch_compact_streams(a, 1, n_tokens, split, stream);
+    a.s[0] = fxr::CompactStream{mask, valid, idx, count, restore ? *restore : fxr::RestoreList{}};
+    return launch_compact_streams(a, 1, n_tokens, split, stream, nullptr, 0, 0, n_heads);
 }
 
 int32_t fxr_mask_compact(int32_t* mask, const uint8_t* valid, int32_t n_tokens, int32_t* idx,
@@ -993,7 +1037,8 @@ static int32_t frame_forward_impl(const fxr_frame_desc* desc, const void* q, con
     // device-resident frames: the gather compacts the mask itself (one launch fewer); host-resident
     // ones need the index list before the gather, for the row upload
     const bool fused = !host && gather_can_compact(1, desc->n_tokens);
-    if (!fused && (st = launch_compact(mask, valid, desc->n_tokens, w.idx, w.count, split, stream)) != FXR_OK)
+    if (!fused && (st = launch_compact(mask, valid, desc->n_tokens, w.idx, w.count, split, stream, &w.restore,
+                                       desc->n_heads)) != FXR_OK)
         return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const size_t eb = dtype_bytes(desc->dtype);
@@ -1011,7 +1056,7 @@ static int32_t frame_forward_impl(const fxr_frame_desc* desc, const void* q, con
         if ((st = check_gather_args(desc, q, k, v, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc, w.ld_qc,
                                     cache_k, cache_v, w.save)) != FXR_OK)
             return st;
-        fxr::GatherStream gs{q, k, v, mask, w.idx, w.count, w.qc, cache_k, cache_v, w.save, valid};
+        fxr::GatherStream gs{q, k, v, mask, w.idx, w.count, w.qc, cache_k, cache_v, w.save, valid, w.restore};
         st = desc->dtype == FXR_BF16
                  ? launch_gather_streams<__nv_bfloat16>(desc, 1, &gs, pos, norm_q, norm_k, w.ld_qc, s, nullptr,
                                                         nullptr, 0, &split)
@@ -1025,11 +1070,13 @@ static int32_t frame_forward_impl(const fxr_frame_desc* desc, const void* q, con
     OutSet os;
     os.out = out;
     os.split = split;
+    bool restored = false;
     st = desc->dtype == FXR_BF16
-             ? launch_attention<__nv_bfloat16>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s)
-             : launch_attention<__half>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s);
+             ? launch_attention<__nv_bfloat16>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s, &w,
+                                               &restored)
+             : launch_attention<__half>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s, &w, &restored);
     if (st != FXR_OK) return st;
-    if ((st = fxr_restore_rows(desc, mask, w.idx, w.count, w.save, cache_k, cache_v, stream)) != FXR_OK)
+    if (!restored && (st = fxr_restore_rows(desc, mask, w.idx, w.count, w.save, cache_k, cache_v, stream)) != FXR_OK)
         return st;
     if (host) {
         const void* src[1] = {out};
@@ -1067,7 +1114,7 @@ int32_t fxr_frame_step(int32_t step, const fxr_frame_desc* desc, const void* q, 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (step) {
     case FXR_STEP_COMPACT:
-        return launch_compact(mask, valid, desc->n_tokens, w.idx, w.count, split, stream);
+        return launch_compact(mask, valid, desc->n_tokens, w.idx, w.count, split, stream, &w.restore, desc->n_heads);
     case FXR_STEP_GATHER:
     case FXR_STEP_GATHER_COMPACT: {
         if (!cache_k || !cache_v || !aligned16(cache_k) || !aligned16(cache_v))
@@ -1080,7 +1127,7 @@ int32_t fxr_frame_step(int32_t step, const fxr_frame_desc* desc, const void* q, 
         if ((st = check_gather_args(desc, q, k, v, mask, w.idx, w.count, pos, norm_q, norm_k, w.qc, w.ld_qc,
                                     cache_k, cache_v, w.save)) != FXR_OK)
             return st;
-        fxr::GatherStream gs{q, k, v, mask, w.idx, w.count, w.qc, cache_k, cache_v, w.save, valid};
+        fxr::GatherStream gs{q, k, v, mask, w.idx, w.count, w.qc, cache_k, cache_v, w.save, valid, w.restore};
         return desc->dtype == FXR_BF16
                    ? launch_gather_streams<__nv_bfloat16>(desc, 1, &gs, pos, norm_q, norm_k, w.ld_qc, s, nullptr,
                                                           nullptr, 0, &split)
@@ -1093,11 +1140,16 @@ int32_t fxr_frame_step(int32_t step, const fxr_frame_desc* desc, const void* q, 
         OutSet os;
         os.out = out;
         os.split = split;
+        bool restored = false;
         return desc->dtype == FXR_BF16
-                   ? launch_attention<__nv_bfloat16>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s)
-                   : launch_attention<__half>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s);
+                   ? launch_attention<__nv_bfloat16>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s,
+                                                     &w, &restored)
+                   : launch_attention<__half>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s, &w,
+                                              &restored);
     }
     default:
+        // nothing left to do when the two-tile attention restored the rows in its tail
+        if (attention_restores(desc->dtype)) return FXR_OK;
         return fxr_restore_rows(desc, mask, w.idx, w.count, w.save, cache_k, cache_v, stream);
     }
 }
@@ -1490,8 +1542,9 @@ static int32_t double_block_impl(const fxr_frame_desc* desc, const fxr_double_bl
     // 1. compaction; text tokens always execute; the GEMM sync words start from zero
     {
         fxr::CompactArgs ca{};
-        ca.s[0] = fxr::CompactStream{mask, valid, idx, count};
-        if ((st = launch_compact_streams(ca, 1, N, b.split, stream, gemm, fxr::gemm::kSyncBytes, T)) != FXR_OK)
+        ca.s[0] = fxr::CompactStream{mask, valid, idx, count, b.frame.restore};
+        if ((st = launch_compact_streams(ca, 1, N, b.split, stream, gemm, fxr::gemm::kSyncBytes, T,
+                                         desc->n_heads)) != FXR_OK)
             return st;
     }
     if ((st = block_upload(host, x_in, C, dtype_bytes(dt), idx, count, N, s)) != FXR_OK) return st;
@@ -1540,12 +1593,14 @@ static int32_t double_block_impl(const fxr_frame_desc* desc, const fxr_double_bl
     OutSet os;
     os.out = b.attn;
     os.split = b.split;
+    bool restored = false;
     st = dt == FXR_BF16 ? launch_attention<__nv_bfloat16>(&fd, b.frame.qc, b.frame.ld_qc, count, cache_k, cache_v,
-                                                          idx, os, s)
+                                                          idx, os, s, &b.frame, &restored)
                         : launch_attention<__half>(&fd, b.frame.qc, b.frame.ld_qc, count, cache_k, cache_v, idx,
-                                                   os, s);
+                                                   os, s, &b.frame, &restored);
     if (st != FXR_OK) return st;
-    if ((st = fxr_restore_rows(&fd, mask, idx, count, b.frame.save, cache_k, cache_v, stream)) != FXR_OK) return st;
+    if (!restored && (st = fxr_restore_rows(&fd, mask, idx, count, b.frame.save, cache_k, cache_v, stream)) != FXR_OK)
+        return st;
     // 7. MLP up with GELU (compact), 8. out-projection + MLP down + gated residual (scattered)
     for (int k = first; k < 2; ++k) {
         const fxr_block_stream& w = *ss[k];
@@ -1636,8 +1691,9 @@ static int32_t single_block_impl(const fxr_frame_desc* desc, const fxr_single_bl
     const size_t gemm_bytes = fxr_rows_gemm_scratch_size();
     {
         fxr::CompactArgs ca{};
-        ca.s[0] = fxr::CompactStream{mask, valid, idx, count};
-        if ((st = launch_compact_streams(ca, 1, N, b.split, stream, b.gemm, fxr::gemm::kSyncBytes, T)) != FXR_OK)
+        ca.s[0] = fxr::CompactStream{mask, valid, idx, count, b.frame.restore};
+        if ((st = launch_compact_streams(ca, 1, N, b.split, stream, b.gemm, fxr::gemm::kSyncBytes, T,
+                                         desc->n_heads)) != FXR_OK)
             return st;
     }
     if ((st = block_upload(host, x_in, C, dtype_bytes(dt), idx, count, N, s)) != FXR_OK) return st;
@@ -1667,12 +1723,14 @@ static int32_t single_block_impl(const fxr_frame_desc* desc, const fxr_single_bl
     OutSet os;
     os.out = b.attn;
     os.split = b.split;
+    bool restored = false;
     st = dt == FXR_BF16 ? launch_attention<__nv_bfloat16>(&fd, b.frame.qc, b.frame.ld_qc, count, cache_k, cache_v,
-                                                          idx, os, s)
+                                                          idx, os, s, &b.frame, &restored)
                         : launch_attention<__half>(&fd, b.frame.qc, b.frame.ld_qc, count, cache_k, cache_v, idx,
-                                                   os, s);
+                                                   os, s, &b.frame, &restored);
     if (st != FXR_OK) return st;
-    if ((st = fxr_restore_rows(&fd, mask, idx, count, b.frame.save, cache_k, cache_v, stream)) != FXR_OK) return st;
+    if (!restored && (st = fxr_restore_rows(&fd, mask, idx, count, b.frame.save, cache_k, cache_v, stream)) != FXR_OK)
+        return st;
     {   // x_out = x_in + gate * ([attention | MLP] . W_out^T + b_out): W_out's two column blocks
         fxr_rows_gemm_desc g{};
         g.dtype = dt;
@@ -1816,19 +1874,21 @@ static int32_t batch_group(const fxr_frame_desc* desc, int32_t nb, const fxr_str
     fxr::GatherStream gs[fxr::kMaxBatch];
     AttnStreamArgs as[fxr::kMaxBatch];
     fxr::RestoreArgs ra{};
+    Views wv[fxr::kMaxBatch];
     int64_t ld_qc = 0;
     for (int32_t b = 0; b < nb; ++b) {
-        const Views w = carve(desc, ws + (size_t)b * base);
+        wv[b] = carve(desc, ws + (size_t)b * base);
+        const Views& w = wv[b];
         const fxr_stream_frame& x = f[b];
         if (!x.q || !x.k || !x.v || !x.mask || !x.cache_k || !x.cache_v || !x.out)
             return fail(FXR_ERR_INVALID, "stream %d: null pointer", b);
         if (!aligned16(x.q) || !aligned16(x.k) || !aligned16(x.v) || !aligned16(x.cache_k) ||
             !aligned16(x.cache_v) || !aligned16(x.out))
             return fail(FXR_ERR_INVALID, "stream %d: buffers must be 16-byte aligned", b);
-        ca.s[b] = fxr::CompactStream{x.mask, x.valid, w.idx, w.count};
+        ca.s[b] = fxr::CompactStream{x.mask, x.valid, w.idx, w.count, w.restore};
         gs[b] = fxr::GatherStream{x.q, x.k, x.v, x.mask, w.idx, w.count, w.qc, x.cache_k, x.cache_v, w.save,
-                                  x.valid};
-        as[b] = AttnStreamArgs{w.qc, w.ld_qc, w.count, x.cache_k, x.cache_v, w.idx, x.out};
+                                  x.valid, w.restore};
+        as[b] = AttnStreamArgs{w.qc, w.ld_qc, w.count, x.cache_k, x.cache_v, w.idx, x.out, &wv[b]};
         ra.s[b] = fxr::RestoreStream{x.mask, w.idx, w.count, static_cast<const uint4*>(w.save),
                                      static_cast<char*>(x.cache_k), static_cast<char*>(x.cache_v)};
         ld_qc = w.ld_qc;
@@ -1837,12 +1897,15 @@ static int32_t batch_group(const fxr_frame_desc* desc, int32_t nb, const fxr_str
     // the gather compacts every stream's mask itself when its rows fit (one launch fewer)
     const SplitArea none{};
     const bool fused = gather_can_compact(nb, desc->n_tokens);
-    if (!fused && (st = launch_compact_streams(ca, nb, desc->n_tokens, SplitArea{}, s)) != FXR_OK) return st;
+    if (!fused && (st = launch_compact_streams(ca, nb, desc->n_tokens, SplitArea{}, s, nullptr, 0, 0,
+                                               desc->n_heads)) != FXR_OK)
+        return st;
     if ((st = launch_gather_streams<T>(desc, nb, gs, pos, nq, nk, ld_qc, s, nullptr, nullptr, 0,
                                        fused ? &none : nullptr)) != FXR_OK)
         return st;
-    if ((st = launch_attention_streams<T>(desc, nb, as, SplitArea{}, s)) != FXR_OK) return st;
-    return launch_restore_streams(desc, ra, nb, s);
+    bool restored = false;
+    if ((st = launch_attention_streams<T>(desc, nb, as, SplitArea{}, s, &restored)) != FXR_OK) return st;
+    return restored ? FXR_OK : launch_restore_streams(desc, ra, nb, s);
 }
 
 extern "C" {
@@ -1964,7 +2027,8 @@ int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g, c
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     OutSet os;
     os.split = split_area(need, workspace, workspace_bytes, sd.n_heads);
-    if ((st = launch_compact(mask, valid, sd.n_tokens, w.frame.idx, w.frame.count, os.split, stream)) != FXR_OK)
+    if ((st = launch_compact(mask, valid, sd.n_tokens, w.frame.idx, w.frame.count, os.split, stream,
+                             &w.frame.restore, sd.n_heads)) != FXR_OK)
         return st;
     if ((st = fxr_gather_norm_rope(&sd, static_cast<const char*>(q) + col, static_cast<const char*>(k) + col,
                                    static_cast<const char*>(v) + col, mask, w.frame.idx, w.frame.count, pos,
@@ -1984,11 +2048,15 @@ int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g, c
     } else {
         os.out = static_cast<char*>(g->out[0]) + col;
     }
+    bool restored = false;
     st = sd.dtype == FXR_BF16
-             ? launch_attention<__nv_bfloat16>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, att_idx, os, s)
-             : launch_attention<__half>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, att_idx, os, s);
+             ? launch_attention<__nv_bfloat16>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, att_idx,
+                                               os, s, &w.frame, &restored)
+             : launch_attention<__half>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, att_idx, os,
+                                        s, &w.frame, &restored);
     if (st != FXR_OK) return st;
-    if ((st = fxr_restore_rows(&sd, mask, w.frame.idx, w.frame.count, w.frame.save, cache_k, cache_v, stream)) != FXR_OK)
+    if (!restored &&
+        (st = fxr_restore_rows(&sd, mask, w.frame.idx, w.frame.count, w.frame.save, cache_k, cache_v, stream)) != FXR_OK)
         return st;
     if (!peers) return FXR_OK;
     fxr::PushArgs a{};
@@ -2145,7 +2213,8 @@ int32_t fxr_frame_forward_heads_nccl(const fxr_frame_desc* desc, const fxr_head_
     sd.ld_cache = (int64_t)g->n_heads * desc->head_dim;
     const size_t col = (size_t)g->head0 * desc->head_dim * dtype_bytes(desc->dtype);
     const SplitArea split = split_area(w.total, workspace, workspace_bytes, sd.n_heads);
-    if ((st = launch_compact(mask, valid, sd.n_tokens, w.frame.idx, w.frame.count, split, stream)) != FXR_OK)
+    if ((st = launch_compact(mask, valid, sd.n_tokens, w.frame.idx, w.frame.count, split, stream,
+                             &w.frame.restore, sd.n_heads)) != FXR_OK)
         return st;
     if (g->n_heads > 0) {
         if ((st = fxr_gather_norm_rope(&sd, static_cast<const char*>(q) + col, static_cast<const char*>(k) + col,
@@ -2163,11 +2232,18 @@ int32_t fxr_frame_forward_heads_nccl(const fxr_frame_desc* desc, const fxr_head_
         OutSet os;
         os.out = w.o_local;
         os.split = split;
+        bool restored = false;
         st = od.dtype == FXR_BF16
-                 ? launch_attention<__nv_bfloat16>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, w.iota, os, s)
-                 : launch_attention<__half>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, w.iota, os, s);
+                 ? launch_attention<__nv_bfloat16>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v,
+                                                   w.iota, os, s, &w.frame, &restored)
+                 : launch_attention<__half>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, w.iota,
+                                            os, s, &w.frame, &restored);
         if (st != FXR_OK) return st;
-        if ((st = fxr_restore_rows(&sd, mask, w.frame.idx, w.frame.count, w.frame.save, cache_k, cache_v, stream)) != FXR_OK)
+        if (!restored &&
+            (st = fxr_restore_rows(&sd, mask, w.frame.idx, w.frame.count, w.frame.save, cache_k, cache_v, stream)) != FXR_OK)
+            return st;
+        if (!restored &&
+            (st = fxr_restore_rows(&sd, mask, w.frame.idx, w.frame.count, w.frame.save, cache_k, cache_v, stream)) != FXR_OK)
             return st;
     }
     return fxr_allgather_heads(desc, g, nccl_comm, w.o_local, m_cap, w.gathered, w.frame.idx, w.frame.count,

@@ -36,6 +36,17 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 // Independent edit streams (frames of one geometry) processed by one launch, at most.
 constexpr int kMaxBatch = 8;
 
+// Arrival counters per head of the attention's fused restore of mask==1 cache rows (two-tile
+// kernel); the compaction zeroes them.
+constexpr int kRestoreSlots = 1;
+
+// Atomic add with acquire-release semantics at GPU scope; returns the old value.
+__device__ __forceinline__ int32_t atom_add_acq_rel_gpu(int32_t* addr, int32_t v) {
+    int32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+    return old;
+}
+
 // Release-ordered add at system scope (visible to other GPUs after the writes it orders).
 __device__ __forceinline__ void red_release_sys_add(uint32_t* addr, uint32_t v) {
     asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");

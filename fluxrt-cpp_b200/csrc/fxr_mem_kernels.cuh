@@ -30,11 +30,21 @@ constexpr int kCompactWarps = kCompactThreads / 32;
 constexpr int kCompactGroups = 32;                              // per warp and chunk, at most
 constexpr int kCompactChunk = kCompactWarps * kCompactGroups * 32;
 
+// Rows whose cache rows must be put back after the attention (mask 1, execute without updating the
+// cache), listed by the compaction for the attention's fused restore (two-tile kernel) or for
+// restore_rows_kernel. rows == nullptr: no list.
+struct RestoreList {
+    int32_t* rows;        // [N] compact rows of mask==1 tokens, in no particular order
+    int32_t* count;       // how many
+    int32_t* head_done;   // [n_heads * kRestoreSlots] the attention's arrival counters, zeroed here
+};
+
 struct CompactStream {
     int32_t* mask;
     const uint8_t* valid;
     int32_t* idx;
     int32_t* count;
+    RestoreList rl;
 };
 
 struct CompactArgs {
@@ -45,6 +55,7 @@ struct CompactArgs {
     uint4* zero2;                 // a second area CTA 0 zeroes (the block's GEMM sync words)
     int32_t zero2_vec;
     int32_t n_force;              // tokens below this one execute whatever their mask (0 -> 2)
+    int32_t n_heads;              // restore lists: counters per stream = n_heads * kRestoreSlots
 };
 
 __global__ void __launch_bounds__(kCompactThreads, 1) compact_kernel(const __grid_constant__ CompactArgs a) {
@@ -53,11 +64,16 @@ __global__ void __launch_bounds__(kCompactThreads, 1) compact_kernel(const __gri
     int32_t* __restrict__ idx = a.s[blockIdx.x].idx;
     int32_t* __restrict__ count = a.s[blockIdx.x].count;
     const int32_t n = a.n;
+    const RestoreList rl = a.s[blockIdx.x].rl;
     __shared__ int32_t warp_tot[kCompactWarps];
+    __shared__ int32_t n_restore;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t lt = (1u << lane) - 1u;
     pdl_launch_dependents();
     pdl_wait();  // the previous frame's kernels may still read mask / idx / count
+    if (threadIdx.x == 0) n_restore = 0;
+    if (rl.head_done)
+        for (int32_t e = threadIdx.x; e < a.n_heads * kRestoreSlots; e += kCompactThreads) rl.head_done[e] = 0;
     // the attention's key-split arrival counters of this frame (zero_vec 16-byte words)
     if (blockIdx.x == 0) {
         for (int32_t e = threadIdx.x; e < a.zero_vec; e += kCompactThreads) a.zero[e] = make_uint4(0, 0, 0, 0);
@@ -102,13 +118,20 @@ __global__ void __launch_bounds__(kCompactThreads, 1) compact_kernel(const __gri
         }
 #pragma unroll
         for (int g = 0; g < kCompactGroups; ++g) {
-            if ((ballot[g] >> lane) & 1u) idx[off + __popc(ballot[g] & lt)] = e0 + g * 32;
+            if ((ballot[g] >> lane) & 1u) {
+                const int32_t R = off + __popc(ballot[g] & lt);
+                idx[R] = e0 + g * 32;
+                if (rl.rows != nullptr && mval[g] == 1) rl.rows[atomicAdd(&n_restore, 1)] = R;
+            }
             off += __popc(ballot[g]);
         }
         base += chunk_tot;
         __syncthreads();
     }
-    if (threadIdx.x == 0) *count = base;
+    if (threadIdx.x == 0) {
+        *count = base;
+        if (rl.count) *rl.count = n_restore;
+    }
 }
 
 __global__ void preprocess_mask_kernel(int32_t* __restrict__ mask, const uint8_t* __restrict__ valid,
@@ -152,6 +175,7 @@ struct GatherStream {           // one stream's buffers
     void* cache_v;
     void* save;
     const uint8_t* valid;       // compacting launches: cache-row validity (NULL: every row valid)
+    RestoreList rl;             // compacting launches: the mask==1 list for the restore
 };
 
 struct GatherArgs {
@@ -267,6 +291,7 @@ struct BulkLayout {
 __device__ __forceinline__ int32_t compact_into_list(const GatherArgs& a, uint2* list) {
     __shared__ int32_t cnt[kScanPer * kScanWarps];
     __shared__ int32_t off[kScanPer * kScanWarps + 1];
+    __shared__ int32_t n_restore;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t lt = (1u << lane) - 1u;
     const bool writer = blockIdx.x == 0;
@@ -278,6 +303,12 @@ __device__ __forceinline__ int32_t compact_into_list(const GatherArgs& a, uint2*
         int32_t* mask = const_cast<int32_t*>(a.s[b].mask);
         const uint8_t* valid = a.s[b].valid;
         int32_t* idx = const_cast<int32_t*>(a.s[b].idx);
+        const RestoreList rl = a.s[b].rl;
+        if (writer) {
+            if (threadIdx.x == 0) n_restore = 0;
+            if (rl.head_done)
+                for (int32_t e = threadIdx.x; e < a.n_heads * kRestoreSlots; e += kBulkThreads) rl.head_done[e] = 0;
+        }
         int32_t base = 0;
         for (int32_t c0 = 0; c0 < n; c0 += kScanPer * kBulkThreads) {
             int32_t mv[kScanPer];
@@ -328,7 +359,10 @@ __device__ __forceinline__ int32_t compact_into_list(const GatherArgs& a, uint2*
                 if ((bal[k] >> lane) & 1u) {
                     const int32_t tok = c0 + k * kBulkThreads + (int32_t)threadIdx.x;
                     const int32_t R = base + off[k * kScanWarps + warp] + __popc(bal[k] & lt);
-                    if (writer) idx[R] = tok;
+                    if (writer) {
+                        idx[R] = tok;
+                        if (rl.rows != nullptr && mv[k] == 1) rl.rows[atomicAdd(&n_restore, 1)] = R;
+                    }
                     const int32_t g = pre + R;
                     if (g % (int32_t)gridDim.x == (int32_t)blockIdx.x)
                         list[g / (int32_t)gridDim.x] = make_uint2((uint32_t)tok | ((mv[k] == 1 ? 1u : 2u) << 28),
@@ -338,7 +372,10 @@ __device__ __forceinline__ int32_t compact_into_list(const GatherArgs& a, uint2*
             base += off[kScanPer * kScanWarps];
             __syncthreads();   // cnt / off are rewritten by the next pass
         }
-        if (writer && threadIdx.x == 0) *const_cast<int32_t*>(a.s[b].count) = base;
+        if (writer && threadIdx.x == 0) {
+            *const_cast<int32_t*>(a.s[b].count) = base;
+            if (rl.count) *rl.count = n_restore;
+        }
         pre += base;
     }
     __syncthreads();       // the list is complete

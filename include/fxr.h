@@ -220,8 +220,13 @@ int32_t fxr_attention_f32_bhsd(const float* q, const float* k, const float* v, f
 /* ---- composite ------------------------------------------------------------------------------ */
 /* One frame: compact -> gather/norm/RoPE/cache write -> attention + scatter -> restore of
  * mask==1 rows. The body of the sparse attention plugin's enqueue. Workspace: see
- * fxr_workspace_size. Three kernel launches (the gather compacts the mask itself), no host
- * synchronisation. */
+ * fxr_workspace_size. Two kernel launches, no host synchronisation: the gather compacts the mask
+ * itself, and the attention puts back the cache rows of mask==1 tokens in its tail, head by head
+ * once no CTA reads that head any more (with FXR_ATTENTION_TILES=1, the one-tile kernel, a third
+ * launch does that). The kernels are chained with programmatic dependent launch: the last one lets
+ * a successor launched the same way start early, and such a successor must wait for its
+ * dependency (cudaGridDependencySynchronize) before it reads the frame's outputs, as every
+ * kernel of this library does. */
 int32_t fxr_frame_forward(const fxr_frame_desc* desc,
                           const void* q, const void* k, const void* v,
                           int32_t* mask, const uint8_t* valid, const int32_t* pos,
@@ -237,7 +242,8 @@ int32_t fxr_frame_forward(const fxr_frame_desc* desc,
  *   FXR_STEP_GATHER_COMPACT   the two above in one launch, as fxr_frame_forward runs them
  *   FXR_STEP_ATTENTION        attention + scatter, with the workspace's split / stream-K scratch,
  *                             so that its schedule is the frame's
- *   FXR_STEP_RESTORE          restore of the cache rows of mask==1 tokens
+ *   FXR_STEP_RESTORE          restore of the cache rows of mask==1 tokens (launches nothing when
+ *                             the attention step restored them itself, the two-tile kernel)
  * COMPACT, GATHER, ATTENTION, RESTORE in order (or GATHER_COMPACT, ATTENTION, RESTORE) give the
  * result of fxr_frame_forward bit for bit. Unused pointer arguments of a step may be null. */
 enum {

@@ -286,6 +286,27 @@ def test_frame_forward_parity(cuda, wl, heads):
     assert_close(g["out"][ex], ref, what="O vs oracle on stored operands", **TOL_O)
 
 
+@pytest.mark.parametrize("active,heads", [(0.5, 4), (0.27, 24)])
+def test_frame_restores_many_execute_only_rows(cuda, active, heads):
+    """Most executed rows with mask 1 (execute, keep the cache): their cache rows must come back bit
+    for bit after the frame, which the attention does in its tail, eight warps per head sharing the
+    listed rows (here hundreds per warp). At 27 % active with 24 heads the attention runs its
+    stream-K schedule, so the restore follows cut units too. Outputs (sampled rows) against the
+    oracle on the stored operands."""
+    w = small(W.with_active(W.C2, active), heads)
+    fr = _with_exec_only(W.make_frame(w, seed=71), seed=72, frac=0.9)
+    g = _run_frame(w, fr)
+    m = fr["mask"]
+    ones, twos = m == 1, m == 2
+    assert ones.sum() > 1000
+    assert np.array_equal(g["cache_k"][ones], fr["cache_k"][ones])
+    assert np.array_equal(g["cache_v"][ones], fr["cache_v"][ones])
+    assert np.array_equal(g["cache_v"][twos], fr["v"][twos])
+    assert np.array_equal(g["cache_k"][m == 0], fr["cache_k"][m == 0])
+    rows, ref = _oracle_rows(w, fr, None, w.dtype, n_sample=128, seed=73)
+    assert_close(g["out"][rows], ref, what=f"O, {int(ones.sum())} execute-only rows", **TOL_O)
+
+
 def _oracle_rows(w: W.Workload, fr: dict, valid, operand_dtype: str, n_sample=None, seed=0):
     """Oracle attention outputs of the executed rows (or a seeded sample of n_sample of them) with
     every operand as the CUDA path stores it: Q' and K' rounded to `operand_dtype` after RMSNorm +
