@@ -283,6 +283,10 @@ int grid_rows(int64_t rows, int rows_per_cta) {
 struct OutSet {
     void* out = nullptr;
     SplitArea split;   // key-range split scratch (none: never split)
+    // SMs the attention leaves free, for the zero-copy row transfers of host-resident frames that
+    // run beside it: the two-tile kernel holds a whole SM's registers, so nothing else fits next to
+    // one of its CTAs
+    int32_t reserve_sms = 0;
 };
 
 // Attention kernel for launches that need no key-range split: two query tiles per CTA unless
@@ -325,7 +329,8 @@ static bool attention_restores(int32_t dtype) {
 
 template <typename T>
 int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, const AttnStreamArgs* st,
-                                 const SplitArea& split, cudaStream_t stream, bool* restored = nullptr) {
+                                 const SplitArea& split, cudaStream_t stream, bool* restored = nullptr,
+                                 int32_t reserve_sms = 0) {
     if (restored) *restored = false;
     NvtxRange nvtx_("fxr:attention");
     if (n_streams < 1 || n_streams > fxr::kMaxBatch) return fail(FXR_ERR_INVALID, "1..%d streams per launch", fxr::kMaxBatch);
@@ -406,7 +411,8 @@ int32_t launch_attention_streams(const fxr_frame_desc* d, int32_t n_streams, con
             *restored = true;
         }
         const int64_t units = (N + fxr::attn2::kRows - 1) / fxr::attn2::kRows * d->n_heads * n_streams;
-        const int grid = sk ? sm_count() : (int)std::max<int64_t>(1, std::min<int64_t>(units, sm_count()));
+        const int ctas = std::max(1, sm_count() - std::max(0, reserve_sms));
+        const int grid = sk ? ctas : (int)std::max<int64_t>(1, std::min<int64_t>(units, ctas));
         e = sk ? launch_pdl(fxr::attn2::attention_kernel<T, true>, dim3(grid), dim3(fxr::attn2::kThreads),
                             fxr::attn2::kSmemBytes, stream, maps, p)
                : launch_pdl(fxr::attn2::attention_kernel<T, false>, dim3(grid), dim3(fxr::attn2::kThreads),
@@ -433,7 +439,7 @@ int32_t launch_attention(const fxr_frame_desc* d, const void* qc, int64_t ld_qc,
                          const void* ck, const void* cv, const int32_t* idx, const OutSet& os,
                          cudaStream_t stream, const Views* frame = nullptr, bool* restored = nullptr) {
     const AttnStreamArgs st{qc, ld_qc, count, ck, cv, idx, os.out, frame};
-    return launch_attention_streams<T>(d, 1, &st, os.split, stream, restored);
+    return launch_attention_streams<T>(d, 1, &st, os.split, stream, restored, os.reserve_sms);
 }
 
 // Gather of n_streams frames of the same geometry (one launch; rows stream after stream).
@@ -994,6 +1000,10 @@ struct HostIo {
 
 // Executed rows idx[0..M) of n tensors from src to dst at the same row positions (one side mapped
 // host memory), chained to the previous launch on the stream.
+// SMs the attention of a host-resident frame leaves to the zero-copy row transfers (which reach the
+// PCIe rate from 32 CTAs of 64 threads: four per SM fit there)
+constexpr int kHostReserveSms = 8;
+
 static int32_t launch_host_rows(const void* const* src, void* const* dst, int n, int64_t ld_elems,
                                 int64_t row_bytes, size_t elem_bytes, const int32_t* idx,
                                 const int32_t* count, int32_t n_tokens, cudaStream_t s) {
@@ -1070,6 +1080,8 @@ static int32_t frame_forward_impl(const fxr_frame_desc* desc, const void* q, con
     OutSet os;
     os.out = out;
     os.split = split;
+    // host-resident frames: leave SMs to the row transfers of the frames before and after this one
+    os.reserve_sms = host ? kHostReserveSms : 0;
     bool restored = false;
     st = desc->dtype == FXR_BF16
              ? launch_attention<__nv_bfloat16>(desc, w.qc, w.ld_qc, w.count, cache_k, cache_v, w.idx, os, s, &w,
@@ -1593,6 +1605,7 @@ static int32_t double_block_impl(const fxr_frame_desc* desc, const fxr_double_bl
     OutSet os;
     os.out = b.attn;
     os.split = b.split;
+    os.reserve_sms = host ? kHostReserveSms : 0;   // host-resident x: SMs for the row transfers
     bool restored = false;
     st = dt == FXR_BF16 ? launch_attention<__nv_bfloat16>(&fd, b.frame.qc, b.frame.ld_qc, count, cache_k, cache_v,
                                                           idx, os, s, &b.frame, &restored)
@@ -1723,6 +1736,7 @@ static int32_t single_block_impl(const fxr_frame_desc* desc, const fxr_single_bl
     OutSet os;
     os.out = b.attn;
     os.split = b.split;
+    os.reserve_sms = host ? kHostReserveSms : 0;   // host-resident x: SMs for the row transfers
     bool restored = false;
     st = dt == FXR_BF16 ? launch_attention<__nv_bfloat16>(&fd, b.frame.qc, b.frame.ld_qc, count, cache_k, cache_v,
                                                           idx, os, s, &b.frame, &restored)

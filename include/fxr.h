@@ -267,7 +267,10 @@ int32_t fxr_frame_step(int32_t step, const fxr_frame_desc* desc,
  *   1. the mask is copied to the workspace and compacted on the device;
  *   2. a zero-copy kernel reads the executed tokens' Q, K, V rows from host memory into device
  *      staging rows (other rows are never read: the attention takes their K/V from the cache);
- *   3. the frame runs as fxr_frame_forward on the staging buffers;
+ *   3. the frame runs as fxr_frame_forward on the staging buffers, its attention on 8 fewer SMs
+ *      so that the row transfers of the frames around it (another stream) keep running beside it
+ *      (results equal fxr_frame_forward's bit for bit when both schedules run whole units, and
+ *      within rounding when the smaller grid changes the attention's schedule);
  *   4. a zero-copy kernel writes the executed tokens' output rows into host_out.
  * Arguments:
  *   host_q, host_k, host_v  [n_tokens, n_heads * head_dim] dtype, page-locked host memory mapped
