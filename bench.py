@@ -77,8 +77,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--split", choices=["replicas", "heads", "heads_nccl"], default=None,
                     help="multi-GPU mode: independent streams per GPU (default except c5) or one "
-                         "frame split by heads with the O all-gather fused into the attention "
-                         "epilogue (default for c5), or the same split with the O exchange as "
+                         "frame split by heads whose O rows an exchange kernel stores into every "
+                         "GPU's output over NVLink (default for c5), or the same split with the O "
+                         "exchange as "
                          "one NCCL all-gather + scatter (heads_nccl)")
     a = ap.parse_args()
     if a.split is None:
@@ -997,12 +998,12 @@ def run_heads(args, embedded: bool = False):
                      "achieved_frac": round(max(t_tensor, t_link) * 1e3 / ms_per_step, 4),
                      "peak_tensor": pk["bf16_tflops"], "peak_nvlink_gbs": 770.0,
                      "nvlink_bytes_per_rank": nvlink_bytes,
-                     "note": "frac = roofline time of one frame / measured frame time (whole frame, 5 kernels)"},
+                     "note": "frac = roofline time of one frame / measured frame time (the whole frame)"},
         "e2e": None,
-        # compaction, gather, attention (which restores mask==1 rows); with peers also the row
-        # numbering and the exchange (heads_push_kernel, or heads_scatter_kernel after NCCL's own
-        # all-gather kernel)
-        "gpu_launches": (3 if world == 1 else 5) * args.steps,
+        # the gather (which compacts the mask) and the attention (which restores mask==1 rows);
+        # with peers also the exchange and the arrival wait (heads_push_kernel, arrival_wait_kernel),
+        # or the scatter after NCCL's own all-gather kernel (heads_scatter_kernel)
+        "gpu_launches": (3 if nccl else 2 if world == 1 else 4) * args.steps,
         "clocks": clk,
     }
     if rank == 0 and not embedded:

@@ -451,12 +451,18 @@ static bool gather_can_compact(int32_t n_streams, int32_t n_tokens) {
     return n_tokens < (1 << 24) && (rows + grid - 1) / grid <= fxr::kBulkListCap;
 }
 
+// Identity output rows that a gather launch writes besides its own work (GatherArgs::iota).
+struct RowIota {
+    int32_t* idx = nullptr;
+    int32_t n = 0, cap = 0;
+};
+
 template <typename T>
 int32_t launch_gather_streams(const fxr_frame_desc* d, int32_t n_streams, const fxr::GatherStream* gs,
                               const int32_t* pos, const float* nq, const float* nk, int64_t ld_qc,
                               cudaStream_t stream, const float* nq_txt = nullptr,
                               const float* nk_txt = nullptr, int32_t n_text_norm = 0,
-                              const SplitArea* compact_split = nullptr) {
+                              const SplitArea* compact_split = nullptr, RowIota iota = RowIota{}) {
     NvtxRange nvtx_("fxr:gather");
     if (n_streams < 1 || n_streams > fxr::kMaxBatch) return fail(FXR_ERR_INVALID, "1..%d streams per launch", fxr::kMaxBatch);
     fxr::GatherArgs a{};
@@ -469,6 +475,9 @@ int32_t launch_gather_streams(const fxr_frame_desc* d, int32_t n_streams, const 
     }
     for (int32_t b = 0; b < n_streams; ++b) a.s[b] = gs[b];
     a.n_streams = n_streams;
+    a.iota = iota.idx;
+    a.iota_n = iota.n;
+    a.iota_cap = iota.cap;
     a.pos = pos;
     a.norm_q = nq;
     a.norm_k = nk;
@@ -1979,6 +1988,33 @@ int32_t fxr_head_group_init(fxr_head_group* g, int32_t world, int32_t rank, int3
     return FXR_OK;
 }
 
+// Gather of one GPU's share of a head-split frame (its heads of every executed token, read from
+// the full-width rows at q/k/v + the share's first column). The gather compacts the mask itself
+// when its lists fit (one launch), else a compaction kernel runs first; `iota` also receives the
+// identity row list of a compact attention output.
+static int32_t gather_share(const fxr_frame_desc* sd, const char* q, const char* k, const char* v, int32_t* mask,
+                            const uint8_t* valid, const Views& fw, const int32_t* pos, const float* norm_q,
+                            const float* norm_k, void* cache_k, void* cache_v, const SplitArea& split,
+                            RowIota iota, cudaStream_t s) {
+    int32_t st = check_desc(sd, false);
+    if (st != FXR_OK) return st;
+    const bool fused = gather_can_compact(1, sd->n_tokens);
+    if (!fused && (st = launch_compact(mask, valid, sd->n_tokens, fw.idx, fw.count, split, s, &fw.restore,
+                                       sd->n_heads)) != FXR_OK)
+        return st;
+    if ((st = check_gather_args(sd, q, k, v, mask, fw.idx, fw.count, pos, norm_q, norm_k, fw.qc, fw.ld_qc, cache_k,
+                                cache_v, fw.save)) != FXR_OK)
+        return st;
+    fxr::GatherStream gs{q, k, v, mask, fw.idx, fw.count, fw.qc, cache_k, cache_v, fw.save,
+                         fused ? valid : nullptr, fw.restore};
+    const SplitArea* cs = fused ? &split : nullptr;
+    return sd->dtype == FXR_BF16
+               ? launch_gather_streams<__nv_bfloat16>(sd, 1, &gs, pos, norm_q, norm_k, fw.ld_qc, s, nullptr, nullptr,
+                                                      0, cs, iota)
+               : launch_gather_streams<__half>(sd, 1, &gs, pos, norm_q, norm_k, fw.ld_qc, s, nullptr, nullptr, 0, cs,
+                                               iota);
+}
+
 // Workspace of one GPU's share of a head-split frame with peers: the share's frame workspace, then
 // an identity row list (the attention's compact output) and the compact O rows of its heads.
 struct HeadsViews {
@@ -2041,21 +2077,16 @@ int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g, c
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     OutSet os;
     os.split = split_area(need, workspace, workspace_bytes, sd.n_heads);
-    if ((st = launch_compact(mask, valid, sd.n_tokens, w.frame.idx, w.frame.count, os.split, stream,
-                             &w.frame.restore, sd.n_heads)) != FXR_OK)
-        return st;
-    if ((st = fxr_gather_norm_rope(&sd, static_cast<const char*>(q) + col, static_cast<const char*>(k) + col,
-                                   static_cast<const char*>(v) + col, mask, w.frame.idx, w.frame.count, pos,
-                                   norm_q, norm_k, w.frame.qc, w.frame.ld_qc, cache_k, cache_v, w.frame.save,
-                                   stream)) != FXR_OK)
+    // with peers the attention writes a compact output, row m of this GPU's heads at o_local[m]
+    // (identity row list written by the gather), which the exchange scatters
+    const RowIota iota = peers ? RowIota{w.iota, desc->n_tokens, desc->n_tokens} : RowIota{};
+    if ((st = gather_share(&sd, static_cast<const char*>(q) + col, static_cast<const char*>(k) + col,
+                           static_cast<const char*>(v) + col, mask, valid, w.frame, pos, norm_q, norm_k, cache_k,
+                           cache_v, os.split, iota, s)) != FXR_OK)
         return st;
     fxr_frame_desc od = sd;
     const int32_t* att_idx = w.frame.idx;
     if (peers) {
-        // compact output: row m of this GPU's heads at o_local[m]; the exchange scatters it
-        fxr::iota_rows_kernel<<<std::max(1, std::min(grid_rows(desc->n_tokens, 256), sm_count())), 256, 0, s>>>(
-            w.iota, desc->n_tokens, desc->n_tokens);
-        FXR_CHECK_LAUNCH("iota_rows_kernel launch");
         od.ld_out = sd.ld_cache;
         os.out = w.o_local;
         att_idx = w.iota;
@@ -2227,18 +2258,17 @@ int32_t fxr_frame_forward_heads_nccl(const fxr_frame_desc* desc, const fxr_head_
     sd.ld_cache = (int64_t)g->n_heads * desc->head_dim;
     const size_t col = (size_t)g->head0 * desc->head_dim * dtype_bytes(desc->dtype);
     const SplitArea split = split_area(w.total, workspace, workspace_bytes, sd.n_heads);
-    if ((st = launch_compact(mask, valid, sd.n_tokens, w.frame.idx, w.frame.count, split, stream,
+    if (g->n_heads == 0 &&
+        (st = launch_compact(mask, valid, sd.n_tokens, w.frame.idx, w.frame.count, split, stream,
                              &w.frame.restore, sd.n_heads)) != FXR_OK)
         return st;
     if (g->n_heads > 0) {
-        if ((st = fxr_gather_norm_rope(&sd, static_cast<const char*>(q) + col, static_cast<const char*>(k) + col,
-                                       static_cast<const char*>(v) + col, mask, w.frame.idx, w.frame.count, pos,
-                                       norm_q, norm_k, w.frame.qc, w.frame.ld_qc, cache_k, cache_v, w.frame.save,
-                                       stream)) != FXR_OK)
+        // compact output rows m < m_cap (identity list written by the gather; rows past m_cap are
+        // flagged by the attention as out of range)
+        if ((st = gather_share(&sd, static_cast<const char*>(q) + col, static_cast<const char*>(k) + col,
+                               static_cast<const char*>(v) + col, mask, valid, w.frame, pos, norm_q, norm_k,
+                               cache_k, cache_v, split, RowIota{w.iota, desc->n_tokens, m_cap}, s)) != FXR_OK)
             return st;
-        fxr::iota_rows_kernel<<<std::max(1, std::min(grid_rows(desc->n_tokens, 256), sm_count())), 256, 0, s>>>(
-            w.iota, m_cap, desc->n_tokens);
-        FXR_CHECK_LAUNCH("iota_rows_kernel launch");
         fxr_frame_desc od = sd;                          // compact O output: row m, local heads
         od.ld_out = (int64_t)((desc->n_heads + g->world - 1) / g->world) * desc->head_dim;
         if (!cache_k || !cache_v || !aligned16(cache_k) || !aligned16(cache_v))
@@ -2253,9 +2283,6 @@ int32_t fxr_frame_forward_heads_nccl(const fxr_frame_desc* desc, const fxr_head_
                  : launch_attention<__half>(&od, w.frame.qc, w.frame.ld_qc, w.frame.count, cache_k, cache_v, w.iota,
                                             os, s, &w.frame, &restored);
         if (st != FXR_OK) return st;
-        if (!restored &&
-            (st = fxr_restore_rows(&sd, mask, w.frame.idx, w.frame.count, w.frame.save, cache_k, cache_v, stream)) != FXR_OK)
-            return st;
         if (!restored &&
             (st = fxr_restore_rows(&sd, mask, w.frame.idx, w.frame.count, w.frame.save, cache_k, cache_v, stream)) != FXR_OK)
             return st;

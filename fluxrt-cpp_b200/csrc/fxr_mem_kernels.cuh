@@ -188,6 +188,10 @@ struct GatherArgs {
     int32_t compact;
     uint4* zero;
     int32_t zero_vec;
+    // iota != null: the launch also writes iota[m] = m for m < iota_cap and -1 up to iota_n (the
+    // output rows of an attention into a compact buffer, as a head-split frame's share uses)
+    int32_t* iota;
+    int32_t iota_n, iota_cap;
     const int32_t* pos;
     const float* norm_q;
     const float* norm_k;
@@ -419,6 +423,9 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
         for (int64_t l = t; l < pos_lines; l += stride) prefetch_l2(reinterpret_cast<const char*>(a.pos) + l * 128);
     }
     pdl_wait();  // count / idx / mask come from the compaction
+    if (a.iota != nullptr)
+        for (int32_t m = blockIdx.x * kBulkThreads + threadIdx.x; m < a.iota_n; m += gridDim.x * kBulkThreads)
+            a.iota[m] = m < a.iota_cap ? m : -1;
 
     // executed rows of all streams, stream after stream: row r of the launch is row r - pre[b] of
     // stream b (pre = exclusive prefix of the streams' counts)
@@ -801,11 +808,6 @@ arrival_wait_kernel(uint32_t* __restrict__ slots, ArrivalCounts c, int32_t n) {
 // output (m < m_cap: m; beyond: -1, which the attention skips and reports), and the scatter of the
 // all-gathered compact rows of every rank into the full-frame output.
 // ---------------------------------------------------------------------------------------------
-__global__ void iota_rows_kernel(int32_t* __restrict__ idx, int32_t m_cap, int32_t n) {
-    for (int32_t m = blockIdx.x * blockDim.x + threadIdx.x; m < n; m += gridDim.x * blockDim.x)
-        idx[m] = m < m_cap ? m : -1;
-}
-
 struct HeadsScatterArgs {
     const char* gathered;      // [world][m_cap][row_bytes]
     const int32_t* idx;
