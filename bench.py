@@ -385,7 +385,13 @@ def run_ours(args):
            "algorithmic_bytes_per_launch": gb, "traffic": profile_traffic(f"gather_{w.name}")}
 
     # ---- end to end through the C ABI with host buffers ----
-    e2e = e2e_measure(cfg, w, frames, wss, stream, reps=max(5, min(50, args.steps)), world=world)
+    # PCIe throughput varies between runs of the same frames by up to ~15 %: three rounds, the
+    # median one reported with all three
+    rounds = [e2e_measure(cfg, w, frames, wss, stream, reps=max(5, min(100, args.steps)), world=world)
+              for _ in range(3)]
+    rounds_us = [r["us_per_frame"] for r in rounds]
+    e2e = sorted(rounds, key=lambda r: r["us_per_frame"])[1]
+    e2e["rounds_us_per_frame"] = rounds_us
 
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
