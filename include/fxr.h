@@ -223,7 +223,8 @@ int32_t fxr_attention_f32_bhsd(const float* q, const float* k, const float* v, f
  * fxr_workspace_size. Two kernel launches, no host synchronisation: the gather compacts the mask
  * itself, and the attention puts back the cache rows of mask==1 tokens in its tail, head by head
  * once no CTA reads that head any more (with FXR_ATTENTION_TILES=1, the one-tile kernel, a third
- * launch does that). The kernels are chained with programmatic dependent launch: the last one lets
+ * launch does that; frames of more than 1024 tokens per SM, over ~150 000 tokens on 148 SMs, exceed
+ * the gather's row list and add a compaction launch). The kernels are chained with programmatic dependent launch: the last one lets
  * a successor launched the same way start early, and such a successor must wait for its
  * dependency (cudaGridDependencySynchronize) before it reads the frame's outputs, as every
  * kernel of this library does. */
@@ -569,8 +570,11 @@ int32_t fxr_head_group_init(fxr_head_group* g, int32_t world, int32_t rank, int3
 /* One frame of this rank's heads. desc describes the FULL frame (n_heads = all heads, ld_qkv and
  * ld_out over all heads); q/k/v are the full-frame inputs; cache_k/cache_v hold this rank's heads
  * only, [n_tokens, g->n_heads * head_dim] packed. Workspace: fxr_workspace_size(desc) suffices.
- * Issues compaction, gather/norm/RoPE, attention, the mask==1 cache restore and (with peers) the
- * exchange with its arrivals; it does not wait for the other ranks (fxr_head_group_wait does), so
+ * Issues the gather/norm/RoPE (which also compacts the mask, and with peers writes the identity row
+ * list of the compact output), the attention (which also restores the mask==1 cache rows) and, with
+ * peers, the exchange with its arrivals: three launches, two on a single GPU (plus the compaction or
+ * the restore launch in the cases fxr_frame_forward names). It does
+ * not wait for the other ranks (fxr_head_group_wait does), so
  * a single GPU may emulate several ranks by issuing every rank's frame before any rank's wait.
  * Callers must not let a rank start frame f+1 while another rank still reads frame f's output. */
 int32_t fxr_frame_forward_heads(const fxr_frame_desc* desc, fxr_head_group* g,

@@ -421,6 +421,29 @@ def test_high_resolution_and_split_attention_vs_oracle(cuda, wl, heads, active, 
         assert_close(g["out"][rows], u[rows], what="O cut vs whole units", **TOL_O)
 
 
+def test_frame_past_the_gather_list_capacity_vs_oracle(cuda):
+    """A frame of 160 512 tokens (a 400 x 400 grid and 512 text tokens), one head, 2 % of the image
+    active: more tokens per CTA than the gather's shared-memory row list holds, so the frame runs
+    the compaction kernel before a gather that reads the index list; its 15 units of 1254 key steps
+    run stream-K with every unit cut into about ten parts that one CTA combines. Sampled executed
+    rows against the oracle, the other rows and the cache bit-exact."""
+    w = W.Workload("grid400_h1", 400, 400, 512, n_heads=1, dtype="bf16", active=0.02)
+    n_sm = torch.cuda.get_device_properties(0).multi_processor_count
+    assert -(-w.n_tokens // n_sm) > 1024          # past the gather's per-CTA list (kBulkListCap)
+    fr = W.make_frame(w, seed=61)
+    M = int((fr["mask"] != 0).sum())
+    assert _cuts_units(M, 1, w.n_tokens, grid=n_sm, slots=4 * n_sm), M
+    g = _run_frame(w, fr)
+    mask = fr["mask"]
+    assert np.array_equal(g["out"][mask == 0], fr["out"][mask == 0])
+    assert np.array_equal(g["cache_k"][mask == 0], fr["cache_k"][mask == 0])
+    assert np.array_equal(g["cache_v"][mask == 2], fr["v"][mask == 2])
+    rows, ref = _oracle_rows(w, fr, None, "bf16", n_sample=64, seed=62)
+    assert_close(g["out"][rows], ref, what="O 160k tokens vs oracle on stored operands", **TOL_O)
+    _, ref32 = _oracle_rows(w, fr, None, "f32", n_sample=64, seed=62)
+    assert_close(g["out"][rows], ref32, what="O 160k tokens vs fp32 oracle", **TOL_O)
+
+
 # ---------------------------------------------------------------------------------------------
 # reference known-answer tests, run through the GPU path
 # ---------------------------------------------------------------------------------------------
