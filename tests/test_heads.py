@@ -138,11 +138,17 @@ def _frame_tensors(w, fr):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("world,dtype", [(2, "bf16"), (3, "bf16"), (4, "f16")])
-def test_heads_emulated_on_one_gpu_match_the_frame(cuda, world, dtype):
+@pytest.mark.parametrize("world,dtype,geom", [(2, "bf16", "c2_h12"), (3, "bf16", "c2_h12"), (4, "f16", "c2_h12"),
+                                              (2, "bf16", "grid400_h2")])
+def test_heads_emulated_on_one_gpu_match_the_frame(cuda, world, dtype, geom):
+    """Every rank's share issued before any wait, on one GPU; the assembled frame equals the
+    single-GPU frame within the O bar and the oracle on sampled rows. grid400_h2: 160 512 tokens,
+    more per CTA than the gather's row list holds (the compaction kernel runs first)."""
     import torch
-    w = W.Workload("c2_h12", 64, 64, 512, 12, 128, dtype, 0.25, "bernoulli", (16, 56, 56),
-                   10000.0)
+    if geom == "c2_h12":
+        w = W.Workload("c2_h12", 64, 64, 512, 12, 128, dtype, 0.25, "bernoulli", (16, 56, 56), 10000.0)
+    else:
+        w = W.Workload("grid400_h2", 400, 400, 512, 2, 128, dtype, 0.02, "bernoulli", (16, 56, 56), 10000.0)
     cfg = fxr.FrameConfig(n_tokens=w.n_tokens, n_text=w.n_text, n_heads=w.n_heads, dtype=dtype,
                           rope_axes=w.rope_axes, rope_theta=w.rope_theta)
     ws_full = torch.empty(fxr.workspace_size(cfg), dtype=torch.uint8, device="cuda")
