@@ -512,6 +512,7 @@ int32_t launch_gather_streams(const fxr_frame_desc* d, int32_t n_streams, const 
         configured[dev] = true;
     }
     const int grid = std::max(1, std::min<int>(sm_count(), d->n_tokens));
+    a.grid_magic = grid > 1 ? (uint32_t)(((1ull << 32) + (uint64_t)grid - 1) / (uint64_t)grid) : 0u;
     cudaError_t e = launch_pdl(fxr::gather_bulk_kernel<T>, dim3(grid), dim3(fxr::kBulkThreads), smem,
                                stream, a, lay);
     if (e != cudaSuccess) return cuda_status(e, "gather_bulk_kernel launch");

@@ -186,6 +186,7 @@ struct GatherArgs {
     // in shared memory; CTA 0 writes the preprocessed masks, idx and count for the later kernels
     // and zeroes the attention's key-split arrival counters (zero, zero_vec 16-byte words).
     int32_t compact;
+    uint32_t grid_magic;         // ceil(2^32 / grid) for grids above 1 (the compaction's row split)
     uint4* zero;
     int32_t zero_vec;
     // iota != null: the launch also writes iota[m] = m for m < iota_cap and -1 up to iota_n (the
@@ -367,10 +368,13 @@ __device__ __forceinline__ int32_t compact_into_list(const GatherArgs& a, uint2*
                         idx[R] = tok;
                         if (rl.rows != nullptr && mv[k] == 1) rl.rows[atomicAdd(&n_restore, 1)] = R;
                     }
-                    const int32_t g = pre + R;
-                    if (g % (int32_t)gridDim.x == (int32_t)blockIdx.x)
-                        list[g / (int32_t)gridDim.x] = make_uint2((uint32_t)tok | ((mv[k] == 1 ? 1u : 2u) << 28),
-                                                                  ((uint32_t)b << 24) | (uint32_t)R);
+                    // g / grid by a multiply with ceil(2^32 / grid): exact while g x grid < 2^32,
+                    // and a compacting launch has g < 1024 x grid (gather_can_compact)
+                    const uint32_t g = (uint32_t)(pre + R);
+                    const uint32_t q = gridDim.x > 1 ? __umulhi(g, a.grid_magic) : g;
+                    if (g - q * gridDim.x == blockIdx.x)
+                        list[q] = make_uint2((uint32_t)tok | ((mv[k] == 1 ? 1u : 2u) << 28),
+                                             ((uint32_t)b << 24) | (uint32_t)R);
                 }
             }
             base += off[kScanPer * kScanWarps];
