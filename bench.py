@@ -404,14 +404,14 @@ def run_ours(args):
         "kernels": {"gather": mem,
                     "in_frame_us": {k[:-3]: round(v, 2) for k, v in kern.items()},
                     "isolated_us": {k[:-3]: round(v, 2) for k, v in iso.items()},
-                    "timing": "the frame's launches (compacting gather, attention; the restore step "
-                              "launches nothing when the attention restores mask==1 rows itself) through "
+                    "timing": "the frame's launches (compacting gather, attention, which restores "
+                              "mask==1 rows itself; the one-tile attention adds a restore launch) through "
                               "fxr_frame_step on the frame's workspace; in_frame: event records between "
                               "them in a CUDA graph, mean over frames (each interval also holds one "
                               "launch gap); isolated: 40 back-to-back launches of one step per graph; the "
                               "attention roofline uses in_frame, the gather roofline isolated"},
         "e2e": e2e,
-        "gpu_launches": 2 * args.steps,   # compacting gather + attention (which restores mask==1 rows)
+        "gpu_launches": len(FRAME_STEPS) * args.steps,   # compacting gather + attention (+ restore)
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -467,14 +467,16 @@ def run_step(cfg, fr, ws, step):
                    fr["norm_k"], fr["cache_k"], fr["cache_v"], fr["out"], ws)
 
 
-# The frame's steps as fxr_frame_step runs them (same workspace, same schedule; the restore step
-# launches nothing when the two-tile attention restored the mask==1 rows itself).
-FRAME_STEPS = (("gather_us", 2), ("attention_us", 3), ("restore_us", 4))
+# The frame's launches as fxr_frame_step runs them (same workspace, same schedule): the compacting
+# gather and the attention, which restores the mask==1 rows itself; the one-tile attention
+# (FXR_ATTENTION_TILES=1) leaves the restore to a third launch.
+ONE_TILE = os.environ.get("FXR_ATTENTION_TILES", "") == "1"
+FRAME_STEPS = (("gather_us", 2), ("attention_us", 3)) + ((("restore_us", 4),) if ONE_TILE else ())
 
 
 def per_kernel_times(cfg, w, frames, wss, stream, reps: int):
-    """Per-kernel device time inside a stream of frames: the frame's three launches (compacting
-    gather, attention, restore; fxr_frame_step on the frame's own workspace) of `reps` frames are
+    """Per-kernel device time inside a stream of frames: the frame's launches (FRAME_STEPS, through
+    fxr_frame_step on the frame's own workspace) of `reps` frames are
     captured in one CUDA graph with event records between them (on the launching stream), so host
     launch overhead does not leak into the intervals. Mean over frames: event timestamps inside a
     graph advance in steps of about 2 us on this GPU, so a median would land on a tick; the mean
