@@ -500,10 +500,12 @@ int32_t fxr_qkv_project(const fxr_frame_desc* desc, const void* hidden, int64_t 
 
 /* ---- independent edit streams in one set of launches -------------------------------------------
  * n_streams frames of the same geometry (the plugin's batch dimension; config 4 runs 8 streams of
- * 768x768): one compaction launch (a CTA per stream), one gather launch over every stream's
- * executed rows, one attention launch over every stream's (query tile, head) units — which fills
- * the GPU where one small frame leaves SMs idle — and one restore launch; more than FXR_MAX_BATCH
- * streams run as consecutive groups. Streams share the geometry, pos and the norm weights; each
+ * 768x768): one gather launch over every stream's executed rows, which also compacts every
+ * stream's mask, and one attention launch over every stream's (query tile, head) units — which
+ * fills the GPU where one small frame leaves SMs idle — and also restores every stream's mask==1
+ * cache rows (a compaction launch is added when the streams' rows exceed the gather's row list, a
+ * restore launch with FXR_ATTENTION_TILES=1); more than FXR_MAX_BATCH streams run as consecutive
+ * groups. Streams share the geometry, pos and the norm weights; each
  * has its own inputs, mask, validity, K/V cache and output. Results equal per-stream
  * fxr_frame_forward calls bit for bit. */
 #define FXR_MAX_BATCH 8
