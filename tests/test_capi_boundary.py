@@ -125,3 +125,18 @@ def test_batch_workspace_and_arguments(lib):
     assert lib.fxr_frame_forward_batch(ctypes.byref(d), 0, None, None, None, None, None, 0, None) == fxr.FXR_OK
     st = lib.fxr_frame_forward_batch(ctypes.byref(d), 2, None, None, None, None, None, 0, None)
     assert st == fxr.FXR_ERR_INVALID
+
+
+def test_compaction_row_owner_by_multiply_is_exact():
+    """The compacting gather finds the CTA that owns launch row g (g mod grid) and the row's slot
+    (g div grid) with q = umulhi(g, ceil(2^32 / grid)) instead of a division (compact_into_list in
+    fxr_mem_kernels.cuh, the constant from launch_gather_streams in fxr_capi.cu). Restated here for
+    every grid up to 256 CTAs and every row a compacting launch can hold (fewer than 1024 x grid):
+    the quotient equals the integer division, as the bound g x grid < 2^32 guarantees."""
+    import numpy as np
+    for grid in range(2, 257):
+        magic = ((1 << 32) + grid - 1) // grid
+        g = np.arange(0, 1024 * grid, dtype=np.uint64)
+        q = (g * np.uint64(magic)) >> np.uint64(32)
+        assert np.array_equal(q, g // np.uint64(grid)), grid
+        assert 1024 * grid * grid < (1 << 32)
