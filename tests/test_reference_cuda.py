@@ -8,8 +8,8 @@ frame runs on the state the first one left — bit-exact; the GELU, bias and mod
 (flux2_kernels.cu:14-56, gather_scatter_kernels.cu:77-99) against the oracle's restatements
 (oracle/fxr_oracle.c) and the GEMM's fused epilogue. The reference RMSNorm and LayerNorm (uninitialised shared
 accumulators, flux2_kernels.cu:58-82, gather_scatter_kernels.cu:129-150) and attention (one warp's partial max and sum broadcast as
-the block's, attention_kernels.cu:117-139) are not deterministic oracles and are only timed
-(oracle/time_reference_cuda.py)."""
+the block's, attention_kernels.cu:117-139) are not deterministic oracles and are only timed (the `reference_cuda` record of
+`bench.py --impl reference`)."""
 import numpy as np
 import pytest
 
