@@ -536,6 +536,14 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
         if (wtxt != nullptr) wtxt += 8 * sub;
         const bool bulk_lane = gw == 0 && lane == 0;
         const int gtid = gw * 32 + lane;
+        // this lane's four rotary pairs (the same in every row): frequency and axis
+        float om[4];
+        int axv[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            om[t] = a.rope.omega[4 * sub + t];
+            axv[t] = a.rope.axis[4 * sub + t];
+        }
         for (int32_t k = grp; k < rows_here; k += kBulkGroups) {
             const uint32_t st = (uint32_t)k % S, use = (uint32_t)k / S;
             if (!__all_sync(0xffffffffu, mbar_wait_suspend(full(st), use & 1, abort))) break;
@@ -577,13 +585,11 @@ gather_bulk_kernel(const __grid_constant__ GatherArgs a, const BulkLayout lay) {
                 float cs[4], sn[4];
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
-                    const int j = 4 * sub + t;
-                    const int ax = a.rope.axis[j];
-                    if (ax < 0) {
+                    if (axv[t] < 0) {
                         cs[t] = 1.f;
                         sn[t] = 0.f;
                     } else {
-                        rope_sincos((float)inf[2 + ax] * a.rope.omega[j], &sn[t], &cs[t]);
+                        rope_sincos((float)inf[2 + axv[t]] * om[t], &sn[t], &cs[t]);
                     }
                 }
                 // kUnitBatch independent head vectors per half-warp at a time (their loads,
